@@ -1,0 +1,19 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself.
+
+The fixtures (tests/golden/*.pt) were written by tests/golden/make_golden.py,
+which runs fisalt/GPA's own ``gpa.DenseGPA`` (torch backend).  The oracle must
+reproduce every stored field: outputs, input and parameter gradients, final
+cache tensors, cached-call partitions and one-token decode steps.
+"""
+import pytest
+
+from cases import CASES
+from check_oracle import TOLERANCE, oracle_errors
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_oracle_matches_reference_golden(name, cpu_threads):
+    errors = oracle_errors(name)
+    tol = TOLERANCE[CASES[name]["dtype"]]
+    bad = {k: v for k, v in errors.items() if not v <= tol}
+    assert not bad, bad
