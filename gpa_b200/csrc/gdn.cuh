@@ -1,0 +1,84 @@
+// Chunked gated-delta-rule (GDN) scans over lag blocks: forward and backward.
+//
+// Recurrence (key-major, src/gpa/ops.py:29-46, docs/EQUATIONS.md:7-28):
+//   S_t = a_t S_{t-1} + b_t k_t (v_t - a_t k_t^T S_{t-1})^T,   y_t = q_t^T S_t,
+// with unit-normalised q, k supplied by the caller and a_t = exp(g_t).
+//
+// Chunk form (the WY / UT representation of Yang et al. 2024, "Parallelizing
+// Linear Transformers with the Delta Rule over Sequence Length"), per block of
+// c <= 64 tokens with G = inclusive cumsum of g inside the block:
+//   A_ts = b_t exp(G_t - G_s) k_t.k_s  (s < t),   (I + A) [U | Wk] = [b V | b e^G K]
+//   W = U - Wk S_0,   O = e^G (Q S_0) + ((Q K^T) o Gamma) W,
+//   S_c = e^{G_c} S_0 + K^T diag(e^{G_c - G}) W.
+// The triangular system is solved by column-parallel forward substitution
+// (one thread per right-hand-side column), so T = (I + A)^-1 is never formed;
+// the backward uses back substitution with (I + A)^T the same way.
+//
+// Kernels (SIMT fp32 in this file; every launch covers a batch of scans that
+// may have different K, V):
+//   gdn_fwd_chunk   chunk-parallel:  A, U, Wk                        (also backward recompute)
+//   gdn_fwd_state   sequential over blocks, V-sliced: boundary states, W
+//   gdn_fwd_out     chunk-parallel, V-sliced: O
+//   gdn_bwd_local   chunk-parallel, V-sliced: dQ, dK (read part), dW_local, dG (read part)
+//   gdn_bwd_state   sequential reverse over blocks, V-sliced: D (dS) at block ends, dW
+//   gdn_bwd_chunk_v chunk-parallel, V-sliced: state-update + U-path terms
+//   gdn_bwd_chunk_k chunk-parallel: Wk-path terms, dA consequences, dg = revcumsum(dG)
+#pragma once
+#include "common.cuh"
+
+namespace gpa {
+
+constexpr int kMaxScans = 8;
+constexpr int kVSlice = 64;
+constexpr int kAStride = 65;  // padded row stride of c x c tiles in shared memory
+
+struct ScanDesc {
+  int K, V;
+  const float* q;     // [U,T,K] unit-normalised queries (null: no output)
+  const float* k;     // [U,T,K] unit-normalised keys
+  const float* v;     // [U,T,V]
+  const float* g;     // log decay, element (u,t) at g[u*g_su + t*g_st]
+  const float* beta;  // same indexing as g
+  int64_t g_su, g_st;
+  const float* S0;    // [U,K,V] initial state
+  float* Sb;          // [U,NB+1,K,V] block-boundary states
+  float* W;           // [U,T,V] pseudo-values
+  float* Ub;          // [U,T,V] T diag(b) V (may alias W in the forward)
+  float* Wk;          // [U,T,K] T diag(b e^G) K
+  float* O;           // [U,T,V] output (null: none)
+  float* S_final;     // [U,K,V] copy of the final state (null: none)
+  // ---- backward ----
+  const float* dO;        // [U,T,V] output gradient (null: zero)
+  const float* dO_scale;  // per-unit scale of dO (null: 1)
+  const float* ext;       // [U,NB+1,K,V] external gradients of boundary states (null: zero)
+  const float* dS_final;  // [U,K,V] gradient of the final state (null: zero)
+  float* dq;              // [U,T,K] += (null: skip)
+  float* dk;              // [U,T,K] +=
+  float* dv;              // [U,T,V] +=
+  float* dg;              // += at dg[u*dg_su + t*dg_st]
+  float* dbeta;           // += with dg's indexing
+  int64_t dg_su, dg_st;
+  float* dS0;             // [U,K,V] gradient of the initial state (written)
+  float* sc_dW;           // [U,T,V] scratch
+  float* sc_dK;           // [U,T,K] scratch (zeroed by the caller)
+  float* sc_dWk;          // [U,T,K] scratch (zeroed)
+  float* sc_dG;           // [U,T]   scratch (zeroed)
+  float* sc_db;           // [U,T]   scratch (zeroed)
+  float* sc_dA;           // [U,NB,64,64] scratch (zeroed)
+  float* Dend;            // [U,NB,K,V] dS at each block end
+};
+
+struct ScanBatch {
+  int n;
+  ScanDesc s[kMaxScans];
+};
+
+// Host launchers (gdn.cu).  All are stream-ordered and allocate nothing.
+cudaError_t gdn_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
+                        cudaStream_t st);
+cudaError_t gdn_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+cudaError_t gdn_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+cudaError_t gdn_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+int gdn_max_smem_bytes();
+
+}  // namespace gpa

@@ -1,0 +1,1248 @@
+// Level, relation-reader and output kernels of the DenseGPA core (SIMT fp32).
+//
+// Reference formulas (src/gpa/attention.py): gates :161-174, slot :176-184,
+// residual :190-194, base logits :196-204, relation gates :206-223, dense
+// reader (bridge) :225-262, lag-block writes :314-316, output mix :340-341.
+#include "level.cuh"
+
+namespace gpa {
+namespace {
+
+constexpr int kRowsPerTile = 64;
+constexpr int kMaxPerLane = 8;  // vectors up to 256 long per warp row
+
+GPA_DEV int64_t row(int u, int T, int t) { return (int64_t)u * T + t; }
+
+// softmax over the lane-strided vector x[0..n) held in registers
+GPA_DEV void warp_softmax(float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) mx = fmaxf(mx, x[i]);
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) {
+      x[i] = __expf(x[i] - mx);
+      s += x[i];
+    }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) x[i] *= inv;
+}
+
+GPA_DEV float warp_norm(const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) s += x[i] * x[i];
+  return sqrtf(warp_sum(s));
+}
+
+GPA_DEV float warp_dot(const float (&x)[kMaxPerLane], const float (&y)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) s += x[i] * y[i];
+  return warp_sum(s);
+}
+
+GPA_DEV void load_vec(float (&x)[kMaxPerLane], const float* p, int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) x[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
+}
+
+GPA_DEV void store_vec(float* p, const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) p[lane + 32 * i] = x[i];
+}
+
+// unit-normalisation backward: y = x / max(|x|, eps)
+GPA_DEV void unit_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
+                      const float (&dy)[kMaxPerLane], float nrm, int n) {
+  if (nrm > kUnitEps) {
+    const float yd = warp_dot(y, dy, n);
+    const float inv = 1.f / nrm;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = (dy[i] - y[i] * yd) * inv;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = dy[i] / kUnitEps;
+  }
+}
+
+GPA_DEV void softmax_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
+                         const float (&dy)[kMaxPerLane], int n) {
+  const float yd = warp_dot(y, dy, n);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) dx[i] = y[i] * (dy[i] - yd);
+}
+
+GPA_DEV float block_sum(float x, float* red) {
+  x = warp_sum(x);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+  }
+  return s;  // valid in warp 0
+}
+
+// ------------------------------------------------------------------ forward
+
+// one warp per (u, t): fp32 copies, unit-normalised q
+__global__ void k_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
+                        int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int U = B * H;
+  if (w >= U * T) return;
+  const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
+  const int64_t src = ((int64_t)b * T + t) * H + h;
+  float ss = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float x = load_in(q, src * D + d, dt);
+    qf[(int64_t)w * D + d] = x;
+    ss += x * x;
+    key0[(int64_t)w * D + d] = load_in(k, src * D + d, dt);
+  }
+  const float nrm = sqrtf(warp_sum(ss));
+  const float inv = 1.f / fmaxf(nrm, kUnitEps);
+  for (int d = lane; d < D; d += 32) qh[(int64_t)w * D + d] = qf[(int64_t)w * D + d] * inv;
+  if (lane == 0) qn[w] = nrm;
+  for (int d = lane; d < Dv; d += 32) val0[(int64_t)w * Dv + d] = load_in(v, src * Dv + d, dt);
+}
+
+// CTA per (u, 64-token tile): u(k), slot = k C^T, u(slot), gates.
+__global__ void __launch_bounds__(256) k_level_prep(int U, int T, int H, int D, int M,
+                                                    const float* key, const float* C,
+                                                    const float* Wg, const float* gbias,
+                                                    float beta_max, int pos_none, float* nk,
+                                                    float* kn, float* slot, float* ns, float* sn,
+                                                    float* raw4, float* gates) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * kRowsPerTile;
+  const int c = min(kRowsPerTile, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* Kt = sm;                       // 64*D
+  float* St = Kt + kRowsPerTile * D;    // 64*M
+  load_tile(Kt, key + row(u, T, t0) * D, c, D, D);
+  __syncthreads();
+  const float* wg = Wg + (int64_t)h * D * 4;
+  for (int t = warp; t < c; t += nw) {
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) ss += Kt[t * D + d] * Kt[t * D + d];
+    const float nrm = sqrtf(warp_sum(ss));
+    const float inv = 1.f / fmaxf(nrm, kUnitEps);
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int d = lane; d < D; d += 32) {
+      const float x = Kt[t * D + d] * inv;
+      nk[row(u, T, t0 + t) * D + d] = x;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) r[cc] += x * wg[d * 4 + cc];
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) r[cc] = warp_sum(r[cc]) + gbias[h * 4 + cc];
+    if (lane == 0) {
+      const int64_t o = row(u, T, t0 + t);
+      kn[o] = nrm;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) raw4[o * 4 + cc] = r[cc];
+      const float gi = pos_none ? 0.f : -fminf(softplus(r[0]), 10.f);
+      const float go = pos_none ? 0.f : -fminf(softplus(r[2]), 10.f);
+      gates[o * 4 + 0] = gi;
+      gates[o * 4 + 1] = beta_max * sigmoid(r[1]);
+      gates[o * 4 + 2] = go;
+      gates[o * 4 + 3] = beta_max * sigmoid(r[3]);
+    }
+  }
+  const float* Ch = C + (int64_t)h * M * D;
+  block_gemm<2, 4>(
+      c, M, D, [&](int t, int d) { return Kt[t * D + d]; },
+      [&](int d, int m) { return Ch[m * D + d]; },
+      [&](int t, int m, float acc) {
+        St[t * M + m] = acc;
+        slot[row(u, T, t0 + t) * M + m] = acc;
+      });
+  __syncthreads();
+  for (int t = warp; t < c; t += nw) {
+    float ss = 0.f;
+    for (int m = lane; m < M; m += 32) ss += St[t * M + m] * St[t * M + m];
+    const float nrm = sqrtf(warp_sum(ss));
+    const float inv = 1.f / fmaxf(nrm, kUnitEps);
+    for (int m = lane; m < M; m += 32) ns[row(u, T, t0 + t) * M + m] = St[t * M + m] * inv;
+    if (lane == 0) sn[row(u, T, t0 + t)] = nrm;
+  }
+}
+
+GPA_DEV const float* frozen_ptr(const float* bnd, const float* fz, int u, int n, int nb, int post,
+                                int64_t sz) {
+  if (n == 0 && fz) return fz + (int64_t)u * sz;
+  return bnd + ((int64_t)u * (nb + 1) + n + post) * sz;
+}
+
+// CTA per (u, lag block): writes from the frozen snapshots, residual key/value.
+__global__ void __launch_bounds__(256) k_level_post(
+    int U, Blocks bl, int post, int H, int D, int Dv, int M, int with_residual, const float* nk,
+    const float* key, const float* val, const float* Abnd, const float* Bbnd, const float* fzA,
+    const float* fzB, const float* residual_raw, int j, float* write, float* bsum,
+    float* key_next, float* val_next) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* As = sm;               // D*M
+  float* Bs = As + D * M;       // M*Dv
+  float* Wr = Bs + M * Dv;      // 64*M
+  const float* Af = frozen_ptr(Abnd, fzA, u, n, bl.nb, post, (int64_t)D * M);
+  const float* Bf = frozen_ptr(Bbnd, fzB, u, n, bl.nb, post, (int64_t)M * Dv);
+  load_tile(As, Af, D, M, M);
+  if (with_residual) load_tile(Bs, Bf, M, Dv, Dv);
+  __syncthreads();
+  const float* nkb = nk + row(u, T, t0) * D;
+  block_gemm<2, 4>(
+      c, M, D, [&](int t, int d) { return nkb[t * D + d]; },
+      [&](int d, int m) { return As[d * M + m]; },
+      [&](int t, int m, float acc) { Wr[t * M + m] = acc; });
+  __syncthreads();
+  for (int t = warp; t < c; t += nw) {
+    float x[kMaxPerLane];
+    load_vec(x, Wr + t * M, M);
+    warp_softmax(x, M);
+    store_vec(Wr + t * M, x, M);
+    store_vec(write + row(u, T, t0 + t) * M, x, M);
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float s = 0.f;
+    for (int t = 0; t < c; ++t) s += Wr[t * M + m];
+    bsum[((int64_t)u * bl.nb + n) * M + m] = s;
+  }
+  if (!with_residual) return;
+  const float ek = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 0]);
+  const float ev = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 1]);
+  block_gemm<2, 4>(
+      c, D, M, [&](int t, int m) { return Wr[t * M + m]; },
+      [&](int m, int d) { return As[d * M + m]; },
+      [&](int t, int d, float acc) {
+        const int64_t o = row(u, T, t0 + t) * D + d;
+        key_next[o] = key[o] - ek * acc;
+      });
+  block_gemm<2, 4>(
+      c, Dv, M, [&](int t, int m) { return Wr[t * M + m]; },
+      [&](int m, int v) { return Bs[m * Dv + v]; },
+      [&](int t, int v, float acc) {
+        const int64_t o = row(u, T, t0 + t) * Dv + v;
+        val_next[o] = val[o] - ev * acc;
+      });
+}
+
+// CTA per (u, lag block): counts = n0 + cumsum(write); logits; u(local); u(write).
+__global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, float read_scale,
+                                                const float* count_gain_raw, int j,
+                                                const float* n0, const float* bsum,
+                                                const float* write, const float* raw,
+                                                float* counts, float* logits, float* lh,
+                                                float* ln, float* wh, float* wn, float* n_final) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float acc = n0[(int64_t)u * M + m];
+    for (int p = 0; p < n; ++p) acc += bsum[((int64_t)u * bl.nb + p) * M + m];
+    for (int t = 0; t < c; ++t) {
+      acc += write[row(u, T, t0 + t) * M + m];
+      counts[row(u, T, t0 + t) * M + m] = acc;
+    }
+    if (n == bl.nb - 1) n_final[(int64_t)u * M + m] = acc;
+  }
+  __syncthreads();
+  const float gain = softplus(count_gain_raw[j * H + h]);
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float x[kMaxPerLane], w[kMaxPerLane], cn[kMaxPerLane];
+    load_vec(x, raw + o * M, M);
+    load_vec(cn, counts + o * M, M);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) x[i] = read_scale * x[i] + gain * log1pf(cn[i]);
+    store_vec(logits + o * M, x, M);
+    warp_softmax(x, M);
+    const float a = warp_norm(x, M);
+    const float ia = 1.f / fmaxf(a, kUnitEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
+    store_vec(lh + o * M, x, M);
+    load_vec(w, write + o * M, M);
+    const float b = warp_norm(w, M);
+    const float ib = 1.f / fmaxf(b, kUnitEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) w[i] *= ib;
+    store_vec(wh + o * M, w, M);
+    if ((threadIdx.x & 31) == 0) {
+      ln[o] = a;
+      wn[o] = b;
+    }
+  }
+}
+
+__global__ void k_rel_gates(int U, int H, int E, int pos_none, const float* decay_raw,
+                            const float* beta_raw, float* ge, float* be) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= E * U) return;
+  const int e = i / U, u = i - e * U, h = u % H;
+  ge[i] = pos_none ? 0.f : -softplus(decay_raw[e * H + h]);
+  be[i] = sigmoid(beta_raw[e * H + h]);
+}
+
+// softmax over the incoming edges' logits for head h
+GPA_DEV void edge_weights(const BridgeIn& in, const float* edge_logits, int H, int h,
+                          float* w) {
+  float mx = -INFINITY;
+  for (int a = 0; a < in.n; ++a) mx = fmaxf(mx, edge_logits[in.edge[a] * H + h]);
+  float s = 0.f;
+  for (int a = 0; a < in.n; ++a) {
+    w[a] = __expf(edge_logits[in.edge[a] * H + h] - mx);
+    s += w[a];
+  }
+  for (int a = 0; a < in.n; ++a) w[a] /= s;
+}
+
+// CTA per (u, 64-token tile), target level j: dense reader, route MLP, query projection.
+__global__ void __launch_bounds__(256) k_bridge(
+    int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
+    const float* relation_gain, const float* route_up, const float* route_down,
+    const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
+    const float* logits, const float* qf, float* r_out, float* hp_out, float* mlp_out,
+    float* route_out, float* qoh, float* qon) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * kRowsPerTile;
+  const int c = min(kRowsPerTile, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* Rt = sm;                          // 64*M
+  float* Hd = Rt + kRowsPerTile * M;       // 64*2M
+  float* Mt = Hd + kRowsPerTile * 2 * M;   // 64*M
+  float w[kMaxIn];
+  edge_weights(in, edge_logits, H, h, w);
+  const float rg = relation_gain[j * H + h];
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float base[kMaxPerLane];
+    load_vec(base, logits + o * M, M);
+    if (in.n > 0) {
+      float inc[kMaxPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
+      }
+      const int lane = threadIdx.x & 31;
+      float mean = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i)
+        if (lane + 32 * i < M) mean += inc[i];
+      mean = warp_sum(mean) / M;
+      float var = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i)
+        if (lane + 32 * i < M) {
+          inc[i] -= mean;
+          var += inc[i] * inc[i];
+        }
+      var = warp_sum(var) / M;
+      const float sd = rsqrtf(var + kCenterEps);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) base[i] += rg * tanhf(inc[i] * sd);
+    }
+    warp_softmax(base, M);
+    store_vec(Rt + t * M, base, M);
+    store_vec(r_out + o * M, base, M);
+  }
+  __syncthreads();
+  const float* Uh = route_up + (int64_t)h * M * 2 * M;
+  const float* Dh = route_down + (int64_t)h * 2 * M * M;
+  block_gemm<2, 4>(
+      c, 2 * M, M, [&](int t, int m) { return Rt[t * M + m]; },
+      [&](int m, int r) { return Uh[m * 2 * M + r]; },
+      [&](int t, int r, float acc) {
+        hp_out[row(u, T, t0 + t) * 2 * M + r] = acc;
+        Hd[t * 2 * M + r] = gelu(acc);
+      });
+  __syncthreads();
+  const float mg = route_mlp_gain[j * H + h];
+  block_gemm<2, 4>(
+      c, M, 2 * M, [&](int t, int r) { return Hd[t * 2 * M + r]; },
+      [&](int r, int m) { return Dh[r * M + m]; },
+      [&](int t, int m, float acc) {
+        mlp_out[row(u, T, t0 + t) * M + m] = acc;
+        Mt[t * M + m] = acc;
+      });
+  __syncthreads();
+  for (int i = threadIdx.x; i < c * M; i += blockDim.x) {
+    const int t = i / M, m = i - t * M;
+    const float x = Rt[i] + mg * Mt[i];
+    Rt[i] = x;
+    route_out[row(u, T, t0 + t) * M + m] = x;
+  }
+  __syncthreads();
+  const float* Wr = Wrs + (int64_t)h * M * M;
+  const float* Wq = Wqs + (int64_t)h * D * M;
+  const float* qb = qf + row(u, T, t0) * D;
+  block_gemm<2, 4>(
+      c, M, M + D,
+      [&](int t, int kk) { return kk < M ? Rt[t * M + kk] : qs * qb[t * D + (kk - M)]; },
+      [&](int kk, int nn) { return kk < M ? Wr[kk * M + nn] : Wq[(kk - M) * M + nn]; },
+      [&](int t, int nn, float acc) { Mt[t * M + nn] = acc; });
+  __syncthreads();
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float x[kMaxPerLane];
+    load_vec(x, Mt + t * M, M);
+    const float a = warp_norm(x, M);
+    const float ia = 1.f / fmaxf(a, kUnitEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
+    store_vec(qoh + o * M, x, M);
+    if ((threadIdx.x & 31) == 0) qon[o] = a;
+  }
+}
+
+struct YPtrs {
+  const float* y[kMaxLevels];
+};
+
+// one warp per (u, t): out = sum_j softmax_L(output_logits)_j y_j
+__global__ void k_mix(int B, int T, int H, int Dv, int L, const float* output_logits, YPtrs yp,
+                      void* out, int dt) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int U = B * H;
+  if (w >= U * T) return;
+  const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
+  float ow[kMaxLevels];
+  float mx = -INFINITY, s = 0.f;
+  for (int j = 0; j < L; ++j) mx = fmaxf(mx, output_logits[j * H + h]);
+  for (int j = 0; j < L; ++j) {
+    ow[j] = __expf(output_logits[j * H + h] - mx);
+    s += ow[j];
+  }
+  const int64_t dst = (((int64_t)b * T + t) * H + h) * Dv;
+  for (int v = lane; v < Dv; v += 32) {
+    float acc = 0.f;
+    for (int j = 0; j < L; ++j) acc += (ow[j] / s) * yp.y[j][(int64_t)w * Dv + v];
+    store_out(out, dst + v, acc, dt);
+  }
+}
+
+__global__ void k_copy(float* dst, const float* src, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src[i];
+}
+
+__global__ void k_to_bthx(const float* src, void* dst, int dt, int B, int T, int H, int X) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * T * H * X) return;
+  const int64_t x = i % X, r = i / X;  // r = (b*T + t)*H + h
+  const int64_t h = r % H, bt = r / H, t = bt % T, b = bt / T;
+  store_out(dst, i, src[(((b * H + h) * T) + t) * X + x], dt);
+}
+
+__global__ void k_add(float* dst, const float* src, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] += src[i];
+}
+
+__global__ void k_boundary(float* dst, const float* src, int U, int nb1, int idx, int64_t sz,
+                           int scatter_add) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)U * sz) return;
+  const int64_t u = i / sz, r = i - u * sz;
+  const int64_t b = (u * nb1 + idx) * sz + r;
+  if (scatter_add) dst[b] += src[i];
+  else dst[i] = src[b];
+}
+
+// ----------------------------------------------------------------- backward
+
+__global__ void k_scales(int U, int H, int L, const float* output_logits, float* ow_scale) {
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= U) return;
+  const int h = u % H;
+  float mx = -INFINITY, s = 0.f;
+  for (int j = 0; j < L; ++j) mx = fmaxf(mx, output_logits[j * H + h]);
+  for (int j = 0; j < L; ++j) s += __expf(output_logits[j * H + h] - mx);
+  for (int j = 0; j < L; ++j) ow_scale[j * U + u] = __expf(output_logits[j * H + h] - mx) / s;
+}
+
+// one warp per (u, t): fp32 unit-major dout; per-unit sum of dout . y_j
+__global__ void k_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt, YPtrs yp,
+                          float* dout_f, float* scal) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int U = B * H;
+  if (w >= U * T) return;
+  const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
+  const int64_t src = (((int64_t)b * T + t) * H + h) * Dv;
+  float acc[kMaxLevels];
+  for (int j = 0; j < L; ++j) acc[j] = 0.f;
+  for (int v = lane; v < Dv; v += 32) {
+    const float g = load_in(dout, src + v, dt);
+    dout_f[(int64_t)w * Dv + v] = g;
+    for (int j = 0; j < L; ++j) acc[j] += g * yp.y[j][(int64_t)w * Dv + v];
+  }
+  for (int j = 0; j < L; ++j) {
+    const float s = warp_sum(acc[j]);
+    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_OutW], s);
+  }
+}
+
+// CTA per (u, 64-token tile), level j: backward of the reader / route MLP / projections.
+__global__ void __launch_bounds__(256) k_bridge_bwd(
+    int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
+    const float* relation_gain, const float* route_up, const float* route_down,
+    const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
+    const float* logits, const float* r_in, const float* hp, const float* mlp, const float* qoh,
+    const float* qon, const float* dqoh, float* dqo_out, float* droute_out, float* dhp_out,
+    float* dlogits, float* dq_direct, float* scal, float* scalE, int E) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * kRowsPerTile;
+  const int c = min(kRowsPerTile, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ float sm[];
+  float* Q = sm;                          // 64*M   dqo
+  float* R = Q + kRowsPerTile * M;        // 64*M   droute -> dr
+  float* Hd = R + kRowsPerTile * M;       // 64*2M  dhp
+  float* red = Hd + kRowsPerTile * 2 * M; // 32
+  float* ew = red + 32;                   // kMaxIn accumulators
+  if (threadIdx.x < kMaxIn) ew[threadIdx.x] = 0.f;
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+    load_vec(y, qoh + o * M, M);
+    load_vec(dy, dqoh + o * M, M);
+    unit_bwd(dx, y, dy, qon[o], M);
+    store_vec(Q + t * M, dx, M);
+    store_vec(dqo_out + o * M, dx, M);
+  }
+  __syncthreads();
+  const float* Wr = Wrs + (int64_t)h * M * M;
+  const float* Wq = Wqs + (int64_t)h * D * M;
+  block_gemm<2, 4>(
+      c, M, M, [&](int t, int nn) { return Q[t * M + nn]; },
+      [&](int nn, int m) { return Wr[m * M + nn]; },
+      [&](int t, int m, float acc) {
+        R[t * M + m] = acc;
+        droute_out[row(u, T, t0 + t) * M + m] = acc;
+      });
+  block_gemm<2, 4>(
+      c, D, M, [&](int t, int nn) { return Q[t * M + nn]; },
+      [&](int nn, int d) { return Wq[d * M + nn]; },
+      [&](int t, int d, float acc) { dq_direct[row(u, T, t0 + t) * D + d] += qs * acc; });
+  __syncthreads();
+  {
+    float part = 0.f;
+    for (int i = threadIdx.x; i < c * M; i += blockDim.x) {
+      const int t = i / M, m = i - t * M;
+      part += R[i] * mlp[row(u, T, t0 + t) * M + m];
+    }
+    const float s = block_sum(part, red);
+    if (threadIdx.x == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_MlpGain], s);
+  }
+  const float mg = route_mlp_gain[j * H + h];
+  const float* Uh = route_up + (int64_t)h * M * 2 * M;
+  const float* Dh = route_down + (int64_t)h * 2 * M * M;
+  block_gemm<2, 4>(
+      c, 2 * M, M, [&](int t, int m) { return R[t * M + m]; },
+      [&](int m, int rr) { return Dh[rr * M + m]; },
+      [&](int t, int rr, float acc) {
+        const float x = mg * acc * gelu_grad(hp[row(u, T, t0 + t) * 2 * M + rr]);
+        Hd[t * 2 * M + rr] = x;
+        dhp_out[row(u, T, t0 + t) * 2 * M + rr] = x;
+      });
+  __syncthreads();
+  block_gemm<2, 4>(
+      c, M, 2 * M, [&](int t, int rr) { return Hd[t * 2 * M + rr]; },
+      [&](int rr, int m) { return Uh[m * 2 * M + rr]; },
+      [&](int t, int m, float acc) { R[t * M + m] += acc; });
+  __syncthreads();
+  float w[kMaxIn];
+  edge_weights(in, edge_logits, H, h, w);
+  const float rg = relation_gain[j * H + h];
+  float rg_acc = 0.f, ew_acc[kMaxIn];
+  for (int a = 0; a < kMaxIn; ++a) ew_acc[a] = 0.f;
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float r[kMaxPerLane], dr[kMaxPerLane], db[kMaxPerLane];
+    load_vec(r, r_in + o * M, M);
+    load_vec(dr, R + t * M, M);
+    softmax_bwd(db, r, dr, M);
+    store_vec(dlogits + o * M, db, M);
+    if (in.n > 0) {
+      float inc[kMaxPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
+      }
+      float mean = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i)
+        if (lane + 32 * i < M) mean += inc[i];
+      mean = warp_sum(mean) / M;
+      float var = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i)
+        if (lane + 32 * i < M) {
+          inc[i] -= mean;  // centred
+          var += inc[i] * inc[i];
+        }
+      var = warp_sum(var) / M;
+      const float sd = rsqrtf(var + kCenterEps);
+      float dz[kMaxPerLane], tz[kMaxPerLane];
+      float rgp = 0.f, dsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        tz[i] = tanhf(inc[i] * sd);
+        if (lane + 32 * i < M) rgp += db[i] * tz[i];
+        dz[i] = rg * db[i] * (1.f - tz[i] * tz[i]);
+        if (lane + 32 * i < M) dsum += dz[i] * inc[i];
+      }
+      rg_acc += warp_sum(rgp);
+      dsum = warp_sum(dsum);
+      const float dvar = dsum * -0.5f * sd * sd * sd;
+      float dmean = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        dz[i] = dz[i] * sd + dvar * 2.f * inc[i] / M;  // dcc
+        if (lane + 32 * i < M) dmean += dz[i];
+      }
+      dmean = warp_sum(dmean) / M;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) dz[i] -= dmean;  // dinc
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane], dm[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) dm[i] = w[a] * dz[i];
+        store_vec(in.dmsg[a] + o * M, dm, M);
+        ew_acc[a] += warp_dot(dz, x, M);
+      }
+    }
+  }
+  if (lane == 0 && in.n > 0) {
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], rg_acc);
+    for (int a = 0; a < in.n; ++a)
+      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], ew_acc[a]);
+  }
+}
+
+// one warp per (u, t), level j: logits / local-softmax / count-log backward.
+__global__ void k_logits_bwd(int U, Blocks bl, int H, int M, int L, int j, float read_scale,
+                             const float* count_gain_raw, const float* logits,
+                             const float* counts, const float* lh, const float* ln,
+                             const float* wh, const float* wn, const float* dlh, const float* dwh,
+                             const float* dlogits, float* dwrite, float* draw, float* dn,
+                             float* dnsum, float* scal) {
+  const int T = bl.T;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= U * T) return;
+  const int u = w / T, t = w - u * T, h = u % H;
+  const int64_t o = (int64_t)w * M;
+  const float cgr = count_gain_raw[j * H + h];
+  const float gain = softplus(cgr);
+  float x[kMaxPerLane], y[kMaxPerLane], dy[kMaxPerLane], d1[kMaxPerLane], d2[kMaxPerLane];
+  load_vec(x, logits + o, M);
+  warp_softmax(x, M);  // local
+  load_vec(y, lh + o, M);
+  load_vec(dy, dlh + o, M);
+  unit_bwd(d1, y, dy, ln[w], M);  // dlocal
+  softmax_bwd(d2, x, d1, M);
+  load_vec(d1, dlogits + o, M);
+  float cn[kMaxPerLane];
+  load_vec(cn, counts + o, M);
+  float cg = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const float dl = d1[i] + d2[i];
+    d1[i] = read_scale * dl;
+    if (lane + 32 * i < M) cg += dl * log1pf(cn[i]);
+    d2[i] = gain * dl / (1.f + cn[i]);
+  }
+  store_vec(draw + o, d1, M);
+  store_vec(dn + o, d2, M);
+  const int n = bl.block_of(t);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < M) atomicAdd(&dnsum[((int64_t)u * bl.nb + n) * M + lane + 32 * i], d2[i]);
+  cg = warp_sum(cg);
+  if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], cg);
+  load_vec(y, wh + o, M);
+  load_vec(dy, dwh + o, M);
+  unit_bwd(d1, y, dy, wn[w], M);
+  load_vec(d2, dwrite + o, M);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) d2[i] += d1[i];
+  store_vec(dwrite + o, d2, M);
+}
+
+// CTA per (u, lag block): dwrite += suffix sums of dn; dn0.
+__global__ void k_counts_bwd(int U, Blocks bl, int M, const float* dn, const float* dnsum,
+                             const float* dn_final, float* dwrite, float* dn0) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float acc = dn_final ? dn_final[(int64_t)u * M + m] : 0.f;
+    for (int p = n + 1; p < bl.nb; ++p) acc += dnsum[((int64_t)u * bl.nb + p) * M + m];
+    for (int t = c - 1; t >= 0; --t) {
+      const int64_t o = row(u, T, t0 + t) * M + m;
+      acc += dn[o];
+      dwrite[o] += acc;
+    }
+    if (n == 0) dn0[(int64_t)u * M + m] = acc;
+  }
+}
+
+// CTA per (u, lag block), level j: residual + write backward; frozen-snapshot gradients.
+__global__ void __launch_bounds__(256) k_post_bwd(
+    int U, Blocks bl, int post, int offset, int H, int D, int Dv, int M, int L, int j,
+    int with_residual, const float* nk, const float* write, const float* Abnd, const float* Bbnd,
+    const float* fzA, const float* fzB, const float* residual_raw, const float* dkey,
+    const float* dval, float* dwrite, float* dnk, float* extA, float* extB, float* dfzA,
+    float* dfzB, float* scal) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* As = sm;              // D*M
+  float* Bs = As + D * M;      // M*Dv
+  float* Wr = Bs + M * Dv;     // 64*M
+  float* dW = Wr + kRowsPerTile * M;  // 64*M
+  float* red = dW + kRowsPerTile * M; // 32 + 2
+  const bool fz0 = (n == 0 && offset != 0);
+  const float* Af = frozen_ptr(Abnd, fz0 ? fzA : nullptr, u, n, bl.nb, post, (int64_t)D * M);
+  const float* Bf = frozen_ptr(Bbnd, fz0 ? fzB : nullptr, u, n, bl.nb, post, (int64_t)M * Dv);
+  load_tile(As, Af, D, M, M);
+  if (with_residual) load_tile(Bs, Bf, M, Dv, Dv);
+  load_tile(Wr, write + row(u, T, t0) * M, c, M, M);
+  load_tile(dW, dwrite + row(u, T, t0) * M, c, M, M);
+  if (threadIdx.x < 34) red[threadIdx.x] = 0.f;
+  __syncthreads();
+  const float ek = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 0]);
+  const float ev = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 1]);
+  const float* dk = dkey + row(u, T, t0) * D;
+  const float* dv = dval + row(u, T, t0) * Dv;
+  if (with_residual) {
+    // d eta_k = -sum dk . (A_f write), d eta_v = -sum dv . (write B_f)
+    float pk = 0.f, pv = 0.f;
+    block_gemm<2, 4>(
+        c, D, M, [&](int t, int m) { return Wr[t * M + m]; },
+        [&](int m, int d) { return As[d * M + m]; },
+        [&](int t, int d, float acc) { pk += acc * dk[t * D + d]; });
+    block_gemm<2, 4>(
+        c, Dv, M, [&](int t, int m) { return Wr[t * M + m]; },
+        [&](int m, int v) { return Bs[m * Dv + v]; },
+        [&](int t, int v, float acc) { pv += acc * dv[t * Dv + v]; });
+    pk = warp_sum(pk);
+    pv = warp_sum(pv);
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(&red[32], pk);
+      atomicAdd(&red[33], pv);
+    }
+    // dW += -ek dk A_f - ev dv B_f^T
+    block_gemm<2, 4>(
+        c, M, D + Dv,
+        [&](int t, int kk) { return kk < D ? -ek * dk[t * D + kk] : -ev * dv[t * Dv + (kk - D)]; },
+        [&](int kk, int m) { return kk < D ? As[kk * M + m] : Bs[m * Dv + (kk - D)]; },
+        [&](int t, int m, float acc) { dW[t * M + m] += acc; });
+  }
+  __syncthreads();
+  if (with_residual && threadIdx.x == 0) {
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaK], -red[32]);
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaV], -red[33]);
+  }
+  // dlw = softmax backward (in place in dW)
+  for (int t = warp; t < c; t += nw) {
+    float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+    load_vec(y, Wr + t * M, M);
+    load_vec(dy, dW + t * M, M);
+    softmax_bwd(dx, y, dy, M);
+    store_vec(dW + t * M, dx, M);
+  }
+  __syncthreads();
+  const float* nkb = nk + row(u, T, t0) * D;
+  // dnk = dlw A_f^T
+  block_gemm<2, 4>(
+      c, D, M, [&](int t, int m) { return dW[t * M + m]; },
+      [&](int m, int d) { return As[d * M + m]; },
+      [&](int t, int d, float acc) { dnk[row(u, T, t0 + t) * D + d] = acc; });
+  // dA_f = -ek dk^T write + nk^T dlw ;  dB_f = -ev write^T dv
+  float* ta = fz0 ? dfzA + (int64_t)u * D * M
+                  : extA + ((int64_t)u * (bl.nb + 1) + n + post) * D * M;
+  float* tb = fz0 ? dfzB + (int64_t)u * M * Dv
+                  : extB + ((int64_t)u * (bl.nb + 1) + n + post) * M * Dv;
+  block_gemm<2, 4>(
+      D, M, with_residual ? 2 * c : c,
+      [&](int d, int tt) { return tt < c ? nkb[tt * D + d] : -ek * dk[(tt - c) * D + d]; },
+      [&](int tt, int m) { return tt < c ? dW[tt * M + m] : Wr[(tt - c) * M + m]; },
+      [&](int d, int m, float acc) { ta[d * M + m] += acc; });
+  if (with_residual) {
+    block_gemm<2, 4>(
+        M, Dv, c, [&](int m, int t) { return Wr[t * M + m]; },
+        [&](int t, int v) { return -ev * dv[t * Dv + v]; },
+        [&](int m, int v, float acc) { tb[m * Dv + v] += acc; });
+  }
+}
+
+// CTA per (u, 64-token tile), level j: gates / slot / unit-norm backward into dkey.
+__global__ void __launch_bounds__(256) k_prep_bwd(int U, int T, int H, int D, int M,
+                                                  const float* C, const float* Wg, float beta_max,
+                                                  int pos_none, const float* raw4,
+                                                  const float* nk, const float* kn,
+                                                  const float* ns, const float* sn,
+                                                  const float* dgates, const float* dnk,
+                                                  const float* dns, float* dslot, float* d4out,
+                                                  float* dkey) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * kRowsPerTile;
+  const int c = min(kRowsPerTile, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ float sm[];
+  float* Ds = sm;  // 64*M  dslot (total)
+  const float* wg = Wg + (int64_t)h * D * 4;
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float d4[4];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) d4[cc] = 0.f;
+    const float* r4 = raw4 + o * 4;
+    const float* dg = dgates + o * 4;
+    if (!pos_none) {
+      if (softplus(r4[0]) <= 10.f) d4[0] = -dg[0] * sigmoid(r4[0]);
+      if (softplus(r4[2]) <= 10.f) d4[2] = -dg[2] * sigmoid(r4[2]);
+    }
+    {
+      const float s1 = sigmoid(r4[1]), s3 = sigmoid(r4[3]);
+      d4[1] = dg[1] * beta_max * s1 * (1.f - s1);
+      d4[3] = dg[3] * beta_max * s3 * (1.f - s3);
+    }
+    if (lane < 4) d4out[o * 4 + lane] = d4[lane];
+    // dslot = dslot_value + unit_bwd(ns, dns)
+    float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane], base[kMaxPerLane];
+    load_vec(y, ns + o * M, M);
+    load_vec(dy, dns + o * M, M);
+    unit_bwd(dx, y, dy, sn[o], M);
+    load_vec(base, dslot + o * M, M);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) base[i] += dx[i];
+    store_vec(Ds + t * M, base, M);
+    store_vec(dslot + o * M, base, M);
+    // dnk_total = dnk + d4 Wg^T ; dkey += unit_bwd(nk, dnk_total)
+    float a[kMaxPerLane], da[kMaxPerLane], dkx[kMaxPerLane];
+    load_vec(a, nk + o * D, D);
+    load_vec(da, dnk + o * D, D);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D)
+        da[i] += d4[0] * wg[d * 4] + d4[1] * wg[d * 4 + 1] + d4[2] * wg[d * 4 + 2] +
+                 d4[3] * wg[d * 4 + 3];
+    }
+    unit_bwd(dkx, a, da, kn[o], D);
+    float cur[kMaxPerLane];
+    load_vec(cur, dkey + o * D, D);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) cur[i] += dkx[i];
+    store_vec(dkey + o * D, cur, D);
+  }
+  __syncthreads();
+  const float* Ch = C + (int64_t)h * M * D;
+  block_gemm<2, 4>(
+      c, D, M, [&](int t, int m) { return Ds[t * M + m]; },
+      [&](int m, int d) { return Ch[m * D + d]; },
+      [&](int t, int d, float acc) { dkey[row(u, T, t0 + t) * D + d] += acc; });
+}
+
+// out[h] += scale[h] * sum_{b, t} X^T Y over the rows of head h.
+constexpr int kHoTile = 32;
+constexpr int kHoRows = 64;
+constexpr int kHoSplit = 2048;  // tokens per CTA
+__global__ void __launch_bounds__(256) k_head_outer(int B, int T, int H, const float* X, int P,
+                                                    int xmode, const float* Y, int Q,
+                                                    const float* scale, int64_t scale_stride,
+                                                    float cscale, float* out) {
+  const int h = blockIdx.x;
+  const int tp = (P + kHoTile - 1) / kHoTile, tq = (Q + kHoTile - 1) / kHoTile;
+  const int p0 = (blockIdx.y / tq) * kHoTile, q0 = (blockIdx.y % tq) * kHoTile;
+  const int pw = min(kHoTile, P - p0), qw = min(kHoTile, Q - q0);
+  const int64_t total = (int64_t)B * T;
+  const int64_t r0 = (int64_t)blockIdx.z * kHoSplit;
+  const int64_t r1 = min(total, r0 + kHoSplit);
+  __shared__ float Xs[kHoRows * kHoTile], Ys[kHoRows * kHoTile], Acc[kHoTile * kHoTile];
+  for (int i = threadIdx.x; i < kHoTile * kHoTile; i += blockDim.x) Acc[i] = 0.f;
+  for (int64_t rr = r0; rr < r1; rr += kHoRows) {
+    const int rows = (int)min((int64_t)kHoRows, r1 - rr);
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * kHoTile; i += blockDim.x) {
+      const int rw = i / kHoTile, cc = i - rw * kHoTile;
+      const int64_t g = rr + rw;  // (b, t) flattened
+      const int b = (int)(g / T), t = (int)(g - (int64_t)b * T);
+      const int64_t o = row(b * H + h, T, t);
+      float x = 0.f;
+      if (cc < pw) {
+        if (xmode == 2) x = 1.f;
+        else {
+          x = X[o * P + p0 + cc];
+          if (xmode == 1) x = gelu(x);
+        }
+      }
+      Xs[i] = x;
+      Ys[i] = cc < qw ? Y[o * Q + q0 + cc] : 0.f;
+    }
+    __syncthreads();
+    block_gemm<2, 2>(
+        pw, qw, rows, [&](int p, int r) { return Xs[r * kHoTile + p]; },
+        [&](int r, int q) { return Ys[r * kHoTile + q]; },
+        [&](int p, int q, float acc) { Acc[p * kHoTile + q] += acc; });
+  }
+  __syncthreads();
+  const float s = cscale * (scale ? scale[(int64_t)h * scale_stride] : 1.f);
+  float* o = out + (int64_t)h * P * Q;
+  for (int i = threadIdx.x; i < pw * qw; i += blockDim.x) {
+    const int p = i / qw, q = i - p * qw;
+    atomicAdd(&o[(p0 + p) * Q + q0 + q], s * Acc[p * kHoTile + q]);
+  }
+}
+
+// one warp per (u, t): final input gradients in the input layout / dtype.
+__global__ void k_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
+                            const float* qn, const float* dqh, const float* dq_direct,
+                            const float* dkey, const float* dval, void* dq, void* dk, void* dv) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int U = B * H;
+  if (w >= U * T) return;
+  const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
+  const int64_t dst = ((int64_t)b * T + t) * H + h;
+  const float nrm = qn[w];
+  float yd = 0.f;
+  for (int d = lane; d < D; d += 32) yd += qh[(int64_t)w * D + d] * dqh[(int64_t)w * D + d];
+  yd = warp_sum(yd);
+  for (int d = lane; d < D; d += 32) {
+    const int64_t i = (int64_t)w * D + d;
+    const float g = nrm > kUnitEps ? (dqh[i] - qh[i] * yd) / nrm : dqh[i] / kUnitEps;
+    store_out(dq, dst * D + d, g + dq_direct[i], dt);
+    store_out(dk, dst * D + d, dkey[i], dt);
+  }
+  for (int d = lane; d < Dv; d += 32) store_out(dv, dst * Dv + d, dval[(int64_t)w * Dv + d], dt);
+}
+
+// per head: scalar parameter gradients from per-unit sums.
+__global__ void k_fold(FoldArgs a) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= a.H) return;
+  const int H = a.H, L = a.L, E = a.E;
+  auto S = [&](int j, int slot) {
+    float s = 0.f;
+    for (int b = 0; b < a.B; ++b) s += a.scal[((int64_t)(b * H + h) * L + j) * kNScal + slot];
+    return s;
+  };
+  auto SE = [&](int e, int slot) {
+    float s = 0.f;
+    for (int b = 0; b < a.B; ++b) s += a.scalE[((int64_t)(b * H + h) * E + e) * kNEdge + slot];
+    return s;
+  };
+  float ow[kMaxLevels], dow[kMaxLevels];
+  float mx = -INFINITY, ssum = 0.f;
+  for (int j = 0; j < L; ++j) mx = fmaxf(mx, a.output_logits[j * H + h]);
+  for (int j = 0; j < L; ++j) {
+    ow[j] = __expf(a.output_logits[j * H + h] - mx);
+    ssum += ow[j];
+  }
+  float dot = 0.f;
+  for (int j = 0; j < L; ++j) {
+    ow[j] /= ssum;
+    dow[j] = S(j, kS_OutW);
+    dot += ow[j] * dow[j];
+  }
+  for (int j = 0; j < L; ++j) {
+    a.g_output_logits[j * H + h] += ow[j] * (dow[j] - dot);
+    const float tk = tanhf(a.residual_raw[(j * H + h) * 2]);
+    const float tv = tanhf(a.residual_raw[(j * H + h) * 2 + 1]);
+    a.g_residual_raw[(j * H + h) * 2] += S(j, kS_EtaK) * .25f * (1.f - tk * tk);
+    a.g_residual_raw[(j * H + h) * 2 + 1] += S(j, kS_EtaV) * .25f * (1.f - tv * tv);
+    a.g_count_gain_raw[j * H + h] += S(j, kS_CountGain) * sigmoid(a.count_gain_raw[j * H + h]);
+    a.g_route_mlp_gain[j * H + h] += S(j, kS_MlpGain);
+    a.g_relation_gain[j * H + h] += S(j, kS_RelGain);
+    // edge-logit softmax over the edges into j
+    float w[kMaxIn], dw[kMaxIn];
+    int ids[kMaxIn], n = 0;
+    for (int e = 0; e < E; ++e)
+      if (a.edge_dst[e] == j) ids[n++] = e;
+    if (n) {
+      float m2 = -INFINITY, s2 = 0.f, d2 = 0.f;
+      for (int i = 0; i < n; ++i) m2 = fmaxf(m2, a.edge_logits[ids[i] * H + h]);
+      for (int i = 0; i < n; ++i) {
+        w[i] = __expf(a.edge_logits[ids[i] * H + h] - m2);
+        s2 += w[i];
+      }
+      for (int i = 0; i < n; ++i) {
+        w[i] /= s2;
+        dw[i] = SE(ids[i], kE_W);
+        d2 += w[i] * dw[i];
+      }
+      for (int i = 0; i < n; ++i) a.g_edge_logits[ids[i] * H + h] += w[i] * (dw[i] - d2);
+    }
+  }
+  for (int e = 0; e < E; ++e) {
+    const float sd = sigmoid(a.relation_decay_raw[e * H + h]);
+    if (!a.pos_none) a.g_relation_decay_raw[e * H + h] += -SE(e, kE_G) * sd;
+    const float sb = sigmoid(a.relation_beta_raw[e * H + h]);
+    a.g_relation_beta_raw[e * H + h] += SE(e, kE_B) * sb * (1.f - sb);
+  }
+}
+
+int blocks_for(int64_t n, int per) { return (int)((n + per - 1) / per); }
+
+template <class Kern, class... Args>
+cudaError_t launch_smem(Kern k, int grid, size_t smem, cudaStream_t st, Args... args) {
+  if (grid <= 0) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<grid, 256, smem, st>>>(args...);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
+                         int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0,
+                         cudaStream_t st) {
+  const int rows = B * T * H;
+  if (!rows) return cudaSuccess;
+  k_input<<<blocks_for(rows, 8), 256, 0, st>>>(q, k, v, dt, B, T, H, D, Dv, qf, qh, qn, key0,
+                                                val0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_level_prep(int U, int T, int H, int D, int M, const float* key, const float* C,
+                              const float* Wg, const float* gbias, float beta_max, int pos_none,
+                              float* nk, float* kn, float* slot, float* ns, float* sn, float* raw4,
+                              float* gates, cudaStream_t st) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const size_t smem = sizeof(float) * kRowsPerTile * (D + M);
+  return launch_smem(k_level_prep, U * ntile, smem, st, U, T, H, D, M, key, C, Wg, gbias,
+                     beta_max, pos_none, nk, kn, slot, ns, sn, raw4, gates);
+}
+
+cudaError_t launch_level_post(int U, const Blocks& bl, int post, int H, int D, int Dv, int M,
+                              int with_residual, const float* nk, const float* key, const float* val,
+                              const float* Abnd, const float* Bbnd, const float* fzA,
+                              const float* fzB, const float* residual_raw, int j, float* write,
+                              float* bsum, float* key_next, float* val_next, cudaStream_t st) {
+  const size_t smem = sizeof(float) * (D * M + M * Dv + kRowsPerTile * M);
+  return launch_smem(k_level_post, U * bl.nb, smem, st, U, bl, post, H, D, Dv, M, with_residual,
+                     nk, key, val, Abnd, Bbnd, fzA, fzB, residual_raw, j, write, bsum, key_next,
+                     val_next);
+}
+
+cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scale,
+                          const float* count_gain_raw, int j, const float* n0, const float* bsum,
+                          const float* write, const float* raw, float* counts, float* logits,
+                          float* lh, float* ln, float* wh, float* wn, float* n_final,
+                          cudaStream_t st) {
+  if (!U || !bl.nb) return cudaSuccess;
+  k_counts<<<U * bl.nb, 256, 0, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write,
+                                      raw, counts, logits, lh, ln, wh, wn, n_final);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rel_gates(int U, int H, int E, int pos_none, const float* decay_raw,
+                             const float* beta_raw, float* ge, float* be, cudaStream_t st) {
+  if (!E || !U) return cudaSuccess;
+  k_rel_gates<<<blocks_for((int64_t)E * U, 256), 256, 0, st>>>(U, H, E, pos_none, decay_raw,
+                                                                beta_raw, ge, be);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bridge(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                          const float* edge_logits, const float* relation_gain,
+                          const float* route_up, const float* route_down,
+                          const float* route_mlp_gain, const float* Wrs, const float* Wqs,
+                          float qs, const float* logits, const float* qf, float* r, float* hp,
+                          float* mlp, float* route, float* qoh, float* qon, cudaStream_t st) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const size_t smem = sizeof(float) * kRowsPerTile * 4 * M;
+  return launch_smem(k_bridge, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
+                     relation_gain, route_up, route_down, route_mlp_gain, Wrs, Wqs, qs, logits, qf,
+                     r, hp, mlp, route, qoh, qon);
+}
+
+cudaError_t launch_mix(int B, int T, int H, int Dv, int L, const float* output_logits,
+                       const float* const* y, void* out, int dt, cudaStream_t st) {
+  const int rows = B * T * H;
+  if (!rows) return cudaSuccess;
+  YPtrs yp;
+  for (int j = 0; j < L; ++j) yp.y[j] = y[j];
+  k_mix<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, Dv, L, output_logits, yp, out, dt);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy(float* dst, const float* src, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_copy<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_to_bthx(const float* src, void* dst, int dt, int B, int T, int H, int X,
+                           cudaStream_t st) {
+  const int64_t n = (int64_t)B * T * H * X;
+  if (n <= 0) return cudaSuccess;
+  k_to_bthx<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, dt, B, T, H, X);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(float* dst, const float* src, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_add<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_boundary(float* dst, const float* src, int U, int nb1, int idx,
+                                   int64_t sz, cudaStream_t st) {
+  const int64_t n = (int64_t)U * sz;
+  if (n <= 0) return cudaSuccess;
+  k_boundary<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, U, nb1, idx, sz, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_add_boundary(float* dst, const float* src, int U, int nb1, int idx,
+                                        int64_t sz, cudaStream_t st) {
+  const int64_t n = (int64_t)U * sz;
+  if (n <= 0) return cudaSuccess;
+  k_boundary<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, U, nb1, idx, sz, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scales(int U, int H, int L, const float* output_logits, float* ow_scale,
+                          cudaStream_t st) {
+  k_scales<<<blocks_for(U, 128), 128, 0, st>>>(U, H, L, output_logits, ow_scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt,
+                           const float* const* y, float* dout_f, float* scal, cudaStream_t st) {
+  const int rows = B * T * H;
+  if (!rows) return cudaSuccess;
+  YPtrs yp;
+  for (int j = 0; j < L; ++j) yp.y[j] = y[j];
+  k_mix_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, Dv, L, dout, dt, yp, dout_f, scal);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                              const float* edge_logits, const float* relation_gain,
+                              const float* route_up, const float* route_down,
+                              const float* route_mlp_gain, const float* Wrs, const float* Wqs,
+                              float qs, const float* logits, const float* r, const float* hp,
+                              const float* mlp, const float* qoh, const float* qon,
+                              const float* dqoh, float* dqo, float* droute, float* dhp,
+                              float* dlogits, float* dq_direct, float* scal, float* scalE, int E,
+                              cudaStream_t st) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const size_t smem = sizeof(float) * (kRowsPerTile * 4 * M + 32 + kMaxIn);
+  return launch_smem(k_bridge_bwd, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
+                     relation_gain, route_up, route_down, route_mlp_gain, Wrs, Wqs, qs, logits, r,
+                     hp, mlp, qoh, qon, dqoh, dqo, droute, dhp, dlogits, dq_direct, scal, scalE,
+                     E);
+}
+
+cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int j,
+                              float read_scale, const float* count_gain_raw, const float* logits,
+                              const float* counts, const float* lh, const float* ln,
+                              const float* wh, const float* wn, const float* dlh,
+                              const float* dwh, const float* dlogits, float* dwrite, float* draw,
+                              float* dn, float* dnsum, float* scal, cudaStream_t st) {
+  const int rows = U * bl.T;
+  if (!rows) return cudaSuccess;
+  k_logits_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
+                                                     count_gain_raw, logits, counts, lh, ln, wh,
+                                                     wn, dlh, dwh, dlogits, dwrite, draw, dn,
+                                                     dnsum, scal);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, const float* dnsum,
+                              const float* dn_final, float* dwrite, float* dn0, cudaStream_t st) {
+  if (!U || !bl.nb) return cudaSuccess;
+  k_counts_bwd<<<U * bl.nb, 256, 0, st>>>(U, bl, M, dn, dnsum, dn_final, dwrite, dn0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_post_bwd(int U, const Blocks& bl, int post, int offset, int H, int D, int Dv,
+                            int M, int L, int j, int with_residual, const float* nk,
+                            const float* write, const float* Abnd, const float* Bbnd,
+                            const float* fzA, const float* fzB, const float* residual_raw,
+                            const float* dkey, const float* dval, float* dwrite, float* dnk,
+                            float* extA, float* extB, float* dfzA, float* dfzB, float* scal,
+                            cudaStream_t st) {
+  const size_t smem = sizeof(float) * (D * M + M * Dv + 2 * kRowsPerTile * M + 34);
+  return launch_smem(k_post_bwd, U * bl.nb, smem, st, U, bl, post, offset, H, D, Dv, M, L, j,
+                     with_residual, nk, write, Abnd, Bbnd, fzA, fzB, residual_raw, dkey, dval,
+                     dwrite, dnk, extA, extB, dfzA, dfzB, scal);
+}
+
+cudaError_t launch_prep_bwd(int U, int T, int H, int D, int M, const float* C, const float* Wg,
+                            float beta_max, int pos_none, const float* raw4, const float* nk,
+                            const float* kn, const float* ns, const float* sn, const float* dgates,
+                            const float* dnk, const float* dns, float* dslot, float* d4,
+                            float* dkey, cudaStream_t st) {
+  const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
+  const size_t smem = sizeof(float) * kRowsPerTile * M;
+  return launch_smem(k_prep_bwd, U * ntile, smem, st, U, T, H, D, M, C, Wg, beta_max, pos_none,
+                     raw4, nk, kn, ns, sn, dgates, dnk, dns, dslot, d4, dkey);
+}
+
+cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xmode,
+                              const float* Y, int Q, const float* scale, int64_t scale_stride,
+                              float cscale, float* out, cudaStream_t st) {
+  const int64_t total = (int64_t)B * T;
+  if (!total) return cudaSuccess;
+  const int tp = (P + kHoTile - 1) / kHoTile, tq = (Q + kHoTile - 1) / kHoTile;
+  dim3 grid(H, tp * tq, (unsigned)((total + kHoSplit - 1) / kHoSplit));
+  k_head_outer<<<grid, 256, 0, st>>>(B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale,
+                                     out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
+                             const float* qn, const float* dqh, const float* dq_direct,
+                             const float* dkey, const float* dval, void* dq, void* dk, void* dv,
+                             cudaStream_t st) {
+  const int rows = B * T * H;
+  if (!rows) return cudaSuccess;
+  k_input_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, D, Dv, dt, qh, qn, dqh, dq_direct,
+                                                    dkey, dval, dq, dk, dv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fold(const FoldArgs& a, cudaStream_t st) {
+  k_fold<<<blocks_for(a.H, 64), 64, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace gpa

@@ -1,0 +1,137 @@
+/* gpa_b200.h -- C ABI of the B200-native DenseGPA attention core.
+ *
+ * The library (gpa_b200/libgpa_b200.so, sm_100a) computes the forward and the
+ * backward of fisalt/GPA's DenseGPA core on CUDA device buffers.  Every entry
+ * point is stream-ordered on the caller's stream, allocates no device memory
+ * (the caller passes the workspaces it sized with the *_bytes queries), never
+ * synchronises the device and never traps: failures return a nonzero status
+ * and a message readable with gpa_b200_last_error().
+ *
+ * Reference interfaces replaced (paths relative to the fisalt/GPA project):
+ *   gpa_b200_forward  - DenseGPA.forward            src/gpa/attention.py:347-414
+ *                       (block loop :376-405, lag block :299-345, token :264-297,
+ *                        and the FLA GDN dispatch in gdn_scan src/gpa/ops.py:58-77)
+ *   gpa_b200_backward - autograd through the above (FLA chunk_gated_delta_rule
+ *                       backward plus ATen autograd of src/gpa/attention.py:161-345)
+ *
+ * Conventions: q, k [B,T,H,Dk] and v, out [B,T,H,Dv] are contiguous in the
+ * input dtype (fp32 / bf16 / fp16).  Parameters, states and their gradients
+ * are contiguous fp32 tensors with the reference's shapes
+ * (src/gpa/attention.py:104-135, src/gpa/state.py:30-58).  Status codes:
+ * 0 ok, 1 bad argument, 2 unsupported configuration, 3 CUDA launch failure.
+ */
+#ifndef GPA_B200_H
+#define GPA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPA_B200_MAX_LEVELS 8
+#define GPA_B200_MAX_EDGES 56
+
+enum { GPA_B200_OK = 0, GPA_B200_BAD_ARGUMENT = 1, GPA_B200_UNSUPPORTED = 2,
+       GPA_B200_LAUNCH_FAILURE = 3 };
+enum { GPA_B200_F32 = 0, GPA_B200_BF16 = 1, GPA_B200_F16 = 2 };
+
+/* Shapes and the scalar GPAConfig fields the core reads (src/gpa/attention.py:17-43). */
+typedef struct GpaDims {
+  int32_t batch, length, heads, key_dim, value_dim, levels;
+  int32_t slots[GPA_B200_MAX_LEVELS];
+  int32_t chunk_size;      /* 1 = exact token recurrence, 2..64 = lag blocks */
+  int32_t chunk_offset;    /* GPAState.chunk_offset of the incoming cache */
+  int32_t input_dtype;     /* GPA_B200_F32 / _BF16 / _F16 */
+  int32_t positional_none; /* positional_mode == "none": zero decays */
+  float read_scale, query_scale, beta_max;
+} GpaDims;
+
+/* Parameter pointers (per-level lists by level, edges in the reference order
+ * (i, j) for i != j, row-major).  The learned prefixes are not listed: they
+ * enter through the incoming state. */
+typedef struct GpaParams {
+  const float* center[GPA_B200_MAX_LEVELS];       /* [H,M,Dk] */
+  const float* route_weight[GPA_B200_MAX_LEVELS]; /* [H,M,M] */
+  const float* query_weight[GPA_B200_MAX_LEVELS]; /* [H,Dk,M] */
+  const float* route_up[GPA_B200_MAX_LEVELS];     /* [H,M,2M] */
+  const float* route_down[GPA_B200_MAX_LEVELS];   /* [H,2M,M] */
+  const float* gate_weight[GPA_B200_MAX_LEVELS];  /* [H,Dk,4] */
+  const float* gate_bias[GPA_B200_MAX_LEVELS];    /* [H,4] */
+  const float* residual_raw;       /* [L,H,2] */
+  const float* count_gain_raw;     /* [L,H] */
+  const float* route_mlp_gain;     /* [L,H] */
+  const float* output_logits;      /* [L,H] */
+  const float* edge_logits;        /* [E,H] */
+  const float* relation_gain;      /* [L,H] */
+  const float* relation_decay_raw; /* [E,H] */
+  const float* relation_beta_raw;  /* [E,H] */
+} GpaParams;
+
+/* Same layout, writable: parameter gradients (accumulated with +=). */
+typedef struct GpaParamGrads {
+  float* center[GPA_B200_MAX_LEVELS];
+  float* route_weight[GPA_B200_MAX_LEVELS];
+  float* query_weight[GPA_B200_MAX_LEVELS];
+  float* route_up[GPA_B200_MAX_LEVELS];
+  float* route_down[GPA_B200_MAX_LEVELS];
+  float* gate_weight[GPA_B200_MAX_LEVELS];
+  float* gate_bias[GPA_B200_MAX_LEVELS];
+  float* residual_raw;
+  float* count_gain_raw;
+  float* route_mlp_gain;
+  float* output_logits;
+  float* edge_logits;
+  float* relation_gain;
+  float* relation_decay_raw;
+  float* relation_beta_raw;
+} GpaParamGrads;
+
+/* Recurrent cache tensors, GPAState layout (src/gpa/state.py:30-58).
+ * frozen_* are the lag-block residual snapshots; NULL when absent. */
+typedef struct GpaStateRef {
+  float* inner[GPA_B200_MAX_LEVELS];  /* A [B,H,Dk,M] */
+  float* outer[GPA_B200_MAX_LEVELS];  /* B [B,H,M,Dv] */
+  float* count[GPA_B200_MAX_LEVELS];  /* n [B,H,M] */
+  float* relation[GPA_B200_MAX_EDGES];/* R [B,H,M_i,M_j] */
+  float* frozen_inner[GPA_B200_MAX_LEVELS];
+  float* frozen_outer[GPA_B200_MAX_LEVELS];
+} GpaStateRef;
+
+/* Bytes of the forward's saved buffer (kept alive until gpa_b200_backward). */
+size_t gpa_b200_saved_bytes(const GpaDims* dims);
+/* Bytes of the backward scratch buffer. */
+size_t gpa_b200_scratch_bytes(const GpaDims* dims);
+
+/* Forward of one call: out [B,T,H,Dv]; state_out receives the final cache
+ * (frozen_* written when (chunk_offset + T) % chunk_size != 0).
+ * Replaces DenseGPA.forward (src/gpa/attention.py:347-414). */
+int gpa_b200_forward(const GpaDims* dims, const GpaParams* params, const void* q, const void* k,
+                     const void* v, const GpaStateRef* state_in, GpaStateRef* state_out,
+                     void* out, void* saved, size_t saved_bytes, void* stream);
+
+/* Backward of one forward call.  dstate_out holds the gradients of the
+ * returned cache tensors (NULL members count as zero).  Writes dq, dk, dv
+ * (input dtype), the incoming-cache gradients dstate_in (every member of
+ * state_in that is non-NULL), and accumulates the parameter gradients. */
+int gpa_b200_backward(const GpaDims* dims, const GpaParams* params, const GpaStateRef* state_in,
+                      const void* saved, const void* dout, const GpaStateRef* dstate_out,
+                      void* dq, void* dk, void* dv, GpaStateRef* dstate_in,
+                      GpaParamGrads* dparams, void* scratch, size_t scratch_bytes, void* stream);
+
+/* Diagnostics: copy the per-level post-MLP routes of a forward call out of its
+ * saved buffer into routes[j] ([B,T,H,M_j], input dtype).  Replaces the
+ * return_diagnostics routes of DenseGPA.forward (src/gpa/attention.py:407-413). */
+int gpa_b200_routes(const GpaDims* dims, const void* saved, void* const* routes, void* stream);
+
+/* Message of the last failure on the calling thread (0 if none). */
+int gpa_b200_last_error(char* buf, size_t len);
+
+/* ABI version of this header. */
+int gpa_b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPA_B200_H */
