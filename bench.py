@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""DenseGPA fwd+bwd throughput on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+
+Workload per rank (weak scaling): H=16, Dk=Dv=128, slots (64,64,64,128),
+chunk 64, B=8, T=8192, bf16 activations, fp32 state; q, k ~ N(0,1)
+L2-normalised per head, v ~ N(0,1), learnable prefixes re-drawn at N(0,0.02);
+seed 0 (data seeded 1000 + rank).  One step = forward, out.float().square().mean(),
+backward (every parameter, input and prefix gradient); with N > 1 the
+parameter gradients are all-reduced over NCCL (data parallel), the only
+cross-GPU exchange the path has.
+
+Prints one JSON line (rank 0).  ``value`` is the device-timed tokens/s of the
+whole job with inputs resident in HBM (inputs are 805 MB per rank, larger than
+the 126 MB L2, and each step streams tens of GB of activations, so no L2 flush
+is needed); ``e2e`` is the same step through the public API with the inputs
+copied from pinned host memory and the loss read back every step.
+``--impl reference`` times the reference algorithm's CPU implementation (the
+test oracle, a restatement of the reference torch backend) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DenseGPA fwd+bwd tokens/s at 1/2/4/8 B200 (T=8192) + % of roofline"
+CFG = dict(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
+BATCH, LENGTH = 8, 8192
+CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ------------------------------------------------------------- algorithmic work
+
+def gdn_g(K, V, C):
+    """Chunked GDN forward FLOPs per token (A, UT solve, W, U, W S, Q S, QK^T V, K^T U)."""
+    return 2 * (3 * K * V + 3 * C * K + 2 * C * V + C * C / 3)
+
+
+def layer_flops_per_token_head(cfg):
+    """Forward FLOPs per token-head; fwd+bwd counts 3x (backward = 2x forward)."""
+    D, Dv, C, M = cfg["key_dim"], cfg["value_dim"], cfg["chunk_size"], cfg["slots"]
+    f = sum(gdn_g(D, m, C) + gdn_g(m, Dv, C) for m in M)
+    f += sum(gdn_g(M[i], M[j], C) for i in range(len(M)) for j in range(len(M)) if i != j)
+    f += 2 * sum(4 * D * m + m * Dv + 5 * m * m + 4 * D for m in M)
+    return f
+
+
+def gdn_scans(cfg):
+    """(K, V) of every GDN scan of the layer: inner, outer, relations."""
+    D, Dv, M = cfg["key_dim"], cfg["value_dim"], cfg["slots"]
+    inner = [(D, m) for m in M]
+    outer = [(m, Dv) for m in M]
+    rel = [(M[i], M[j]) for i in range(len(M)) for j in range(len(M)) if i != j]
+    return inner, outer, rel
+
+
+def kernel_flops(cfg, units, length):
+    """Algorithmic FLOPs per training step of each GDN scan kernel (whole step).
+
+    Per block of c tokens with key width K and value width V:
+      fwd_chunk   c^2 (2K + V)              (K K^T lower half, UT solve of [V | K])
+      fwd_state   4 c K V                   (W = U - Wk S, S += K^T W)
+      fwd_out     c^2 K + 2 c K V + c^2 V   (Q K^T, Q S, P W)
+      bwd_local   3 c^2 K + 2 c^2 V + 4 c K V
+      bwd_state   6 c K V
+      bwd_chunk_v c^2 K + 4 c K V + 2 c^2 V
+      bwd_chunk_k 5 c^2 K
+    """
+    c = cfg["chunk_size"]
+    nb = -(-length // c)
+    inner, outer, rel = gdn_scans(cfg)
+    per = {
+        "gdn_fwd_chunk": lambda K, V: c * c * (2 * K + V),
+        "gdn_fwd_state": lambda K, V: 4 * c * K * V,
+        "gdn_fwd_out": lambda K, V: c * c * K + 2 * c * K * V + c * c * V,
+        "gdn_bwd_local": lambda K, V: 3 * c * c * K + 2 * c * c * V + 4 * c * K * V,
+        "gdn_bwd_state": lambda K, V: 6 * c * K * V,
+        "gdn_bwd_chunk_v": lambda K, V: c * c * K + 4 * c * K * V + 2 * c * c * V,
+        "gdn_bwd_chunk_k": lambda K, V: 5 * c * c * K,
+    }
+    allscans = inner + outer + rel
+    use = {
+        # forward: chunk + state for all scans; out for inner, outer reads, relations
+        "gdn_fwd_chunk": allscans + allscans,   # forward + backward recompute
+        "gdn_fwd_state": allscans,
+        "gdn_fwd_out": allscans,
+        "gdn_bwd_local": allscans,
+        "gdn_bwd_state": allscans,
+        "gdn_bwd_chunk_v": allscans,
+        "gdn_bwd_chunk_k": allscans,
+    }
+    return {k: units * nb * sum(per[k](K, V) for K, V in use[k]) for k in per}
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- b200 arm
+
+def make_model(device, cfg=CFG):
+    from gpa_b200 import DenseGPA, GPAConfig
+    torch.manual_seed(0)
+    model = DenseGPA(GPAConfig(**cfg))
+    g = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.startswith(("inner_prefix", "outer_prefix", "relation_prefix")):
+                p.copy_(torch.randn(p.shape, generator=g) * .02)
+    return model.to(device)
+
+
+def make_inputs(batch, length, seed, device="cpu", dtype=torch.bfloat16, cfg=CFG):
+    g = torch.Generator().manual_seed(seed)
+    H, D, Dv = cfg["heads"], cfg["key_dim"], cfg["value_dim"]
+    q = torch.randn(batch, length, H, D, generator=g)
+    k = torch.randn(batch, length, H, D, generator=g)
+    v = torch.randn(batch, length, H, Dv, generator=g)
+    q = q / q.norm(dim=-1, keepdim=True)
+    k = k / k.norm(dim=-1, keepdim=True)
+    return [x.to(dtype).to(device) for x in (q, k, v)]
+
+
+def allreduce_grads(model, world):
+    if world == 1:
+        return
+    grads = [p.grad for p in model.parameters() if p.grad is not None]
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat)
+    flat /= world
+    off = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[off:off + n].view_as(g))
+        off += n
+
+
+def run_b200(args, rank, world, local):
+    from gpa_b200 import _lib
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    model = make_model(device)
+    q, k, v = make_inputs(BATCH, LENGTH, 1000 + rank, device)
+    for x in (q, k, v):
+        x.requires_grad_(True)
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        for x in (q, k, v):
+            x.grad = None
+        out, _ = model(q, k, v)
+        loss = out.float().square().mean()
+        loss.backward()
+        allreduce_grads(model, world)
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    launches0 = _lib.launch_count()
+    _lib.profile_start()
+    with ClockSampler(local) as clocks:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    prof = _lib.profile_stop()
+    launches = _lib.launch_count() - launches0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_all = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
+    ms = float(ms_all.item())
+
+    # end-to-end through the public API with pinned host inputs
+    hq, hk, hv = (x.detach().cpu().pin_memory() for x in (q, k, v))
+    del q, k, v
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+
+    def e2e_step():
+        model.zero_grad(set_to_none=True)
+        xs = [x.to(device, non_blocking=True).requires_grad_() for x in (hq, hk, hv)]
+        out, _ = model(*xs)
+        loss = out.float().square().mean()
+        loss.backward()
+        allreduce_grads(model, world)
+        return loss.item()
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_steps = max(1, args.steps // 2)
+    t0 = time.perf_counter()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max(ev2.elapsed_time(ev3), (time.perf_counter() - t0) * 1e3) / e2e_steps
+    e2e_all = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(e2e_all, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_all.item())
+
+    tokens = BATCH * LENGTH * world
+    value = tokens / (ms / 1e3)
+    pk = peaks()
+    units = BATCH * CFG["heads"]
+    kf = kernel_flops(CFG, units, LENGTH)
+    # dominant kernel by device time
+    top = max(prof, key=lambda n: prof[n][1])
+    n_launch, tot_ms = prof[top]
+    per_step_ms = {n: round(t / args.steps, 3) for n, (c, t) in prof.items()}
+    if top in kf:
+        achieved = kf[top] / (tot_ms / args.steps / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 5),
+                "traffic": None, "kernel": top, "launches_per_step": n_launch // args.steps,
+                "avg_launch_ms": round(tot_ms / n_launch, 4),
+                "flops_per_step": kf[top], "peak_source": pk["source"]}
+    else:
+        roof = {"bound": "tensor", "achieved": None, "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": None, "traffic": None, "kernel": top,
+                "peak_source": pk["source"]}
+    step_flops = 3 * layer_flops_per_token_head(CFG) * CFG["heads"] * BATCH * LENGTH
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), q/k L2-normalised; random-init weights, prefixes N(0,0.02))",
+        "config": {"workload": "config 2: DenseGPA layer fwd+bwd", "model": "DenseGPA",
+                   "global_batch": BATCH * world, "seq_len": LENGTH, "heads": CFG["heads"],
+                   "key_dim": CFG["key_dim"], "value_dim": CFG["value_dim"],
+                   "slots": list(CFG["slots"]), "chunk_size": CFG["chunk_size"],
+                   "state_dtype": "fp32", "parallelism": f"dp{world} (batch x heads per rank)",
+                   "l2": "inputs 805 MB/rank > 126 MB L2; no flush"},
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "step_roofline": {"flops_per_step": step_flops,
+                          "achieved_tflops": round(step_flops / (ms / 1e3) / 1e12, 3),
+                          "frac_of_bf16_peak": round(step_flops / (ms / 1e3) / 1e12 / pk["bf16_tflops_sustained"], 5)},
+        "kernel_ms_per_step": per_step_ms,
+        "clocks": clocks.summary(),
+    }
+    return result
+
+
+# --------------------------------------------------------------- CPU (oracle) arm
+
+def cpu_sample_step(threads):
+    """One fwd+bwd of the reference algorithm (oracle) on the bounded CPU sample."""
+    import oracle
+    torch.set_num_threads(threads)
+    model = make_model("cpu")
+    p = {n: t.detach().clone().requires_grad_() for n, t in model.state_dict().items()}
+    ocfg = oracle.OracleConfig(heads=CFG["heads"], key_dim=CFG["key_dim"],
+                               value_dim=CFG["value_dim"], slots=CFG["slots"],
+                               chunk_size=CFG["chunk_size"])
+    xs = [x.requires_grad_() for x in make_inputs(CPU_SAMPLE["batch"], CPU_SAMPLE["length"], 1000)]
+
+    def step():
+        for t in list(p.values()) + xs:
+            t.grad = None
+        out, _ = oracle.forward(ocfg, p, *xs)
+        out.float().square().mean().backward()
+
+    return step
+
+
+def cpu_baseline(threads):
+    step = cpu_sample_step(threads)
+    step()
+    t0 = time.perf_counter()
+    step()
+    dt = time.perf_counter() - t0
+    toks = CPU_SAMPLE["batch"] * CPU_SAMPLE["length"]
+    return {"value": round(toks / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle (restated reference torch backend) fwd+bwd, config-2 layer, "
+                      f"B={CPU_SAMPLE['batch']}, T={CPU_SAMPLE['length']}, bf16 activations, "
+                      f"{dt:.2f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    step = cpu_sample_step(threads)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    toks = CPU_SAMPLE["batch"] * CPU_SAMPLE["length"]
+    value = toks / dt
+    return {"metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config 2: DenseGPA layer fwd+bwd (bounded CPU sample)",
+                       "model": "DenseGPA", "global_batch": CPU_SAMPLE["batch"],
+                       "seq_len": CPU_SAMPLE["length"], "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"B={CPU_SAMPLE['batch']}, T={CPU_SAMPLE['length']}"},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(minutes=10),
+                                device_id=torch.device("cuda", local))
+    res = run_b200(args, rank, world, local)
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(os.cpu_count() or 1)
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -50,7 +50,8 @@ class GpaStateRef(ctypes.Structure):
 
 EXPORTS = ("gpa_b200_saved_bytes", "gpa_b200_scratch_bytes", "gpa_b200_forward",
            "gpa_b200_backward", "gpa_b200_routes", "gpa_b200_last_error",
-           "gpa_b200_abi_version")
+           "gpa_b200_abi_version", "gpa_b200_launch_count", "gpa_b200_profile_start",
+           "gpa_b200_profile_stop")
 
 _lib = None
 
@@ -83,6 +84,12 @@ def load():
     lib.gpa_b200_last_error.restype = c_int
     lib.gpa_b200_abi_version.argtypes = []
     lib.gpa_b200_abi_version.restype = c_int
+    lib.gpa_b200_launch_count.argtypes = []
+    lib.gpa_b200_launch_count.restype = ctypes.c_longlong
+    lib.gpa_b200_profile_start.argtypes = []
+    lib.gpa_b200_profile_start.restype = c_int
+    lib.gpa_b200_profile_stop.argtypes = [c_char_p, c_size_t]
+    lib.gpa_b200_profile_stop.restype = c_int
     if lib.gpa_b200_abi_version() != ABI_VERSION:
         raise RuntimeError("libgpa_b200.so ABI version mismatch; rebuild it")
     _lib = lib
@@ -99,6 +106,23 @@ def check(rc: int, what: str):
     if rc in (1, 2):
         raise ValueError(msg)
     raise RuntimeError(msg)
+
+
+def launch_count() -> int:
+    """Kernels launched by the library in this process."""
+    return int(load().gpa_b200_launch_count())
+
+
+def profile_start():
+    check(load().gpa_b200_profile_start(), "gpa_b200_profile_start")
+
+
+def profile_stop() -> dict:
+    """{kernel: (launches, total_ms)} of the launches since profile_start()."""
+    import json
+    buf = ctypes.create_string_buffer(1 << 16)
+    check(load().gpa_b200_profile_stop(buf, len(buf)), "gpa_b200_profile_stop")
+    return {k: (int(v[0]), float(v[1])) for k, v in json.loads(buf.value.decode()).items()}
 
 
 def ptr(t) -> int | None:

@@ -8,8 +8,11 @@
 // The backward runs the same schedule in reverse; boundary-state gradients
 // coming from the writes and residuals enter the reverse GDN sweeps as
 // external terms.  Workspaces are caller-owned; nothing here allocates.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -18,6 +21,40 @@
 #include "level.cuh"
 
 namespace gpa {
+
+// ---------------------------------------------------------- launch accounting
+namespace {
+std::atomic<long long> g_launches{0};
+std::atomic<bool> g_profiling{false};
+std::mutex g_prof_mu;
+struct ProfRec {
+  const char* name;
+  cudaEvent_t a, b;
+};
+std::vector<ProfRec> g_recs;
+size_t g_used = 0;
+}  // namespace
+
+Launch::Launch(const char* name, cudaStream_t s) : slot(-1), st(s) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (!g_profiling.load(std::memory_order_relaxed)) return;
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  if (g_used == g_recs.size()) {
+    ProfRec r{name, nullptr, nullptr};
+    if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return;
+    g_recs.push_back(r);
+  }
+  slot = (int)g_used++;
+  g_recs[slot].name = name;
+  cudaEventRecord(g_recs[slot].a, st);
+}
+
+Launch::~Launch() {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  cudaEventRecord(g_recs[slot].b, st);
+}
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -187,7 +224,8 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
 
 // Backward scratch.
 struct Scratch {
-  float *dout_f, *ow_scale, *dqh, *dq_direct, *dkey, *dval, *scal, *scalE;
+  float *dout_f, *ow_scale, *dqh, *dq_direct, *dkey, *dval;
+  double *scal, *scalE;
   float *dqoh[kMaxLevels], *dqo[kMaxLevels], *droute[kMaxLevels], *dhp[kMaxLevels];
   float *dlogits[kMaxLevels], *dlh[kMaxLevels], *dwh[kMaxLevels], *dwrite[kMaxLevels];
   float *odK[kMaxLevels], *odW[kMaxLevels], *odG[kMaxLevels];
@@ -210,8 +248,8 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
   s->dq_direct = b.take(UT * g.D);
   s->dkey = b.take(UT * g.D);
   s->dval = b.take(UT * g.Dv);
-  s->scal = b.take((size_t)g.U * g.L * kNScal);
-  s->scalE = b.take((size_t)g.U * (g.E ? g.E : 1) * kNEdge);
+  s->scal = reinterpret_cast<double*>(b.take((size_t)g.U * g.L * kNScal * 2));
+  s->scalE = reinterpret_cast<double*>(b.take((size_t)g.U * (g.E ? g.E : 1) * kNEdge * 2));
   for (int j = 0; j < g.L; ++j) {
     const size_t M = g.M[j];
     s->dqoh[j] = b.take(UT * M);
@@ -475,8 +513,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
   CK(zero(x.dq_direct, UT * D, st));
   CK(zero(x.dkey, UT * D, st));
   CK(zero(x.dval, UT * Dv, st));
-  CK(zero(x.scal, (size_t)U * L * kNScal, st));
-  CK(zero(x.scalE, (size_t)U * (E ? E : 1) * kNEdge, st));
+  CK(zero(reinterpret_cast<float*>(x.scal), (size_t)U * L * kNScal * 2, st));
+  CK(zero(reinterpret_cast<float*>(x.scalE), (size_t)U * (E ? E : 1) * kNEdge * 2, st));
   for (int j = 0; j < L; ++j) {
     const size_t M = g.M[j];
     CK(zero(x.dqoh[j], UT * M, st));
@@ -571,8 +609,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
       d.dq = x.dlh[i];
       d.dk = x.dwh[i];
       d.dv = x.dwrite[tj];
-      d.dg = x.scalE + (size_t)e * kNEdge + kE_G;
-      d.dbeta = x.scalE + (size_t)e * kNEdge + kE_B;
+      d.dg64 = x.scalE + (size_t)e * kNEdge + kE_G;
+      d.dbeta64 = x.scalE + (size_t)e * kNEdge + kE_B;
       d.dg_su = (int64_t)E * kNEdge;
       d.dg_st = 0;
       d.dS0 = dsi->relation[e];
@@ -822,5 +860,40 @@ int gpa_b200_last_error(char* buf, size_t len) {
 }
 
 int gpa_b200_abi_version(void) { return 1; }
+
+long long gpa_b200_launch_count(void) { return g_launches.load(); }
+
+int gpa_b200_profile_start(void) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  g_used = 0;
+  g_profiling.store(true);
+  return GPA_B200_OK;
+}
+
+int gpa_b200_profile_stop(char* buf, size_t len) {
+  g_profiling.store(false);
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  std::map<std::string, std::pair<long long, double>> acc;
+  for (size_t i = 0; i < g_used; ++i) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(g_recs[i].b) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, g_recs[i].a, g_recs[i].b) != cudaSuccess)
+      return fail(GPA_B200_LAUNCH_FAILURE, "profile events could not be read");
+    auto& e = acc[g_recs[i].name];
+    e.first += 1;
+    e.second += ms;
+  }
+  std::string out = "{";
+  for (auto& kv : acc) {
+    char item[160];
+    std::snprintf(item, sizeof(item), "%s\"%s\": [%lld, %.6f]", out.size() > 1 ? ", " : "",
+                  kv.first.c_str(), kv.second.first, kv.second.second);
+    out += item;
+  }
+  out += "}";
+  g_used = 0;
+  if (buf && len) std::snprintf(buf, len, "%s", out.c_str());
+  return out.size() + 1 <= len ? GPA_B200_OK : GPA_B200_BAD_ARGUMENT;
+}
 
 }  // extern "C"

@@ -123,6 +123,17 @@ struct Blocks {
   __host__ __device__ int block_of(int t) const { return t < first ? 0 : 1 + (t - first) / C; }
 };
 
+// Kernel accounting: every launch in this library is bracketed by a Launch
+// scope.  It always counts launches; when profiling is on (off by default, so
+// graph capture sees no extra nodes) it records CUDA events on the launch
+// stream and accumulates per-kernel device time.
+struct Launch {
+  Launch(const char* name, cudaStream_t st);
+  ~Launch();
+  int slot;
+  cudaStream_t st;
+};
+
 inline Blocks make_blocks(int T, int C, int offset) {
   Blocks b;
   b.T = T;

@@ -597,6 +597,18 @@ __global__ void __launch_bounds__(256) gdn_bwd_chunk_k_kernel(ScanBatch b, int U
     }
   }
   __syncthreads();
+  if (d.dg64) {
+    if (threadIdx.x == 0) {
+      double sg = 0.0, sb = 0.0;
+      for (int t = 0; t < c; ++t) {
+        sg += dG[t];
+        sb += db[t];
+      }
+      atomicAdd(&d.dg64[(int64_t)u * d.dg_su], sg);
+      atomicAdd(&d.dbeta64[(int64_t)u * d.dg_su], sb);
+    }
+    return;
+  }
   for (int t = threadIdx.x; t < c; t += blockDim.x) {
     const int64_t gi = (int64_t)u * d.dg_su + (int64_t)(t0 + t) * d.dg_st;
     atomicAdd(&d.dg[gi], dG[t]);
@@ -630,11 +642,12 @@ size_t smem_bwd_chunk_v(int K, int) {
 size_t smem_bwd_chunk_k(int K, int) { return sizeof(float) * (3 * C * K + 3 * AS + 4 * C); }
 
 template <class Kern>
-cudaError_t launch(Kern k, dim3 grid, size_t smem, cudaStream_t st, const ScanBatch& b, int U,
-                   const Blocks& bl) {
+cudaError_t launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStream_t st,
+                   const ScanBatch& b, int U, const Blocks& bl) {
   if (grid.x == 0 || grid.y == 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  Launch scope(name, st);
   k<<<grid, 256, smem, st>>>(b, U, bl);
   return cudaGetLastError();
 }
@@ -648,10 +661,10 @@ cudaError_t gdn_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_o
   int K, V;
   max_kv(b, &K, &V);
   const int nvs = (V + VS - 1) / VS;
-  cudaError_t e = launch(gdn_fwd_chunk_kernel, dim3(U * bl.nb, b.n), smem_fwd_chunk(K, V), st, b,
+  cudaError_t e = launch("gdn_fwd_chunk", gdn_fwd_chunk_kernel, dim3(U * bl.nb, b.n), smem_fwd_chunk(K, V), st, b,
                          U, bl);
   if (e != cudaSuccess) return e;
-  e = launch(gdn_fwd_state_kernel, dim3(U * nvs, b.n), smem_fwd_state(K, V), st, b, U, bl);
+  e = launch("gdn_fwd_state", gdn_fwd_state_kernel, dim3(U * nvs, b.n), smem_fwd_state(K, V), st, b, U, bl);
   if (e != cudaSuccess || !with_output) return e;
   return gdn_output(b, U, bl, st);
 }
@@ -660,14 +673,14 @@ cudaError_t gdn_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t
   int K, V;
   max_kv(b, &K, &V);
   const int nvs = (V + VS - 1) / VS;
-  return launch(gdn_fwd_out_kernel, dim3(U * bl.nb * nvs, b.n), smem_fwd_out(K, V), st, b, U, bl);
+  return launch("gdn_fwd_out", gdn_fwd_out_kernel, dim3(U * bl.nb * nvs, b.n), smem_fwd_out(K, V), st, b, U, bl);
 }
 
 cudaError_t gdn_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
   int K, V;
   max_kv(b, &K, &V);
   const int nvs = (V + VS - 1) / VS;
-  return launch(gdn_bwd_local_kernel, dim3(U * bl.nb * nvs, b.n), smem_bwd_local(K, V), st, b, U,
+  return launch("gdn_bwd_local", gdn_bwd_local_kernel, dim3(U * bl.nb * nvs, b.n), smem_bwd_local(K, V), st, b, U,
                 bl);
 }
 
@@ -676,15 +689,15 @@ cudaError_t gdn_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaS
   max_kv(b, &K, &V);
   const int nvs = (V + VS - 1) / VS;
   // recompute U (into Ub scratch) and Wk
-  cudaError_t e = launch(gdn_fwd_chunk_kernel, dim3(U * bl.nb, b.n), smem_fwd_chunk(K, V), st, b,
+  cudaError_t e = launch("gdn_fwd_chunk", gdn_fwd_chunk_kernel, dim3(U * bl.nb, b.n), smem_fwd_chunk(K, V), st, b,
                          U, bl);
   if (e != cudaSuccess) return e;
-  e = launch(gdn_bwd_state_kernel, dim3(U * nvs, b.n), smem_bwd_state(K, V), st, b, U, bl);
+  e = launch("gdn_bwd_state", gdn_bwd_state_kernel, dim3(U * nvs, b.n), smem_bwd_state(K, V), st, b, U, bl);
   if (e != cudaSuccess) return e;
-  e = launch(gdn_bwd_chunk_v_kernel, dim3(U * bl.nb * nvs, b.n), smem_bwd_chunk_v(K, V), st, b, U,
+  e = launch("gdn_bwd_chunk_v", gdn_bwd_chunk_v_kernel, dim3(U * bl.nb * nvs, b.n), smem_bwd_chunk_v(K, V), st, b, U,
              bl);
   if (e != cudaSuccess) return e;
-  return launch(gdn_bwd_chunk_k_kernel, dim3(U * bl.nb, b.n), smem_bwd_chunk_k(K, V), st, b, U,
+  return launch("gdn_bwd_chunk_k", gdn_bwd_chunk_k_kernel, dim3(U * bl.nb, b.n), smem_bwd_chunk_k(K, V), st, b, U,
                 bl);
 }
 

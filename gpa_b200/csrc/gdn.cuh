@@ -58,6 +58,8 @@ struct ScanDesc {
   float* dg;              // += at dg[u*dg_su + t*dg_st]
   float* dbeta;           // += with dg's indexing
   int64_t dg_su, dg_st;
+  double* dg64;           // if set: dg / dbeta are summed over t into dg64 / dbeta64 [u*dg_su]
+  double* dbeta64;
   float* dS0;             // [U,K,V] gradient of the initial state (written)
   float* sc_dW;           // [U,T,V] scratch
   float* sc_dK;           // [U,T,K] scratch (zeroed by the caller)

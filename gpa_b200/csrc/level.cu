@@ -490,7 +490,7 @@ __global__ void k_scales(int U, int H, int L, const float* output_logits, float*
 
 // one warp per (u, t): fp32 unit-major dout; per-unit sum of dout . y_j
 __global__ void k_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt, YPtrs yp,
-                          float* dout_f, float* scal) {
+                          float* dout_f, double* scal) {
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int U = B * H;
   if (w >= U * T) return;
@@ -505,7 +505,7 @@ __global__ void k_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, 
   }
   for (int j = 0; j < L; ++j) {
     const float s = warp_sum(acc[j]);
-    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_OutW], s);
+    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_OutW], (double)s);
   }
 }
 
@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(256) k_bridge_bwd(
     const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
     const float* logits, const float* r_in, const float* hp, const float* mlp, const float* qoh,
     const float* qon, const float* dqoh, float* dqo_out, float* droute_out, float* dhp_out,
-    float* dlogits, float* dq_direct, float* scal, float* scalE, int E) {
+    float* dlogits, float* dq_direct, double* scal, double* scalE, int E) {
   const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
   const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * kRowsPerTile;
   const int c = min(kRowsPerTile, T - t0), h = u % H;
@@ -559,7 +559,7 @@ __global__ void __launch_bounds__(256) k_bridge_bwd(
       part += R[i] * mlp[row(u, T, t0 + t) * M + m];
     }
     const float s = block_sum(part, red);
-    if (threadIdx.x == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_MlpGain], s);
+    if (threadIdx.x == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_MlpGain], (double)s);
   }
   const float mg = route_mlp_gain[j * H + h];
   const float* Uh = route_up + (int64_t)h * M * 2 * M;
@@ -646,9 +646,9 @@ __global__ void __launch_bounds__(256) k_bridge_bwd(
     }
   }
   if (lane == 0 && in.n > 0) {
-    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], rg_acc);
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], (double)rg_acc);
     for (int a = 0; a < in.n; ++a)
-      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], ew_acc[a]);
+      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], (double)ew_acc[a]);
   }
 }
 
@@ -658,7 +658,7 @@ __global__ void k_logits_bwd(int U, Blocks bl, int H, int M, int L, int j, float
                              const float* counts, const float* lh, const float* ln,
                              const float* wh, const float* wn, const float* dlh, const float* dwh,
                              const float* dlogits, float* dwrite, float* draw, float* dn,
-                             float* dnsum, float* scal) {
+                             float* dnsum, double* scal) {
   const int T = bl.T;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (w >= U * T) return;
@@ -691,7 +691,7 @@ __global__ void k_logits_bwd(int U, Blocks bl, int H, int M, int L, int j, float
   for (int i = 0; i < kMaxPerLane; ++i)
     if (lane + 32 * i < M) atomicAdd(&dnsum[((int64_t)u * bl.nb + n) * M + lane + 32 * i], d2[i]);
   cg = warp_sum(cg);
-  if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], cg);
+  if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], (double)cg);
   load_vec(y, wh + o, M);
   load_vec(dy, dwh + o, M);
   unit_bwd(d1, y, dy, wn[w], M);
@@ -724,7 +724,7 @@ __global__ void __launch_bounds__(256) k_post_bwd(
     int with_residual, const float* nk, const float* write, const float* Abnd, const float* Bbnd,
     const float* fzA, const float* fzB, const float* residual_raw, const float* dkey,
     const float* dval, float* dwrite, float* dnk, float* extA, float* extB, float* dfzA,
-    float* dfzB, float* scal) {
+    float* dfzB, double* scal) {
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
   const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -773,8 +773,8 @@ __global__ void __launch_bounds__(256) k_post_bwd(
   }
   __syncthreads();
   if (with_residual && threadIdx.x == 0) {
-    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaK], -red[32]);
-    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaV], -red[33]);
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaK], -(double)red[32]);
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaV], -(double)red[33]);
   }
   // dlw = softmax backward (in place in dW)
   for (int t = warp; t < c; t += nw) {
@@ -957,14 +957,14 @@ __global__ void k_fold(FoldArgs a) {
   if (h >= a.H) return;
   const int H = a.H, L = a.L, E = a.E;
   auto S = [&](int j, int slot) {
-    float s = 0.f;
+    double s = 0.0;
     for (int b = 0; b < a.B; ++b) s += a.scal[((int64_t)(b * H + h) * L + j) * kNScal + slot];
-    return s;
+    return (float)s;
   };
   auto SE = [&](int e, int slot) {
-    float s = 0.f;
+    double s = 0.0;
     for (int b = 0; b < a.B; ++b) s += a.scalE[((int64_t)(b * H + h) * E + e) * kNEdge + slot];
-    return s;
+    return (float)s;
   };
   float ow[kMaxLevels], dow[kMaxLevels];
   float mx = -INFINITY, ssum = 0.f;
@@ -1019,10 +1019,12 @@ __global__ void k_fold(FoldArgs a) {
 int blocks_for(int64_t n, int per) { return (int)((n + per - 1) / per); }
 
 template <class Kern, class... Args>
-cudaError_t launch_smem(Kern k, int grid, size_t smem, cudaStream_t st, Args... args) {
+cudaError_t launch_smem(const char* name, Kern k, int grid, size_t smem, cudaStream_t st,
+                        Args... args) {
   if (grid <= 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  Launch scope(name, st);
   k<<<grid, 256, smem, st>>>(args...);
   return cudaGetLastError();
 }
@@ -1034,6 +1036,7 @@ cudaError_t launch_input(const void* q, const void* k, const void* v, int dt, in
                          cudaStream_t st) {
   const int rows = B * T * H;
   if (!rows) return cudaSuccess;
+  Launch scope_("input", st);
   k_input<<<blocks_for(rows, 8), 256, 0, st>>>(q, k, v, dt, B, T, H, D, Dv, qf, qh, qn, key0,
                                                 val0);
   return cudaGetLastError();
@@ -1045,7 +1048,7 @@ cudaError_t launch_level_prep(int U, int T, int H, int D, int M, const float* ke
                               float* gates, cudaStream_t st) {
   const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
   const size_t smem = sizeof(float) * kRowsPerTile * (D + M);
-  return launch_smem(k_level_prep, U * ntile, smem, st, U, T, H, D, M, key, C, Wg, gbias,
+  return launch_smem("level_prep", k_level_prep, U * ntile, smem, st, U, T, H, D, M, key, C, Wg, gbias,
                      beta_max, pos_none, nk, kn, slot, ns, sn, raw4, gates);
 }
 
@@ -1055,7 +1058,7 @@ cudaError_t launch_level_post(int U, const Blocks& bl, int post, int H, int D, i
                               const float* fzB, const float* residual_raw, int j, float* write,
                               float* bsum, float* key_next, float* val_next, cudaStream_t st) {
   const size_t smem = sizeof(float) * (D * M + M * Dv + kRowsPerTile * M);
-  return launch_smem(k_level_post, U * bl.nb, smem, st, U, bl, post, H, D, Dv, M, with_residual,
+  return launch_smem("level_post", k_level_post, U * bl.nb, smem, st, U, bl, post, H, D, Dv, M, with_residual,
                      nk, key, val, Abnd, Bbnd, fzA, fzB, residual_raw, j, write, bsum, key_next,
                      val_next);
 }
@@ -1066,6 +1069,7 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
                           float* lh, float* ln, float* wh, float* wn, float* n_final,
                           cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
+  Launch scope_("counts", st);
   k_counts<<<U * bl.nb, 256, 0, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write,
                                       raw, counts, logits, lh, ln, wh, wn, n_final);
   return cudaGetLastError();
@@ -1074,6 +1078,7 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
 cudaError_t launch_rel_gates(int U, int H, int E, int pos_none, const float* decay_raw,
                              const float* beta_raw, float* ge, float* be, cudaStream_t st) {
   if (!E || !U) return cudaSuccess;
+  Launch scope_("rel_gates", st);
   k_rel_gates<<<blocks_for((int64_t)E * U, 256), 256, 0, st>>>(U, H, E, pos_none, decay_raw,
                                                                 beta_raw, ge, be);
   return cudaGetLastError();
@@ -1087,7 +1092,7 @@ cudaError_t launch_bridge(int U, int T, int H, int D, int M, int L, int j, const
                           float* mlp, float* route, float* qoh, float* qon, cudaStream_t st) {
   const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
   const size_t smem = sizeof(float) * kRowsPerTile * 4 * M;
-  return launch_smem(k_bridge, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
+  return launch_smem("bridge", k_bridge, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
                      relation_gain, route_up, route_down, route_mlp_gain, Wrs, Wqs, qs, logits, qf,
                      r, hp, mlp, route, qoh, qon);
 }
@@ -1098,12 +1103,14 @@ cudaError_t launch_mix(int B, int T, int H, int Dv, int L, const float* output_l
   if (!rows) return cudaSuccess;
   YPtrs yp;
   for (int j = 0; j < L; ++j) yp.y[j] = y[j];
+  Launch scope_("mix", st);
   k_mix<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, Dv, L, output_logits, yp, out, dt);
   return cudaGetLastError();
 }
 
 cudaError_t launch_copy(float* dst, const float* src, int64_t n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
+  Launch scope_("copy", st);
   k_copy<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, n);
   return cudaGetLastError();
 }
@@ -1112,12 +1119,14 @@ cudaError_t launch_to_bthx(const float* src, void* dst, int dt, int B, int T, in
                            cudaStream_t st) {
   const int64_t n = (int64_t)B * T * H * X;
   if (n <= 0) return cudaSuccess;
+  Launch scope_("to_bthx", st);
   k_to_bthx<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, dt, B, T, H, X);
   return cudaGetLastError();
 }
 
 cudaError_t launch_add(float* dst, const float* src, int64_t n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
+  Launch scope_("add", st);
   k_add<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, n);
   return cudaGetLastError();
 }
@@ -1126,6 +1135,7 @@ cudaError_t launch_gather_boundary(float* dst, const float* src, int U, int nb1,
                                    int64_t sz, cudaStream_t st) {
   const int64_t n = (int64_t)U * sz;
   if (n <= 0) return cudaSuccess;
+  Launch scope_("boundary", st);
   k_boundary<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, U, nb1, idx, sz, 0);
   return cudaGetLastError();
 }
@@ -1134,22 +1144,25 @@ cudaError_t launch_scatter_add_boundary(float* dst, const float* src, int U, int
                                         int64_t sz, cudaStream_t st) {
   const int64_t n = (int64_t)U * sz;
   if (n <= 0) return cudaSuccess;
+  Launch scope_("boundary", st);
   k_boundary<<<blocks_for(n, 256), 256, 0, st>>>(dst, src, U, nb1, idx, sz, 1);
   return cudaGetLastError();
 }
 
 cudaError_t launch_scales(int U, int H, int L, const float* output_logits, float* ow_scale,
                           cudaStream_t st) {
+  Launch scope_("scales", st);
   k_scales<<<blocks_for(U, 128), 128, 0, st>>>(U, H, L, output_logits, ow_scale);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt,
-                           const float* const* y, float* dout_f, float* scal, cudaStream_t st) {
+                           const float* const* y, float* dout_f, double* scal, cudaStream_t st) {
   const int rows = B * T * H;
   if (!rows) return cudaSuccess;
   YPtrs yp;
   for (int j = 0; j < L; ++j) yp.y[j] = y[j];
+  Launch scope_("mix_bwd", st);
   k_mix_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, Dv, L, dout, dt, yp, dout_f, scal);
   return cudaGetLastError();
 }
@@ -1161,11 +1174,11 @@ cudaError_t launch_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, c
                               float qs, const float* logits, const float* r, const float* hp,
                               const float* mlp, const float* qoh, const float* qon,
                               const float* dqoh, float* dqo, float* droute, float* dhp,
-                              float* dlogits, float* dq_direct, float* scal, float* scalE, int E,
-                              cudaStream_t st) {
+                              float* dlogits, float* dq_direct, double* scal, double* scalE,
+                              int E, cudaStream_t st) {
   const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
   const size_t smem = sizeof(float) * (kRowsPerTile * 4 * M + 32 + kMaxIn);
-  return launch_smem(k_bridge_bwd, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
+  return launch_smem("bridge_bwd", k_bridge_bwd, U * ntile, smem, st, U, T, H, D, M, L, j, in, edge_logits,
                      relation_gain, route_up, route_down, route_mlp_gain, Wrs, Wqs, qs, logits, r,
                      hp, mlp, qoh, qon, dqoh, dqo, droute, dhp, dlogits, dq_direct, scal, scalE,
                      E);
@@ -1176,9 +1189,10 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, float* scal, cudaStream_t st) {
+                              float* dn, float* dnsum, double* scal, cudaStream_t st) {
   const int rows = U * bl.T;
   if (!rows) return cudaSuccess;
+  Launch scope_("logits_bwd", st);
   k_logits_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
@@ -1189,6 +1203,7 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
 cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, const float* dnsum,
                               const float* dn_final, float* dwrite, float* dn0, cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
+  Launch scope_("counts_bwd", st);
   k_counts_bwd<<<U * bl.nb, 256, 0, st>>>(U, bl, M, dn, dnsum, dn_final, dwrite, dn0);
   return cudaGetLastError();
 }
@@ -1198,10 +1213,10 @@ cudaError_t launch_post_bwd(int U, const Blocks& bl, int post, int offset, int H
                             const float* write, const float* Abnd, const float* Bbnd,
                             const float* fzA, const float* fzB, const float* residual_raw,
                             const float* dkey, const float* dval, float* dwrite, float* dnk,
-                            float* extA, float* extB, float* dfzA, float* dfzB, float* scal,
+                            float* extA, float* extB, float* dfzA, float* dfzB, double* scal,
                             cudaStream_t st) {
   const size_t smem = sizeof(float) * (D * M + M * Dv + 2 * kRowsPerTile * M + 34);
-  return launch_smem(k_post_bwd, U * bl.nb, smem, st, U, bl, post, offset, H, D, Dv, M, L, j,
+  return launch_smem("post_bwd", k_post_bwd, U * bl.nb, smem, st, U, bl, post, offset, H, D, Dv, M, L, j,
                      with_residual, nk, write, Abnd, Bbnd, fzA, fzB, residual_raw, dkey, dval,
                      dwrite, dnk, extA, extB, dfzA, dfzB, scal);
 }
@@ -1213,7 +1228,7 @@ cudaError_t launch_prep_bwd(int U, int T, int H, int D, int M, const float* C, c
                             float* dkey, cudaStream_t st) {
   const int ntile = (T + kRowsPerTile - 1) / kRowsPerTile;
   const size_t smem = sizeof(float) * kRowsPerTile * M;
-  return launch_smem(k_prep_bwd, U * ntile, smem, st, U, T, H, D, M, C, Wg, beta_max, pos_none,
+  return launch_smem("prep_bwd", k_prep_bwd, U * ntile, smem, st, U, T, H, D, M, C, Wg, beta_max, pos_none,
                      raw4, nk, kn, ns, sn, dgates, dnk, dns, dslot, d4, dkey);
 }
 
@@ -1224,6 +1239,7 @@ cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xm
   if (!total) return cudaSuccess;
   const int tp = (P + kHoTile - 1) / kHoTile, tq = (Q + kHoTile - 1) / kHoTile;
   dim3 grid(H, tp * tq, (unsigned)((total + kHoSplit - 1) / kHoSplit));
+  Launch scope_("head_outer", st);
   k_head_outer<<<grid, 256, 0, st>>>(B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale,
                                      out);
   return cudaGetLastError();
@@ -1235,12 +1251,14 @@ cudaError_t launch_input_bwd(int B, int T, int H, int D, int Dv, int dt, const f
                              cudaStream_t st) {
   const int rows = B * T * H;
   if (!rows) return cudaSuccess;
+  Launch scope_("input_bwd", st);
   k_input_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, D, Dv, dt, qh, qn, dqh, dq_direct,
                                                     dkey, dval, dq, dk, dv);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fold(const FoldArgs& a, cudaStream_t st) {
+  Launch scope_("fold", st);
   k_fold<<<blocks_for(a.H, 64), 64, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -65,7 +65,7 @@ cudaError_t launch_scatter_add_boundary(float* dst, const float* src, int U, int
 cudaError_t launch_scales(int U, int H, int L, const float* output_logits, float* ow_scale,
                           cudaStream_t st);
 cudaError_t launch_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt,
-                           const float* const* y, float* dout_f, float* scal, cudaStream_t st);
+                           const float* const* y, float* dout_f, double* scal, cudaStream_t st);
 cudaError_t launch_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
                               const float* edge_logits, const float* relation_gain,
                               const float* route_up, const float* route_down,
@@ -73,14 +73,14 @@ cudaError_t launch_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, c
                               float qs, const float* logits, const float* r, const float* hp,
                               const float* mlp, const float* qoh, const float* qon,
                               const float* dqoh, float* dqo, float* droute, float* dhp,
-                              float* dlogits, float* dq_direct, float* scal, float* scalE, int E,
+                              float* dlogits, float* dq_direct, double* scal, double* scalE, int E,
                               cudaStream_t st);
 cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int j,
                               float read_scale, const float* count_gain_raw, const float* logits,
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, float* scal, cudaStream_t st);
+                              float* dn, float* dnsum, double* scal, cudaStream_t st);
 cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, const float* dnsum,
                               const float* dn_final, float* dwrite, float* dn0, cudaStream_t st);
 cudaError_t launch_post_bwd(int U, const Blocks& bl, int post, int offset, int H, int D, int Dv,
@@ -88,7 +88,7 @@ cudaError_t launch_post_bwd(int U, const Blocks& bl, int post, int offset, int H
                             const float* write, const float* Abnd, const float* Bbnd,
                             const float* fzA, const float* fzB, const float* residual_raw,
                             const float* dkey, const float* dval, float* dwrite, float* dnk,
-                            float* extA, float* extB, float* dfzA, float* dfzB, float* scal,
+                            float* extA, float* extB, float* dfzA, float* dfzB, double* scal,
                             cudaStream_t st);
 cudaError_t launch_prep_bwd(int U, int T, int H, int D, int M, const float* C, const float* Wg,
                             float beta_max, int pos_none, const float* raw4, const float* nk,
@@ -110,7 +110,7 @@ struct FoldArgs {
   int edge_src[kMaxEdges], edge_dst[kMaxEdges];
   const float *residual_raw, *count_gain_raw, *output_logits, *edge_logits, *relation_decay_raw,
       *relation_beta_raw;
-  const float *scal, *scalE;
+  const double *scal, *scalE;
   float *g_residual_raw, *g_count_gain_raw, *g_route_mlp_gain, *g_relation_gain,
       *g_output_logits, *g_edge_logits, *g_relation_decay_raw, *g_relation_beta_raw;
 };

@@ -131,6 +131,15 @@ int gpa_b200_last_error(char* buf, size_t len);
 /* ABI version of this header. */
 int gpa_b200_abi_version(void);
 
+/* Kernel accounting (no counterpart in the reference, which has no native
+ * code): the number of kernels this library has launched in this process, and
+ * optional per-kernel device timing with CUDA events on the launch streams.
+ * Profiling is off by default; profile_stop synchronises on the recorded
+ * events and writes {"kernel": [launches, total_ms], ...} as JSON into buf. */
+long long gpa_b200_launch_count(void);
+int gpa_b200_profile_start(void);
+int gpa_b200_profile_stop(char* buf, size_t len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,6 +14,13 @@ from gpa_b200.state import tensors
 
 
 def rel(a, b) -> float:
+    """Relative L2 error of a against b; a gradient of None counts as zeros."""
+    if a is None and b is None:
+        return 0.0
+    if a is None:
+        a = torch.zeros_like(b)
+    if b is None:
+        b = torch.zeros_like(a)
     a = a.detach().double().cpu().reshape(-1)
     b = b.detach().double().cpu().reshape(-1)
     nb = b.norm()
