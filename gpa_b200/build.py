@@ -15,7 +15,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ("api.cu", "gdn.cu", "level.cu")
+SOURCES = ("api.cu", "gdn.cu", "gdn_tc.cu", "level.cu")
 OUTPUT = os.path.join(HERE, "libgpa_b200.so")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
@@ -28,7 +28,7 @@ def nvcc_path() -> str:
 
 
 def build(debug: bool = False, verbose: bool = False, extra=()) -> str:
-    cmd = [nvcc_path(), "-std=c++17", "-O3", "-lineinfo", ARCH, "-Xcompiler", "-fPIC", "-shared",
+    cmd = [nvcc_path(), "-std=c++20", "-O3", "-lineinfo", ARCH, "-Xcompiler", "-fPIC", "-shared",
            "-o", OUTPUT, *(os.path.join(CSRC, s) for s in SOURCES), *extra]
     if debug:
         cmd.append("-DGPA_DEBUG=1")

@@ -71,6 +71,7 @@ struct Geo {
   float rs, qs, bm;
   Blocks bl;
   int Mmax;
+  int fast;  // tensor-core GDN kernels (bf16 / fp16 inputs, widths multiples of 16)
 };
 
 int make_geo(const GpaDims* d, Geo* g, std::string* why) {
@@ -138,6 +139,8 @@ int make_geo(const GpaDims* d, Geo* g, std::string* why) {
       }
   g->U = g->B * g->H;
   g->post = g->C == 1;
+  g->fast = g->dt != GPA_B200_F32 && tc_supported(g->D, g->Dv);
+  for (int j = 0; j < g->L; ++j) g->fast = g->fast && tc_supported(g->M[j], g->M[j]);
   g->bl = make_blocks(g->T, g->C, g->offset);
   return GPA_B200_OK;
 }
@@ -218,7 +221,8 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
   s->ge = b.take((size_t)g.E * g.U);
   s->be = b.take((size_t)g.E * g.U);
   const int kw = g.D > g.Mmax ? g.D : g.Mmax;
-  for (int i = 0; i < kMaxScans; ++i) s->wk[i] = b.take(UT * kw);
+  const int nwk = g.L - 1 > 2 ? g.L - 1 : 2;  // widest scan batch: a relation group or a level pair
+  for (int i = 0; i < kMaxScans; ++i) s->wk[i] = i < nwk ? b.take(UT * kw) : nullptr;
   s->bytes = b.off + 256;
 }
 
@@ -355,6 +359,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
                          p->gate_bias[j], g.bm, g.pos_none, s.nk[j], s.kn[j], s.slot[j], s.ns[j],
                          s.sn[j], s.raw4[j], s.gates[j], st));
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = 2;
     ScanDesc& in = sb.s[0];
     ScanDesc& ou = sb.s[1];
@@ -405,6 +410,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
                       s.be, st));
   for (int tj = 0; tj < g.L; ++tj) {
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = 0;
     for (int e = 0; e < g.E; ++e) {
       if (g.ed[e] != tj) continue;
@@ -448,6 +454,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
   }
   {
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = g.L;
     for (int j = 0; j < g.L; ++j) {
       ScanDesc& d = sb.s[j];
@@ -550,6 +557,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
   };
   {
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = L;
     for (int j = 0; j < L; ++j) {
       sb.s[j] = outer_desc(j);
@@ -585,6 +593,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
   // relation scans, grouped by target level
   for (int tj = 0; tj < L; ++tj) {
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = 0;
     for (int e = 0; e < E; ++e) {
       if (g.ed[e] != tj) continue;
@@ -677,6 +686,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     CK(zero(x.dK[0], UT * D, st));
     CK(zero(x.dG[0], UT, st));
     ScanBatch sb;
+    sb.tc = g.fast;
     sb.n = 1;
     ScanDesc& in = sb.s[0];
     in = blank_scan();

@@ -72,6 +72,7 @@ struct ScanDesc {
 
 struct ScanBatch {
   int n;
+  int tc;  // 1: tensor-core kernels (bf16 operands); 0: SIMT fp32 kernels
   ScanDesc s[kMaxScans];
 };
 
@@ -82,5 +83,13 @@ cudaError_t gdn_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t
 cudaError_t gdn_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 cudaError_t gdn_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 int gdn_max_smem_bytes();
+
+// tensor-core variants (gdn_tc.cu); widths must be multiples of 16 and <= 128
+bool tc_supported(int K, int V);
+cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
+                       cudaStream_t st);
+cudaError_t tc_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 
 }  // namespace gpa

@@ -1,0 +1,1035 @@
+// Tensor-core GDN scan kernels (bf16 operands, fp32 accumulation and fp32 state).
+//
+// Same chunk algebra and phase split as the SIMT kernels in gdn.cu (see
+// gdn.cuh), with three differences that the tensor cores make worthwhile:
+//   * T = (I + A)^-1 of a block is formed explicitly (16x16 diagonal blocks by
+//     warp forward substitution, off-diagonal blocks by block substitution) so
+//     that U, Wk, T^T dW, T^T dWk become tile GEMMs;
+//   * one CTA covers the full value width of a block (no value slices), so
+//     every per-token gradient is written by exactly one CTA: no atomics;
+//   * operands are bf16 tiles in shared memory fed to mma.sync m16n8k16 with
+//     fp32 accumulators; states S and dS stay fp32 and are rounded to bf16
+//     only as GEMM operands.
+// Used when the input dtype is bf16 / fp16 and every width is a multiple of 16.
+#include "gdn.cuh"
+#include "gdn_dev.cuh"
+#include "mma.cuh"
+
+namespace gpa {
+namespace {
+
+using tc::Acc;
+using tc::bf16;
+using tc::for_tiles;
+using tc::mma_acc;
+using tc::quad_sum;
+
+constexpr int C = kMaxChunk;     // 64 rows per block tile (zero padded)
+constexpr int LDT = C + 8;       // bf16 row stride of 64-wide tiles
+
+__host__ __device__ __forceinline__ int ld16(int x) { return x + 8; }  // padded bf16 row stride
+
+// Shared-memory carve-up identical on host (sizing) and device (pointers).
+struct Carve {
+  size_t off = 0;
+  __host__ __device__ size_t take(size_t bytes) {
+    off = (off + 15) & ~size_t(15);
+    const size_t r = off;
+    off += bytes;
+    return r;
+  }
+};
+
+// block gates with padding: rows >= c keep G = G[c-1] and beta = 0
+GPA_DEV void load_gates_pad(const ScanDesc& d, int u, int t0, int c, float* G, float* bt) {
+  load_gates(d, u, t0, c, G, bt);
+  __syncthreads();
+  for (int t = c + threadIdx.x; t < C; t += blockDim.x) {
+    G[t] = G[c - 1];
+    if (bt) bt[t] = 0.f;
+  }
+}
+
+// fp32 rows [rows x cols] (row stride src_ld) -> bf16 tile [rows_pad x ld]; zero padding.
+// cols and src_ld are multiples of 4 and src is 16-byte aligned: float4 loads, 4 in flight
+// per thread.  With `lo`, the tile is stored as a hi/lo pair.
+constexpr int kLoadIlp = 4;
+
+GPA_DEV void put4(bf16* hi, bf16* lo, int o, float4 v) {
+  __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+  *reinterpret_cast<__nv_bfloat162*>(hi + o) = h01;
+  *reinterpret_cast<__nv_bfloat162*>(hi + o + 2) = h23;
+  if (lo) {
+    const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+    *reinterpret_cast<__nv_bfloat162*>(lo + o) = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+    *reinterpret_cast<__nv_bfloat162*>(lo + o + 2) = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+  }
+}
+
+GPA_DEV void tile_load(bf16* hi, bf16* lo, int ld, const float* src, int src_ld, int rows,
+                       int cols, int rows_pad, float scale) {
+  const int c4 = cols >> 2, n4 = rows_pad * c4;
+  for (int base = threadIdx.x; base < n4; base += blockDim.x * kLoadIlp) {
+    float4 v[kLoadIlp];
+#pragma unroll
+    for (int j = 0; j < kLoadIlp; ++j) {
+      const int i = base + j * blockDim.x;
+      const int r = i / c4, cc = (i - r * c4) << 2;
+      v[j] = (i < n4 && r < rows) ? *reinterpret_cast<const float4*>(src + (int64_t)r * src_ld + cc)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kLoadIlp; ++j) {
+      const int i = base + j * blockDim.x;
+      if (i >= n4) break;
+      const int r = i / c4, cc = (i - r * c4) << 2;
+      float4 x = v[j];
+      x.x *= scale;
+      x.y *= scale;
+      x.z *= scale;
+      x.w *= scale;
+      put4(hi, lo, r * ld + cc, x);
+    }
+  }
+}
+
+GPA_DEV void tile_to_bf16(bf16* dst, int ld, const float* src, int src_ld, int rows, int cols,
+                          int rows_pad, float scale = 1.f) {
+  tile_load(dst, nullptr, ld, src, src_ld, rows, cols, rows_pad, scale);
+}
+
+GPA_DEV void tile_split(bf16* hi, bf16* lo, int ld, const float* src, int src_ld, int rows,
+                        int cols, int rows_pad, float scale = 1.f) {
+  tile_load(hi, lo, ld, src, src_ld, rows, cols, rows_pad, scale);
+}
+
+// dst[i] = src[i] for n floats (n multiple of 4, 16-byte aligned), float4 copies
+GPA_DEV void copy_f4(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+    *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(src + i);
+}
+
+// T = (I + A)^-1 for a strictly lower 64x64 A (row stride kAStride).  Xs: 768 floats.
+GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < C * kAStride; i += blockDim.x) Tm[i] = 0.f;
+  __syncthreads();
+  if (w < 4 && lane < 16) {
+    const int b0 = 16 * w, j = lane;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float s = (r == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int q = 0; q < r; ++q) s -= A[(b0 + r) * kAStride + b0 + q] * x[q];
+      x[r] = s;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Tm[(b0 + r) * kAStride + b0 + j] = x[r];
+  }
+  __syncthreads();
+  for (int dd = 1; dd < 4; ++dd) {
+    const int nblk = 4 - dd;
+    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
+      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
+      float s = 0.f;
+      for (int kb = jb; kb < ib; ++kb)
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          s += A[(16 * ib + r) * kAStride + 16 * kb + q] * Tm[(16 * kb + q) * kAStride + 16 * jb + cc];
+      Xs[e] = s;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
+      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        s += Tm[(16 * ib + r) * kAStride + 16 * ib + q] * Xs[(jb << 8) + (q << 4) + cc];
+      Tm[(16 * ib + r) * kAStride + 16 * jb + cc] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+// A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
+GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
+                        const float* bt, float* A, float* Atil) {
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.zero();
+    tc::mma_acc3<1, 2, false, true>(acc, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int s, float& v) {
+      const float at = s < t ? __expf(G[t] - G[s]) * v : 0.f;
+      A[t * kAStride + s] = bt[t] * at;
+      if (Atil) Atil[t * kAStride + s] = at;
+    });
+  });
+}
+
+template <int MI, int NI, class Body>
+GPA_DEV void tiles_n(int M, int N, Body body) {
+  // NI chosen at run time: 32-wide tiles when N allows, else 16-wide
+  if (N % 32 == 0) for_tiles<MI, 2>(M, N, [&](int m0, int n0) { body.template operator()<2>(m0, n0); });
+  else for_tiles<MI, 1>(M, N, [&](int m0, int n0) { body.template operator()<1>(m0, n0); });
+}
+
+// ------------------------------------------------------------------ forward
+
+struct LFwdChunk {
+  size_t Ks, Kl, Vs, A, Tm, Xs, Tbh, Tbl, Tgh, Tgl, G, bt, total;
+  __host__ __device__ LFwdChunk(int K, int V) {
+    Carve c;
+    Ks = c.take(2 * C * ld16(K));
+    Kl = c.take(2 * C * ld16(K));
+    Vs = c.take(2 * C * ld16(V));
+    A = c.take(4 * C * kAStride);
+    Tm = c.take(4 * C * kAStride);
+    Xs = c.take(4 * 768);
+    Tbh = c.take(2 * C * LDT);
+    Tbl = c.take(2 * C * LDT);
+    Tgh = c.take(2 * C * LDT);
+    Tgl = c.take(2 * C * LDT);
+    G = c.take(4 * C);
+    bt = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U*NB, nscan): U = T diag(b) V and Wk = T diag(b e^G) K of every block.
+__global__ void __launch_bounds__(256) tc_fwd_chunk(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LFwdChunk L(K, V);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Kl = (bf16*)(smem + L.Kl);
+  bf16* Vs = (bf16*)(smem + L.Vs);
+  float* A = (float*)(smem + L.A);
+  float* Tm = (float*)(smem + L.Tm);
+  float* Xs = (float*)(smem + L.Xs);
+  bf16* Tbh = (bf16*)(smem + L.Tbh);
+  bf16* Tbl = (bf16*)(smem + L.Tbl);
+  bf16* Tgh = (bf16*)(smem + L.Tgh);
+  bf16* Tgl = (bf16*)(smem + L.Tgl);
+  float* G = (float*)(smem + L.G);
+  float* bt = (float*)(smem + L.bt);
+  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Vs, ldv, d.v + row(u, T, t0) * V, V, c, V, C);
+  load_gates_pad(d, u, t0, c, G, bt);
+  __syncthreads();
+  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
+  __syncthreads();
+  invert_unit_lower(A, Tm, Xs);
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    const float x = Tm[t * kAStride + s] * bt[s];
+    tc::split_bf16(x, Tbh + t * LDT + s, Tbl + t * LDT + s);
+    tc::split_bf16(x * __expf(G[s]), Tgh + t * LDT + s, Tgl + t * LDT + s);
+  }
+  __syncthreads();
+  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, false>(acc, Tbh, Tbl, LDT, Vs, nullptr, ldv, m0, n0, C);
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) d.Ub[row(u, T, t0 + t) * V + col] = v;
+    });
+  });
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, false>(acc, Tgh, Tgl, LDT, Ks, Kl, ldk, m0, n0, C);
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) d.Wk[row(u, T, t0 + t) * K + col] = v;
+    });
+  });
+}
+
+struct LFwdState {
+  size_t Sf, Sb, Wkh, Wkl, Ks, Kl, Wch, Wcl, G, lam, total;
+  __host__ __device__ LFwdState(int K, int V) {
+    Carve c;
+    Sf = c.take(4 * K * V);
+    Sb = c.take(2 * K * ld16(V));
+    Wkh = c.take(2 * C * ld16(K));
+    Wkl = c.take(2 * C * ld16(K));
+    Ks = c.take(2 * C * ld16(K));
+    Kl = c.take(2 * C * ld16(K));
+    Wch = c.take(2 * C * ld16(V));
+    Wcl = c.take(2 * C * ld16(V));
+    G = c.take(4 * C);
+    lam = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U, nscan): sequential over blocks, full state [K x V] fp32 in shared memory.
+__global__ void __launch_bounds__(256) tc_fwd_state(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  const int64_t KV = (int64_t)K * V;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LFwdState L(K, V);
+  float* Sf = (float*)(smem + L.Sf);
+  bf16* Sb = (bf16*)(smem + L.Sb);
+  bf16* Wkh = (bf16*)(smem + L.Wkh);
+  bf16* Wkl = (bf16*)(smem + L.Wkl);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Kl = (bf16*)(smem + L.Kl);
+  bf16* Wch = (bf16*)(smem + L.Wch);
+  bf16* Wcl = (bf16*)(smem + L.Wcl);
+  float* G = (float*)(smem + L.G);
+  float* lam = (float*)(smem + L.lam);
+  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
+    const float x = d.S0[u * KV + i];
+    Sf[i] = x;
+    Sb[(i / V) * ldv + (i % V)] = __float2bfloat16(x);
+  }
+  __syncthreads();
+  for (int n = 0; n < bl.nb; ++n) {
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    copy_f4(d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, Sf, K * V);
+    tile_split(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C);
+    tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+    load_gates_pad(d, u, t0, c, G, nullptr);
+    __syncthreads();
+    for (int t = threadIdx.x; t < C; t += blockDim.x) lam[t] = __expf(G[c - 1] - G[t]);
+    __syncthreads();
+    // W = U - Wk S
+    tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      tc::mma_acc3<1, NI, false, false>(acc, Wkh, Wkl, ldk, Sb, nullptr, ldv, m0, n0, K);
+      acc.each(m0, n0, [&](int t, int col, float& v) {
+        float w = 0.f;
+        if (t < c) {
+          const int64_t o = row(u, T, t0 + t) * V + col;
+          w = d.Ub[o] - v;
+          d.W[o] = w;
+        }
+        tc::split_bf16(w * lam[t], Wch + t * ldv + col, Wcl + t * ldv + col);
+      });
+    });
+    __syncthreads();
+    const float gc = __expf(G[c - 1]);
+    // S = e^{G_c} S + K^T diag(lambda) W
+    tiles_n<1, 2>(K, V, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.each(m0, n0, [&](int k, int col, float& v) { v = gc * Sf[k * V + col]; });
+      tc::mma_acc3<1, NI, true, false>(acc, Ks, Kl, ldk, Wch, Wcl, ldv, m0, n0, C);
+      acc.each(m0, n0, [&](int k, int col, float& v) {
+        Sf[k * V + col] = v;
+        Sb[k * ldv + col] = __float2bfloat16(v);
+      });
+    });
+    __syncthreads();
+  }
+  copy_f4(d.Sb + ((int64_t)u * (bl.nb + 1) + bl.nb) * KV, Sf, K * V);
+  if (d.S_final) copy_f4(d.S_final + u * KV, Sf, K * V);
+}
+
+struct LFwdOut {
+  size_t Qs, Ks, Ss, Wh, Wl, Ph, Pl, G, total;
+  __host__ __device__ LFwdOut(int K, int V) {
+    Carve c;
+    Qs = c.take(2 * C * ld16(K));
+    Ks = c.take(2 * C * ld16(K));
+    Ss = c.take(2 * K * ld16(V));
+    Wh = c.take(2 * C * ld16(V));
+    Wl = c.take(2 * C * ld16(V));
+    Ph = c.take(2 * C * LDT);
+    Pl = c.take(2 * C * LDT);
+    G = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U*NB, nscan): O = e^G (Q S_n) + (Q K^T o Gamma) W
+__global__ void __launch_bounds__(256) tc_fwd_out(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  if (!d.q || !d.O) return;
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  const int64_t KV = (int64_t)K * V;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LFwdOut L(K, V);
+  bf16* Qs = (bf16*)(smem + L.Qs);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Ss = (bf16*)(smem + L.Ss);
+  bf16* Wh = (bf16*)(smem + L.Wh);
+  bf16* Wl = (bf16*)(smem + L.Wl);
+  bf16* Ph = (bf16*)(smem + L.Ph);
+  bf16* Pl = (bf16*)(smem + L.Pl);
+  float* G = (float*)(smem + L.G);
+  tile_to_bf16(Qs, ldk, d.q + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Ss, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K);
+  tile_split(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
+  load_gates_pad(d, u, t0, c, G, nullptr);
+  __syncthreads();
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.zero();
+    mma_acc<1, 2, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int s, float& v) {
+      tc::split_bf16(s <= t ? __expf(G[t] - G[s]) * v : 0.f, Ph + t * LDT + s, Pl + t * LDT + s);
+    });
+  });
+  __syncthreads();
+  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
+    tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, Wl, ldv, m0, n0, C);
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) d.O[row(u, T, t0 + t) * V + col] = v;
+    });
+  });
+}
+
+// ----------------------------------------------------------------- backward
+
+GPA_DEV float dscale(const ScanDesc& d, int u) { return d.dO_scale ? d.dO_scale[u] : 1.f; }
+
+struct LBwdLocal {
+  size_t Qs, Ks, Ss, Wh, Wl, dOs, Pf, dPf, Ph, Pl, dXh, dXl, G, racc, total;
+  __host__ __device__ LBwdLocal(int K, int V) {
+    Carve c;
+    Qs = c.take(2 * C * ld16(K));
+    Ks = c.take(2 * C * ld16(K));
+    Ss = c.take(2 * K * ld16(V));
+    Wh = c.take(2 * C * ld16(V));
+    Wl = c.take(2 * C * ld16(V));
+    dOs = c.take(2 * C * ld16(V));
+    Pf = c.take(4 * C * kAStride);
+    dPf = c.take(4 * C * kAStride);
+    Ph = c.take(2 * C * LDT);
+    Pl = c.take(2 * C * LDT);
+    dXh = c.take(2 * C * LDT);
+    dXl = c.take(2 * C * LDT);
+    G = c.take(4 * C);
+    racc = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U*NB, nscan): read-path gradients of O = e^G Q S_n + P W.
+__global__ void __launch_bounds__(256) tc_bwd_local(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  const int64_t KV = (int64_t)K * V;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBwdLocal L(K, V);
+  bf16* Qs = (bf16*)(smem + L.Qs);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Ss = (bf16*)(smem + L.Ss);
+  bf16* Wh = (bf16*)(smem + L.Wh);
+  bf16* Wl = (bf16*)(smem + L.Wl);
+  bf16* dOs = (bf16*)(smem + L.dOs);
+  float* Pf = (float*)(smem + L.Pf);
+  float* dPf = (float*)(smem + L.dPf);
+  bf16* Ph = (bf16*)(smem + L.Ph);
+  bf16* Pl = (bf16*)(smem + L.Pl);
+  bf16* dXh = (bf16*)(smem + L.dXh);
+  bf16* dXl = (bf16*)(smem + L.dXl);
+  float* G = (float*)(smem + L.G);
+  float* racc = (float*)(smem + L.racc);
+  tile_to_bf16(Qs, ldk, d.q + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Ss, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K);
+  tile_split(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
+  tile_to_bf16(dOs, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, dscale(d, u));
+  for (int t = threadIdx.x; t < C; t += blockDim.x) racc[t] = 0.f;
+  load_gates_pad(d, u, t0, c, G, nullptr);
+  __syncthreads();
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.zero();
+    mma_acc<1, 2, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int s, float& v) {
+      const float p = s <= t ? __expf(G[t] - G[s]) * v : 0.f;
+      Pf[t * kAStride + s] = p;
+      tc::split_bf16(p, Ph + t * LDT + s, Pl + t * LDT + s);
+    });
+    acc.zero();
+    tc::mma_acc3<1, 2, false, true>(acc, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
+    acc.each(m0, n0, [&](int t, int s, float& v) { dPf[t * kAStride + s] = s <= t ? v : 0.f; });
+  });
+  // rowsum(dO o (Q S_n))
+  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
+    float part[2] = {0.f, 0.f};
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      part[(t - m0) >> 3 & 1] += v * __bfloat162float(dOs[t * ldv + col]);
+    });
+    const int g = (threadIdx.x & 31) >> 2;
+    const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
+    if ((threadIdx.x & 3) == 0) {
+      atomicAdd(&racc[m0 + g], p0);
+      atomicAdd(&racc[m0 + g + 8], p1);
+    }
+  });
+  __syncthreads();
+  if (threadIdx.x < C) {
+    const int t = threadIdx.x;
+    float rs = 0.f, cs = 0.f;
+    for (int s = 0; s <= t; ++s) rs += dPf[t * kAStride + s] * Pf[t * kAStride + s];
+    for (int r = t; r < C; ++r) cs += dPf[r * kAStride + t] * Pf[r * kAStride + t];
+    if (t < c) d.sc_dG[row(u, T, t0 + t)] = __expf(G[t]) * racc[t] + rs - cs;
+  }
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    const float x = s <= t ? dPf[t * kAStride + s] * __expf(G[t] - G[s]) : 0.f;
+    tc::split_bf16(x, dXh + t * LDT + s, dXl + t * LDT + s);
+  }
+  __syncthreads();
+  if (d.dq) {
+    tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      mma_acc<1, NI, false, true>(acc, dOs, ldv, Ss, ldv, m0, n0, V);
+      acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
+      tc::mma_acc3<1, NI, false, false>(acc, dXh, dXl, LDT, Ks, nullptr, ldk, m0, n0, C);
+      acc.each(m0, n0, [&](int t, int col, float& v) {
+        if (t < c) d.dq[row(u, T, t0 + t) * K + col] += v;
+      });
+    });
+  }
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, true, false>(acc, dXh, dXl, LDT, Qs, nullptr, ldk, m0, n0, C);
+    acc.each(m0, n0, [&](int s, int col, float& v) {
+      if (s < c) d.sc_dK[row(u, T, t0 + s) * K + col] = v;
+    });
+  });
+  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, true, false>(acc, Ph, Pl, LDT, dOs, nullptr, ldv, m0, n0, C);
+    acc.each(m0, n0, [&](int s, int col, float& v) {
+      if (s < c) d.sc_dW[row(u, T, t0 + s) * V + col] = v;
+    });
+  });
+}
+
+struct LBwdState {
+  size_t Dh, Dl, Ks, Qg, Wknh, Wknl, dOs, dWh, dWl, G, lam, total;
+  __host__ __device__ LBwdState(int K, int V) {
+    Carve c;
+    Dh = c.take(2 * K * ld16(V));
+    Dl = c.take(2 * K * ld16(V));
+    Ks = c.take(2 * C * ld16(K));
+    Qg = c.take(2 * C * ld16(K));
+    Wknh = c.take(2 * C * ld16(K));
+    Wknl = c.take(2 * C * ld16(K));
+    dOs = c.take(2 * C * ld16(V));
+    dWh = c.take(2 * C * ld16(V));
+    dWl = c.take(2 * C * ld16(V));
+    G = c.take(4 * C);
+    lam = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U, nscan): reverse sweep; D = dS at block ends; dW = dW_local + lambda K D.
+// D is carried as a hi/lo bf16 pair (~16 significant bits) between blocks.
+__global__ void __launch_bounds__(256) tc_bwd_state(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  const int64_t KV = (int64_t)K * V;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBwdState L(K, V);
+  bf16* Dh = (bf16*)(smem + L.Dh);
+  bf16* Dl = (bf16*)(smem + L.Dl);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Qg = (bf16*)(smem + L.Qg);
+  bf16* Wknh = (bf16*)(smem + L.Wknh);
+  bf16* Wknl = (bf16*)(smem + L.Wknl);
+  bf16* dOs = (bf16*)(smem + L.dOs);
+  bf16* dWh = (bf16*)(smem + L.dWh);
+  bf16* dWl = (bf16*)(smem + L.dWl);
+  float* G = (float*)(smem + L.G);
+  float* lam = (float*)(smem + L.lam);
+  const float sc = dscale(d, u);
+  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
+    float x = d.ext ? d.ext[((int64_t)u * (bl.nb + 1) + bl.nb) * KV + i] : 0.f;
+    if (d.dS_final) x += d.dS_final[u * KV + i];
+    const int o = (i / V) * ldv + (i % V);
+    tc::split_bf16(x, Dh + o, Dl + o);
+  }
+  __syncthreads();
+  for (int n = bl.nb - 1; n >= 0; --n) {
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    float* de = d.Dend + ((int64_t)u * bl.nb + n) * KV;
+    for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
+      const int o = (i / V) * ldv + (i % V);
+      de[i] = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
+    }
+    load_gates_pad(d, u, t0, c, G, nullptr);
+    __syncthreads();
+    for (int t = threadIdx.x; t < C; t += blockDim.x) lam[t] = __expf(G[c - 1] - G[t]);
+    tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+    {
+      const float* qr = d.q + row(u, T, t0) * K;
+      for (int i = threadIdx.x; i < C * K; i += blockDim.x) {
+        const int t = i / K, k = i - t * K;
+        Qg[t * ldk + k] = __float2bfloat16(t < c ? qr[(int64_t)t * K + k] * __expf(G[t]) : 0.f);
+      }
+    }
+    tile_split(Wknh, Wknl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C, -1.f);
+    tile_to_bf16(dOs, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, sc);
+    __syncthreads();
+    // dW = dW_local + lambda (K D)
+    tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      tc::mma_acc3<1, NI, false, false>(acc, Ks, nullptr, ldk, Dh, Dl, ldv, m0, n0, K);
+      acc.each(m0, n0, [&](int t, int col, float& v) {
+        float w = 0.f;
+        if (t < c) {
+          const int64_t o = row(u, T, t0 + t) * V + col;
+          w = d.sc_dW[o] + lam[t] * v;
+          d.sc_dW[o] = w;
+        }
+        tc::split_bf16(w, dWh + t * ldv + col, dWl + t * ldv + col);
+      });
+    });
+    __syncthreads();
+    const float gc = __expf(G[c - 1]);
+    const float* ext = d.ext ? d.ext + ((int64_t)u * (bl.nb + 1) + n) * KV : nullptr;
+    // D <- e^{G_c} D + (e^G Q)^T dO - Wk^T dW + ext_n
+    tiles_n<1, 2>(K, V, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.each(m0, n0, [&](int k, int col, float& v) {
+        const int o = k * ldv + col;
+        v = gc * (__bfloat162float(Dh[o]) + __bfloat162float(Dl[o])) +
+            (ext ? ext[k * V + col] : 0.f);
+      });
+      mma_acc<1, NI, true, false>(acc, Qg, ldk, dOs, ldv, m0, n0, C);
+      tc::mma_acc3<1, NI, true, false>(acc, Wknh, Wknl, ldk, dWh, dWl, ldv, m0, n0, C);
+      __syncwarp();
+      acc.each(m0, n0, [&](int k, int col, float& v) {
+        const int o = k * ldv + col;
+        tc::split_bf16(v, Dh + o, Dl + o);
+      });
+    });
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
+    const int o = (i / V) * ldv + (i % V);
+    d.dS0[u * KV + i] = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
+  }
+}
+
+struct LBwdA {
+  // phase 1 region R: Sb, Db; phase 2 reuses it for Kl, A, Tm, Tth, Ttl
+  size_t Ks, R, Sb, Db, Kl, A, Tm, Tth, Ttl, Wb, dWh, dWl, Uh, Ul, Xs, dRuh, dRul, G, bt, dlam, dbacc,
+      red, total;
+  __host__ __device__ LBwdA(int K, int V) {
+    Carve c;
+    Ks = c.take(2 * C * ld16(K));
+    const size_t sbytes = 2 * K * ld16(V);
+    const size_t p2 = 2 * C * ld16(K) + 2 * (4 * C * kAStride) + 2 * (2 * C * LDT) + 64;
+    R = c.take(2 * sbytes > p2 ? 2 * sbytes : p2);
+    Sb = R;
+    Db = R + sbytes;
+    Carve r2;
+    r2.off = R;
+    Kl = r2.take(2 * C * ld16(K));
+    A = r2.take(4 * C * kAStride);
+    Tm = r2.take(4 * C * kAStride);
+    Tth = r2.take(2 * C * LDT);
+    Ttl = r2.take(2 * C * LDT);
+    Wb = c.take(2 * C * ld16(V));
+    dWh = c.take(2 * C * ld16(V));
+    dWl = c.take(2 * C * ld16(V));
+    Uh = c.take(2 * C * ld16(V));
+    Ul = c.take(2 * C * ld16(V));
+    Xs = c.take(4 * 768);
+    dRuh = c.take(2 * C * ld16(V));
+    dRul = c.take(2 * C * ld16(V));
+    G = c.take(4 * C);
+    bt = c.take(4 * C);
+    dlam = c.take(4 * C);
+    dbacc = c.take(4 * C);
+    red = c.take(4 * 32);
+    total = c.off;
+  }
+};
+
+// grid (U*NB, nscan): state-update terms and the U path of the block backward.
+__global__ void __launch_bounds__(256) tc_bwd_chunk_a(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  const int ldk = ld16(K), ldv = ld16(V);
+  const int64_t KV = (int64_t)K * V;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBwdA L(K, V);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Sb = (bf16*)(smem + L.Sb);
+  bf16* Db = (bf16*)(smem + L.Db);
+  bf16* Kl = (bf16*)(smem + L.Kl);
+  float* A = (float*)(smem + L.A);
+  float* Tm = (float*)(smem + L.Tm);
+  bf16* Tth = (bf16*)(smem + L.Tth);
+  bf16* Ttl = (bf16*)(smem + L.Ttl);
+  bf16* Wb = (bf16*)(smem + L.Wb);
+  bf16* dWh = (bf16*)(smem + L.dWh);
+  bf16* dWl = (bf16*)(smem + L.dWl);
+  bf16* Uh = (bf16*)(smem + L.Uh);
+  bf16* Ul = (bf16*)(smem + L.Ul);
+  float* Xs = (float*)(smem + L.Xs);
+  bf16* dRuh = (bf16*)(smem + L.dRuh);
+  bf16* dRul = (bf16*)(smem + L.dRul);
+  float* G = (float*)(smem + L.G);
+  float* bt = (float*)(smem + L.bt);
+  float* dlam = (float*)(smem + L.dlam);
+  float* dbacc = (float*)(smem + L.dbacc);
+  float* red = (float*)(smem + L.red);
+  const float* sg = d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV;
+  const float* dg = d.Dend + ((int64_t)u * bl.nb + n) * KV;
+  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  tile_to_bf16(Sb, ldv, sg, V, K, V, K);
+  tile_to_bf16(Db, ldv, dg, V, K, V, K);
+  tile_to_bf16(Wb, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
+  tile_split(dWh, dWl, ldv, d.sc_dW + row(u, T, t0) * V, V, c, V, C);
+  tile_split(Uh, Ul, ldv, d.Ub + row(u, T, t0) * V, V, c, V, C);
+  for (int t = threadIdx.x; t < C; t += blockDim.x) dlam[t] = dbacc[t] = 0.f;
+  if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
+  load_gates_pad(d, u, t0, c, G, bt);
+  __syncthreads();
+  // WD = W D^T: dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, true>(acc, Wb, ldv, Db, ldv, m0, n0, V);
+    float part[2] = {0.f, 0.f};
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * K + col;
+        d.sc_dK[o] += __expf(G[c - 1] - G[t]) * v;
+      }
+      part[(t - m0) >> 3 & 1] += v * __bfloat162float(Ks[t * ldk + col]);
+    });
+    const int g = (threadIdx.x & 31) >> 2;
+    const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
+    if ((threadIdx.x & 3) == 0) {
+      atomicAdd(&dlam[m0 + g], p0);
+      atomicAdd(&dlam[m0 + g + 8], p1);
+    }
+  });
+  {  // <D, S> in fp32
+    float part = 0.f;
+    for (int i = threadIdx.x; i < K * V; i += blockDim.x) part += dg[i] * sg[i];
+    part = warp_sum(part);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&red[0], part);
+  }
+  // dWk = -dW S^T
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, true>(acc, dWh, dWl, ldv, Sb, nullptr, ldv, m0, n0, V);
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) d.sc_dWk[row(u, T, t0 + t) * K + col] = -v;
+    });
+  });
+  __syncthreads();  // phase 1 done: region R (Sb, Db) is reused below
+  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  __syncthreads();
+  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
+  __syncthreads();
+  invert_unit_lower(A, Tm, Xs);
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    tc::split_bf16(Tm[t * kAStride + s], Tth + t * LDT + s, Ttl + t * LDT + s);
+  }
+  if (threadIdx.x < 32) {  // dG from the state update (lambda and gamma_c terms)
+    float tot = 0.f;
+    for (int t = threadIdx.x; t < c; t += 32) {
+      const float x = dlam[t] * __expf(G[c - 1] - G[t]);
+      tot += x;
+      d.sc_dG[row(u, T, t0 + t)] -= x;
+    }
+    tot = warp_sum(tot);
+    __syncwarp();
+    if (threadIdx.x == 0) d.sc_dG[row(u, T, t0 + c - 1)] += tot + __expf(G[c - 1]) * red[0];
+  }
+  __syncthreads();
+  // dRu = T^T dW ; dV = b dRu ; db += rowsum(dRu o V)
+  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWh, dWl, ldv, m0, n0, C);
+    float part[2] = {0.f, 0.f};
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      tc::split_bf16(v, dRuh + t * ldv + col, dRul + t * ldv + col);
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * V + col;
+        atomicAdd(&d.dv[o], bt[t] * v);
+        part[(t - m0) >> 3 & 1] += v * d.v[o];
+      }
+    });
+    const int g = (threadIdx.x & 31) >> 2;
+    const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
+    if ((threadIdx.x & 3) == 0) {
+      atomicAdd(&dbacc[m0 + g], p0);
+      atomicAdd(&dbacc[m0 + g + 8], p1);
+    }
+  });
+  __syncthreads();
+  // dA (U path) = -dRu U^T, strictly lower
+  float* dA = d.sc_dA + ((int64_t)u * bl.nb + n) * C * C;
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.zero();
+    tc::mma_acc3<1, 2, false, true>(acc, dRuh, dRul, ldv, Uh, Ul, ldv, m0, n0, V);
+    acc.each(m0, n0, [&](int t, int s, float& v) { dA[t * C + s] = s < t ? -v : 0.f; });
+  });
+  for (int t = threadIdx.x; t < c; t += blockDim.x) d.sc_db[row(u, T, t0 + t)] = dbacc[t];
+}
+
+struct LBwdB {
+  size_t Ks, Kl, Wkh, Wkl, dWkh, dWkl, A, Tm, Xs, Tth, Ttl, dAf, Mmb, dRwh, dRwl, G, bt, dG, db, rw,
+      total;
+  __host__ __device__ LBwdB(int K, int) {
+    Carve c;
+    Ks = c.take(2 * C * ld16(K));
+    Kl = c.take(2 * C * ld16(K));
+    Wkh = c.take(2 * C * ld16(K));
+    Wkl = c.take(2 * C * ld16(K));
+    dWkh = c.take(2 * C * ld16(K));
+    dWkl = c.take(2 * C * ld16(K));
+    A = c.take(4 * C * kAStride);
+    Tm = c.take(4 * C * kAStride);
+    Xs = c.take(4 * 768);
+    Tth = c.take(2 * C * LDT);
+    Ttl = c.take(2 * C * LDT);
+    dAf = c.take(4 * C * kAStride);
+    Mmb = c.take(2 * C * LDT);
+    dRwh = c.take(2 * C * ld16(K));
+    dRwl = c.take(2 * C * ld16(K));
+    G = c.take(4 * C);
+    bt = c.take(4 * C);
+    dG = c.take(4 * C);
+    db = c.take(4 * C);
+    rw = c.take(4 * C);
+    total = c.off;
+  }
+};
+
+// grid (U*NB, nscan): Wk path, dA consequences, final dK / dg / dbeta of every block.
+__global__ void __launch_bounds__(256) tc_bwd_chunk_b(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K;
+  const int ldk = ld16(K);
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBwdB L(K, d.V);
+  bf16* Ks = (bf16*)(smem + L.Ks);
+  bf16* Kl = (bf16*)(smem + L.Kl);
+  bf16* Wkh = (bf16*)(smem + L.Wkh);
+  bf16* Wkl = (bf16*)(smem + L.Wkl);
+  bf16* dWkh = (bf16*)(smem + L.dWkh);
+  bf16* dWkl = (bf16*)(smem + L.dWkl);
+  float* A = (float*)(smem + L.A);
+  float* Tm = (float*)(smem + L.Tm);
+  float* Xs = (float*)(smem + L.Xs);
+  bf16* Tth = (bf16*)(smem + L.Tth);
+  bf16* Ttl = (bf16*)(smem + L.Ttl);
+  float* dAf = (float*)(smem + L.dAf);
+  bf16* Mmb = (bf16*)(smem + L.Mmb);
+  bf16* dRwh = (bf16*)(smem + L.dRwh);
+  bf16* dRwl = (bf16*)(smem + L.dRwl);
+  float* G = (float*)(smem + L.G);
+  float* bt = (float*)(smem + L.bt);
+  float* dG = (float*)(smem + L.dG);
+  float* db = (float*)(smem + L.db);
+  float* rw = (float*)(smem + L.rw);
+  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
+  tile_split(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C);
+  tile_split(dWkh, dWkl, ldk, d.sc_dWk + row(u, T, t0) * K, K, c, K, C);
+  const float* dAg = d.sc_dA + ((int64_t)u * bl.nb + n) * C * C;
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    dAf[t * kAStride + s] = (t < c && s < c) ? dAg[i] : 0.f;
+  }
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    dG[t] = t < c ? d.sc_dG[row(u, T, t0 + t)] : 0.f;
+    db[t] = t < c ? d.sc_db[row(u, T, t0 + t)] : 0.f;
+    rw[t] = 0.f;
+  }
+  load_gates_pad(d, u, t0, c, G, bt);
+  __syncthreads();
+  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
+  __syncthreads();
+  invert_unit_lower(A, Tm, Xs);
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    tc::split_bf16(Tm[t * kAStride + s], Tth + t * LDT + s, Ttl + t * LDT + s);
+  }
+  __syncthreads();
+  // dRw = T^T dWk ; sc_dK += b e^G dRw ; rw_t = dRw_t . k_t
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWkh, dWkl, ldk, m0, n0, C);
+    float part[2] = {0.f, 0.f};
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      tc::split_bf16(v, dRwh + t * ldk + col, dRwl + t * ldk + col);
+      if (t < c) d.sc_dK[row(u, T, t0 + t) * K + col] += bt[t] * __expf(G[t]) * v;
+      part[(t - m0) >> 3 & 1] += v * (__bfloat162float(Ks[t * ldk + col]) +
+                                      __bfloat162float(Kl[t * ldk + col]));
+    });
+    const int g = (threadIdx.x & 31) >> 2;
+    const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
+    if ((threadIdx.x & 3) == 0) {
+      atomicAdd(&rw[m0 + g], p0);
+      atomicAdd(&rw[m0 + g + 8], p1);
+    }
+  });
+  __syncthreads();
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    const float e = __expf(G[t]);
+    db[t] += e * rw[t];
+    dG[t] += bt[t] * e * rw[t];
+  }
+  // dA -= dRw Wk^T (strictly lower)
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.zero();
+    tc::mma_acc3<1, 2, false, true>(acc, dRwh, dRwl, ldk, Wkh, Wkl, ldk, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int s, float& v) {
+      dAf[t * kAStride + s] = s < t ? dAf[t * kAStride + s] - v : 0.f;
+    });
+  });
+  __syncthreads();
+  if (threadIdx.x < C) {
+    const int t = threadIdx.x;
+    // A = b_t Atil: rowsum(dA o Atil) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
+    float r2 = 0.f, c2 = 0.f;
+    for (int s = 0; s < t; ++s) r2 += dAf[t * kAStride + s] * A[t * kAStride + s];
+    for (int s = t + 1; s < C; ++s) c2 += dAf[s * kAStride + t] * A[s * kAStride + t];
+    if (t < c) db[t] += r2 / bt[t];
+    dG[t] += r2 - c2;
+  }
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    Mmb[t * LDT + s] = __float2bfloat16(s < t ? dAf[t * kAStride + s] * bt[t] * __expf(G[t] - G[s]) : 0.f);
+  }
+  __syncthreads();
+  // dK = sc_dK + Mm K + Mm^T K
+  tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
+    acc.each(m0, n0, [&](int t, int col, float& v) {
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * K + col;
+        d.dk[o] += d.sc_dK[o] + v;
+      }
+    });
+  });
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int t = c - 1; t >= 0; --t) {
+      acc += dG[t];
+      dG[t] = acc;
+    }
+  }
+  __syncthreads();
+  if (d.dg64) {
+    if (threadIdx.x == 0) {
+      double sgm = 0.0, sbt = 0.0;
+      for (int t = 0; t < c; ++t) {
+        sgm += dG[t];
+        sbt += db[t];
+      }
+      atomicAdd(&d.dg64[(int64_t)u * d.dg_su], sgm);
+      atomicAdd(&d.dbeta64[(int64_t)u * d.dg_su], sbt);
+    }
+    return;
+  }
+  for (int t = threadIdx.x; t < c; t += blockDim.x) {
+    const int64_t gi = (int64_t)u * d.dg_su + (int64_t)(t0 + t) * d.dg_st;
+    d.dg[gi] += dG[t];
+    d.dbeta[gi] += db[t];
+  }
+}
+
+template <class Kern>
+cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStream_t st,
+                      const ScanBatch& b, int U, const Blocks& bl) {
+  if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  Launch scope(name, st);
+  k<<<grid, 256, smem, st>>>(b, U, bl);
+  return cudaGetLastError();
+}
+
+template <class Lay>
+size_t max_smem(const ScanBatch& b) {
+  size_t m = 0;
+  for (int i = 0; i < b.n; ++i) {
+    const size_t s = Lay(b.s[i].K, b.s[i].V).total;
+    m = s > m ? s : m;
+  }
+  return m;
+}
+
+}  // namespace
+
+bool tc_supported(int K, int V) {
+  return K % 16 == 0 && V % 16 == 0 && K <= 128 && V <= 128;
+}
+
+cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
+                       cudaStream_t st) {
+  cudaError_t e = tc_launch("tc_fwd_chunk", tc_fwd_chunk, dim3(U * bl.nb, b.n),
+                            max_smem<LFwdChunk>(b), st, b, U, bl);
+  if (e != cudaSuccess) return e;
+  e = tc_launch("tc_fwd_state", tc_fwd_state, dim3(U, b.n), max_smem<LFwdState>(b), st, b, U, bl);
+  if (e != cudaSuccess || !with_output) return e;
+  return tc_output(b, U, bl, st);
+}
+
+cudaError_t tc_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  return tc_launch("tc_fwd_out", tc_fwd_out, dim3(U * bl.nb, b.n), max_smem<LFwdOut>(b), st, b,
+                   U, bl);
+}
+
+cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  return tc_launch("tc_bwd_local", tc_bwd_local, dim3(U * bl.nb, b.n), max_smem<LBwdLocal>(b),
+                   st, b, U, bl);
+}
+
+cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  cudaError_t e = tc_launch("tc_fwd_chunk", tc_fwd_chunk, dim3(U * bl.nb, b.n),
+                            max_smem<LFwdChunk>(b), st, b, U, bl);
+  if (e != cudaSuccess) return e;
+  e = tc_launch("tc_bwd_state", tc_bwd_state, dim3(U, b.n), max_smem<LBwdState>(b), st, b, U, bl);
+  if (e != cudaSuccess) return e;
+  e = tc_launch("tc_bwd_chunk_a", tc_bwd_chunk_a, dim3(U * bl.nb, b.n), max_smem<LBwdA>(b), st,
+                b, U, bl);
+  if (e != cudaSuccess) return e;
+  return tc_launch("tc_bwd_chunk_b", tc_bwd_chunk_b, dim3(U * bl.nb, b.n), max_smem<LBwdB>(b), st,
+                   b, U, bl);
+}
+
+}  // namespace gpa
