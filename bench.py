@@ -115,7 +115,14 @@ def kernel_flops(cfg, units, length):
         "gdn_bwd_chunk_v": allscans,
         "gdn_bwd_chunk_k": allscans,
     }
-    return {k: units * nb * sum(per[k](K, V) for K, V in use[k]) for k in per}
+    out = {k: units * nb * sum(per[k](K, V) for K, V in use[k]) for k in per}
+    # tensor-core variants of the same phases (bf16 path)
+    for tk, sk in (("tc_fwd_chunk", "gdn_fwd_chunk"), ("tc_fwd_state", "gdn_fwd_state"),
+                   ("tc_fwd_out", "gdn_fwd_out"), ("tc_bwd_local", "gdn_bwd_local"),
+                   ("tc_bwd_state", "gdn_bwd_state"), ("tc_bwd_chunk_a", "gdn_bwd_chunk_v"),
+                   ("tc_bwd_chunk_b", "gdn_bwd_chunk_k")):
+        out[tk] = out[sk]
+    return out
 
 
 # ------------------------------------------------------------------ clocks
@@ -402,13 +409,19 @@ def run_reference(args, rank):
 
 
 def main():
+    global BATCH, LENGTH
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="per-rank batch (default: config 2); smaller values are for profiling")
+    ap.add_argument("--length", type=int, default=LENGTH,
+                    help="sequence length (default: config 2); smaller values are for profiling")
     args = ap.parse_args()
+    BATCH, LENGTH = args.batch, args.length
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -304,6 +304,15 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
       return fail(GPA_B200_LAUNCH_FAILURE, std::string(#x) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
+// parameter-gradient reduction: tensor-core variant when the widths allow it
+cudaError_t head_outer(const Geo& g, int B, int T, int H, const float* X, int P, int xmode,
+                       const float* Y, int Q, const float* scale, int64_t scale_stride,
+                       float cscale, float* out, cudaStream_t st) {
+  if (g.fast && xmode != 2 && P % 16 == 0 && Q % 16 == 0)
+    return tc_head_outer(B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, st);
+  return launch_head_outer(B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, st);
+}
+
 cudaError_t zero(float* p, size_t n, cudaStream_t st) {
   return n ? cudaMemsetAsync(p, 0, n * sizeof(float), st) : cudaSuccess;
 }
@@ -355,7 +364,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
   CK(launch_input(q, k, v, g.dt, g.B, T, g.H, D, Dv, s.qf, s.qh, s.qn, s.key[0], s.val[0], st));
   for (int j = 0; j < g.L; ++j) {
     const int M = g.M[j];
-    CK(launch_level_prep(U, T, g.H, D, M, s.key[j], p->center[j], p->gate_weight[j],
+    CK((g.fast ? tc_level_prep : launch_level_prep)(U, T, g.H, D, M, s.key[j], p->center[j], p->gate_weight[j],
                          p->gate_bias[j], g.bm, g.pos_none, s.nk[j], s.kn[j], s.slot[j], s.ns[j],
                          s.sn[j], s.raw4[j], s.gates[j], st));
     ScanBatch sb;
@@ -397,7 +406,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     ou.S_final = so->outer[j];
     CK(gdn_forward(sb, U, bl, true, st));
     const int with_res = j + 1 < g.L;
-    CK(launch_level_post(U, bl, g.post, g.H, D, Dv, M, with_res, s.nk[j], s.key[j], s.val[j],
+    CK((g.fast ? tc_level_post : launch_level_post)(U, bl, g.post, g.H, D, Dv, M, with_res, s.nk[j], s.key[j], s.val[j],
                          s.Abnd[j], s.Bbnd[j], fz_in ? si->frozen_inner[j] : nullptr,
                          fz_in ? si->frozen_outer[j] : nullptr, p->residual_raw, j, s.write[j],
                          s.bsum[j], with_res ? s.key[j + 1] : nullptr,
@@ -447,7 +456,7 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
         bi.dmsg[bi.n] = nullptr;
         ++bi.n;
       }
-    CK(launch_bridge(U, T, g.H, D, g.M[j], g.L, j, bi, p->edge_logits, p->relation_gain,
+    CK((g.fast ? tc_bridge : launch_bridge)(U, T, g.H, D, g.M[j], g.L, j, bi, p->edge_logits, p->relation_gain,
                      p->route_up[j], p->route_down[j], p->route_mlp_gain, p->route_weight[j],
                      p->query_weight[j], g.qs, s.logits[j], s.qf, s.r[j], s.hp[j], s.mlp[j],
                      s.route[j], s.qoh[j], s.qon[j], st));
@@ -576,18 +585,18 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
         ++bi.n;
       }
     const int M = g.M[j];
-    CK(launch_bridge_bwd(U, T, H, D, M, L, j, bi, p->edge_logits, p->relation_gain,
+    CK((g.fast ? tc_bridge_bwd : launch_bridge_bwd)(U, T, H, D, M, L, j, bi, p->edge_logits, p->relation_gain,
                          p->route_up[j], p->route_down[j], p->route_mlp_gain, p->route_weight[j],
                          p->query_weight[j], g.qs, s.logits[j], s.r[j], s.hp[j], s.mlp[j],
                          s.qoh[j], s.qon[j], x.dqoh[j], x.dqo[j], x.droute[j], x.dhp[j],
                          x.dlogits[j], x.dq_direct, x.scal, x.scalE, E ? E : 1, st));
-    CK(launch_head_outer(g.B, T, H, s.route[j], M, 0, x.dqo[j], M, nullptr, 0, 1.f,
+    CK(head_outer(g, g.B, T, H, s.route[j], M, 0, x.dqo[j], M, nullptr, 0, 1.f,
                          gp->route_weight[j], st));
-    CK(launch_head_outer(g.B, T, H, s.qf, D, 0, x.dqo[j], M, nullptr, 0, g.qs,
+    CK(head_outer(g, g.B, T, H, s.qf, D, 0, x.dqo[j], M, nullptr, 0, g.qs,
                          gp->query_weight[j], st));
-    CK(launch_head_outer(g.B, T, H, s.r[j], M, 0, x.dhp[j], 2 * M, nullptr, 0, 1.f,
+    CK(head_outer(g, g.B, T, H, s.r[j], M, 0, x.dhp[j], 2 * M, nullptr, 0, 1.f,
                          gp->route_up[j], st));
-    CK(launch_head_outer(g.B, T, H, s.hp[j], 2 * M, 1, x.droute[j], M,
+    CK(head_outer(g, g.B, T, H, s.hp[j], 2 * M, 1, x.droute[j], M,
                          p->route_mlp_gain + (size_t)j * H, 1, 1.f, gp->route_down[j], st));
   }
   // relation scans, grouped by target level
@@ -670,7 +679,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
                                        last + g.post, (int64_t)szB, st));
       }
     }
-    CK(launch_post_bwd(U, bl, g.post, g.offset, H, D, Dv, M, L, j, with_res, s.nk[j], s.write[j],
+    CK((g.fast ? tc_post_bwd : launch_post_bwd)(U, bl, g.post, g.offset, H, D, Dv, M, L, j, with_res, s.nk[j], s.write[j],
                        s.Abnd[j], s.Bbnd[j], fz_in ? si->frozen_inner[j] : nullptr,
                        fz_in ? si->frozen_outer[j] : nullptr, p->residual_raw, x.dkey, x.dval,
                        x.dwrite[j], x.dnk, x.extA, x.extB, fz_in ? dsi->frozen_inner[j] : nullptr,
@@ -741,14 +750,14 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     ou.sc_dA = x.dA[1];
     ou.Dend = x.Dend[1];
     CK(gdn_backward_rest(sb, U, bl, st));
-    CK(launch_prep_bwd(U, T, H, D, M, p->center[j], p->gate_weight[j], g.bm, g.pos_none,
+    CK((g.fast ? tc_prep_bwd : launch_prep_bwd)(U, T, H, D, M, p->center[j], p->gate_weight[j], g.bm, g.pos_none,
                        s.raw4[j], s.nk[j], s.kn[j], s.ns[j], s.sn[j], x.dgates, x.dnk, x.dns,
                        x.dslot, x.d4, x.dkey, st));
-    CK(launch_head_outer(g.B, T, H, x.dslot, M, 0, s.key[j], D, nullptr, 0, 1.f, gp->center[j],
+    CK(head_outer(g, g.B, T, H, x.dslot, M, 0, s.key[j], D, nullptr, 0, 1.f, gp->center[j],
                          st));
-    CK(launch_head_outer(g.B, T, H, s.nk[j], D, 0, x.d4, 4, nullptr, 0, 1.f, gp->gate_weight[j],
+    CK(head_outer(g, g.B, T, H, s.nk[j], D, 0, x.d4, 4, nullptr, 0, 1.f, gp->gate_weight[j],
                          st));
-    CK(launch_head_outer(g.B, T, H, nullptr, 1, 2, x.d4, 4, nullptr, 0, 1.f, gp->gate_bias[j],
+    CK(head_outer(g, g.B, T, H, nullptr, 1, 2, x.d4, 4, nullptr, 0, 1.f, gp->gate_bias[j],
                          st));
   }
   CK(launch_input_bwd(g.B, T, H, D, Dv, g.dt, s.qh, s.qn, x.dqh, x.dq_direct, x.dkey, x.dval, dq,

@@ -4,101 +4,10 @@
 // residual :190-194, base logits :196-204, relation gates :206-223, dense
 // reader (bridge) :225-262, lag-block writes :314-316, output mix :340-341.
 #include "level.cuh"
+#include "rowops.cuh"
 
 namespace gpa {
 namespace {
-
-constexpr int kRowsPerTile = 64;
-constexpr int kMaxPerLane = 8;  // vectors up to 256 long per warp row
-
-GPA_DEV int64_t row(int u, int T, int t) { return (int64_t)u * T + t; }
-
-// softmax over the lane-strided vector x[0..n) held in registers
-GPA_DEV void warp_softmax(float (&x)[kMaxPerLane], int n) {
-  const int lane = threadIdx.x & 31;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) mx = fmaxf(mx, x[i]);
-  mx = warp_max(mx);
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) {
-      x[i] = __expf(x[i] - mx);
-      s += x[i];
-    }
-  s = warp_sum(s);
-  const float inv = 1.f / s;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) x[i] *= inv;
-}
-
-GPA_DEV float warp_norm(const float (&x)[kMaxPerLane], int n) {
-  const int lane = threadIdx.x & 31;
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) s += x[i] * x[i];
-  return sqrtf(warp_sum(s));
-}
-
-GPA_DEV float warp_dot(const float (&x)[kMaxPerLane], const float (&y)[kMaxPerLane], int n) {
-  const int lane = threadIdx.x & 31;
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) s += x[i] * y[i];
-  return warp_sum(s);
-}
-
-GPA_DEV void load_vec(float (&x)[kMaxPerLane], const float* p, int n) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) x[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
-}
-
-GPA_DEV void store_vec(float* p, const float (&x)[kMaxPerLane], int n) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < n) p[lane + 32 * i] = x[i];
-}
-
-// unit-normalisation backward: y = x / max(|x|, eps)
-GPA_DEV void unit_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
-                      const float (&dy)[kMaxPerLane], float nrm, int n) {
-  if (nrm > kUnitEps) {
-    const float yd = warp_dot(y, dy, n);
-    const float inv = 1.f / nrm;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = (dy[i] - y[i] * yd) * inv;
-  } else {
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = dy[i] / kUnitEps;
-  }
-}
-
-GPA_DEV void softmax_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
-                         const float (&dy)[kMaxPerLane], int n) {
-  const float yd = warp_dot(y, dy, n);
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) dx[i] = y[i] * (dy[i] - yd);
-}
-
-GPA_DEV float block_sum(float x, float* red) {
-  x = warp_sum(x);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
-  __syncthreads();
-  float s = 0.f;
-  if (threadIdx.x < 32) {
-    s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    s = warp_sum(s);
-  }
-  return s;  // valid in warp 0
-}
 
 // ------------------------------------------------------------------ forward
 
@@ -304,19 +213,6 @@ __global__ void k_rel_gates(int U, int H, int E, int pos_none, const float* deca
   const int e = i / U, u = i - e * U, h = u % H;
   ge[i] = pos_none ? 0.f : -softplus(decay_raw[e * H + h]);
   be[i] = sigmoid(beta_raw[e * H + h]);
-}
-
-// softmax over the incoming edges' logits for head h
-GPA_DEV void edge_weights(const BridgeIn& in, const float* edge_logits, int H, int h,
-                          float* w) {
-  float mx = -INFINITY;
-  for (int a = 0; a < in.n; ++a) mx = fmaxf(mx, edge_logits[in.edge[a] * H + h]);
-  float s = 0.f;
-  for (int a = 0; a < in.n; ++a) {
-    w[a] = __expf(edge_logits[in.edge[a] * H + h] - mx);
-    s += w[a];
-  }
-  for (int a = 0; a < in.n; ++a) w[a] /= s;
 }
 
 // CTA per (u, 64-token tile), target level j: dense reader, route MLP, query projection.

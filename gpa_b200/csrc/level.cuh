@@ -105,6 +105,49 @@ cudaError_t launch_input_bwd(int B, int T, int H, int D, int Dv, int dt, const f
                              const float* dkey, const float* dval, void* dq, void* dk, void* dv,
                              cudaStream_t st);
 
+// Tensor-core variants (level_tc.cu): bf16 operands, fp32 accumulation; widths
+// (key_dim, value_dim, slots) multiples of 16 and <= 128.  Same arguments as the
+// SIMT launchers above.
+cudaError_t tc_level_prep(int U, int T, int H, int D, int M, const float* key, const float* C,
+                          const float* Wg, const float* gbias, float beta_max, int pos_none,
+                          float* nk, float* kn, float* slot, float* ns, float* sn, float* raw4,
+                          float* gates, cudaStream_t st);
+cudaError_t tc_level_post(int U, const Blocks& bl, int post, int H, int D, int Dv, int M,
+                          int with_residual, const float* nk, const float* key, const float* val,
+                          const float* Abnd, const float* Bbnd, const float* fzA, const float* fzB,
+                          const float* residual_raw, int j, float* write, float* bsum,
+                          float* key_next, float* val_next, cudaStream_t st);
+cudaError_t tc_bridge(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                      const float* edge_logits, const float* relation_gain, const float* route_up,
+                      const float* route_down, const float* route_mlp_gain, const float* Wrs,
+                      const float* Wqs, float qs, const float* logits, const float* qf, float* r,
+                      float* hp, float* mlp, float* route, float* qoh, float* qon,
+                      cudaStream_t st);
+cudaError_t tc_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                          const float* edge_logits, const float* relation_gain,
+                          const float* route_up, const float* route_down,
+                          const float* route_mlp_gain, const float* Wrs, const float* Wqs,
+                          float qs, const float* logits, const float* r, const float* hp,
+                          const float* mlp, const float* qoh, const float* qon, const float* dqoh,
+                          float* dqo, float* droute, float* dhp, float* dlogits, float* dq_direct,
+                          double* scal, double* scalE, int E, cudaStream_t st);
+cudaError_t tc_post_bwd(int U, const Blocks& bl, int post, int offset, int H, int D, int Dv,
+                        int M, int L, int j, int with_residual, const float* nk,
+                        const float* write, const float* Abnd, const float* Bbnd,
+                        const float* fzA, const float* fzB, const float* residual_raw,
+                        const float* dkey, const float* dval, float* dwrite, float* dnk,
+                        float* extA, float* extB, float* dfzA, float* dfzB, double* scal,
+                        cudaStream_t st);
+cudaError_t tc_prep_bwd(int U, int T, int H, int D, int M, const float* C, const float* Wg,
+                        float beta_max, int pos_none, const float* raw4, const float* nk,
+                        const float* kn, const float* ns, const float* sn, const float* dgates,
+                        const float* dnk, const float* dns, float* dslot, float* d4, float* dkey,
+                        cudaStream_t st);
+// P, Q multiples of 16; xmode 0 or 1
+cudaError_t tc_head_outer(int B, int T, int H, const float* X, int P, int xmode, const float* Y,
+                          int Q, const float* scale, int64_t scale_stride, float cscale,
+                          float* out, cudaStream_t st);
+
 struct FoldArgs {
   int B, H, L, E, pos_none;
   int edge_src[kMaxEdges], edge_dst[kMaxEdges];

@@ -1,0 +1,884 @@
+// Tensor-core (bf16 mma.sync, fp32 accumulate) variants of the per-token level
+// kernels, used with bf16 / fp16 inputs when every width is a multiple of 16.
+// Each CTA handles 64 tokens of one unit; per-head weights are staged in
+// shared memory as bf16 (the reference applies them in the activation dtype,
+// src/gpa/attention.py:177, 243-254), per-row softmax / norm work stays on
+// warps.  Formulas are those of the SIMT kernels in level.cu.
+#include "level.cuh"
+#include "rowops.cuh"
+#include "tc_util.cuh"
+
+namespace gpa {
+namespace {
+
+using tc::Acc;
+using tc::bf16;
+using tc::Carve;
+using tc::for_tiles;
+using tc::ld16;
+using tc::mma_acc;
+using tc::quad_sum;
+using tc::tile_split;
+using tc::tile_to_bf16;
+using tc::tiles_n;
+
+constexpr int R = kRowsPerTile;  // 64 tokens per CTA
+
+GPA_DEV void store_bf16_row(bf16* dst, const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) dst[lane + 32 * i] = __float2bfloat16(x[i]);
+}
+
+GPA_DEV void store_split_row(bf16* hi, bf16* lo, const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) tc::split_bf16(x[i], hi + lane + 32 * i, lo + lane + 32 * i);
+}
+
+template <class Lay>
+size_t smem_of(int a, int b, int c) { return Lay(a, b, c).total; }
+
+// ------------------------------------------------------------------ prep
+
+struct LPrep {
+  size_t Kb, Cb, St, total;
+  __host__ __device__ LPrep(int D, int M, int) {
+    Carve c;
+    Kb = c.take(2 * R * ld16(D));
+    Cb = c.take(2 * M * ld16(D));
+    St = c.take(4 * R * M);
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_level_prep(int U, int T, int H, int D, int M,
+                                                     const float* key, const float* C,
+                                                     const float* Wg, const float* gbias,
+                                                     float beta_max, int pos_none, float* nk,
+                                                     float* kn, float* slot, float* ns, float* sn,
+                                                     float* raw4, float* gates) {
+  const int ntile = (T + R - 1) / R;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * R;
+  const int c = min(R, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LPrep L(D, M, 0);
+  bf16* Kb = (bf16*)(smem + L.Kb);
+  bf16* Cb = (bf16*)(smem + L.Cb);
+  float* St = (float*)(smem + L.St);
+  tile_to_bf16(Kb, ld16(D), key + row(u, T, t0) * D, D, c, D, R);
+  tile_to_bf16(Cb, ld16(D), C + (int64_t)h * M * D, D, M, D, M);
+  const float* wg = Wg + (int64_t)h * D * 4;
+  for (int t = warp; t < c; t += nw) {
+    const float* kr = key + row(u, T, t0 + t) * D;
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) ss += kr[d] * kr[d];
+    const float nrm = sqrtf(warp_sum(ss));
+    const float inv = 1.f / fmaxf(nrm, kUnitEps);
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int d = lane; d < D; d += 32) {
+      const float x = kr[d] * inv;
+      nk[row(u, T, t0 + t) * D + d] = x;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) r[cc] += x * wg[d * 4 + cc];
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) r[cc] = warp_sum(r[cc]) + gbias[h * 4 + cc];
+    if (lane == 0) {
+      const int64_t o = row(u, T, t0 + t);
+      kn[o] = nrm;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) raw4[o * 4 + cc] = r[cc];
+      gates[o * 4 + 0] = pos_none ? 0.f : -fminf(softplus(r[0]), 10.f);
+      gates[o * 4 + 1] = beta_max * sigmoid(r[1]);
+      gates[o * 4 + 2] = pos_none ? 0.f : -fminf(softplus(r[2]), 10.f);
+      gates[o * 4 + 3] = beta_max * sigmoid(r[3]);
+    }
+  }
+  __syncthreads();
+  // slot = k C^T
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, true>(acc, Kb, ld16(D), Cb, ld16(D), m0, n0, D);
+    acc.each(m0, n0, [&](int t, int m, float& v) {
+      St[t * M + m] = v;
+      if (t < c) slot[row(u, T, t0 + t) * M + m] = v;
+    });
+  });
+  __syncthreads();
+  for (int t = warp; t < c; t += nw) {
+    float x[kMaxPerLane];
+    load_vec(x, St + t * M, M);
+    const float nrm = warp_norm(x, M);
+    const float inv = 1.f / fmaxf(nrm, kUnitEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= inv;
+    store_vec(ns + row(u, T, t0 + t) * M, x, M);
+    if (lane == 0) sn[row(u, T, t0 + t)] = nrm;
+  }
+}
+
+// ------------------------------------------------------------------ post
+
+GPA_DEV const float* frozen_at(const float* bnd, const float* fz, int u, int n, int nb, int post,
+                               int64_t sz) {
+  if (n == 0 && fz) return fz + (int64_t)u * sz;
+  return bnd + ((int64_t)u * (nb + 1) + n + post) * sz;
+}
+
+struct LPost {
+  size_t Af, Bf, Nk, Wf, Wb, total;
+  __host__ __device__ LPost(int D, int Dv, int M) {
+    Carve c;
+    Af = c.take(2 * D * ld16(M));
+    Bf = c.take(2 * M * ld16(Dv));
+    Nk = c.take(2 * R * ld16(D));
+    Wf = c.take(4 * R * M);
+    Wb = c.take(2 * R * ld16(M));
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_level_post(
+    int U, Blocks bl, int post, int H, int D, int Dv, int M, int with_residual, const float* nk,
+    const float* key, const float* val, const float* Abnd, const float* Bbnd, const float* fzA,
+    const float* fzB, const float* residual_raw, int j, float* write, float* bsum,
+    float* key_next, float* val_next) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LPost L(D, Dv, M);
+  bf16* Af = (bf16*)(smem + L.Af);
+  bf16* Bf = (bf16*)(smem + L.Bf);
+  bf16* Nk = (bf16*)(smem + L.Nk);
+  float* Wf = (float*)(smem + L.Wf);
+  bf16* Wb = (bf16*)(smem + L.Wb);
+  const int lm = ld16(M), ld = ld16(D), lv = ld16(Dv);
+  tile_to_bf16(Af, lm, frozen_at(Abnd, fzA, u, n, bl.nb, post, (int64_t)D * M), M, D, M, D);
+  if (with_residual)
+    tile_to_bf16(Bf, lv, frozen_at(Bbnd, fzB, u, n, bl.nb, post, (int64_t)M * Dv), Dv, M, Dv, M);
+  tile_to_bf16(Nk, ld, nk + row(u, T, t0) * D, D, c, D, R);
+  __syncthreads();
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Nk, ld, Af, lm, m0, n0, D);
+    acc.each(m0, n0, [&](int t, int m, float& v) { Wf[t * M + m] = v; });
+  });
+  __syncthreads();
+  for (int t = warp; t < R; t += nw) {
+    float x[kMaxPerLane];
+    if (t < c) {
+      load_vec(x, Wf + t * M, M);
+      warp_softmax(x, M);
+      store_vec(write + row(u, T, t0 + t) * M, x, M);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) x[i] = 0.f;
+    }
+    store_vec(Wf + t * M, x, M);
+    store_bf16_row(Wb + t * lm, x, M);
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float s = 0.f;
+    for (int t = 0; t < c; ++t) s += Wf[t * M + m];
+    bsum[((int64_t)u * bl.nb + n) * M + m] = s;
+  }
+  if (!with_residual) return;
+  const float ek = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 0]);
+  const float ev = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 1]);
+  // rk = write A_f^T, key_{j+1} = key - ek rk
+  tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, true>(acc, Wb, lm, Af, lm, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int d, float& v) {
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * D + d;
+        key_next[o] = key[o] - ek * v;
+      }
+    });
+  });
+  // rv = write B_f, val_{j+1} = val - ev rv
+  tiles_n<1, 2>(R, Dv, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Wb, lm, Bf, lv, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int vv, float& v) {
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * Dv + vv;
+        val_next[o] = val[o] - ev * v;
+      }
+    });
+  });
+}
+
+// ------------------------------------------------------------------ bridge
+
+struct LBridge {
+  size_t Rf, ARQ, Hb, Wbuf, Of, total;
+  __host__ __device__ LBridge(int D, int M, int) {
+    Carve c;
+    Rf = c.take(4 * R * M);
+    ARQ = c.take(2 * R * ld16(M + D));
+    Hb = c.take(2 * R * ld16(2 * M));
+    const size_t w1 = 2 * M * ld16(2 * M), w2 = 2 * (2 * M) * ld16(M), w3 = 2 * (M + D) * ld16(M);
+    size_t w = w1 > w2 ? w1 : w2;
+    w = w > w3 ? w : w3;
+    Wbuf = c.take(w);
+    Of = c.take(4 * R * M);
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_bridge(
+    int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
+    const float* relation_gain, const float* route_up, const float* route_down,
+    const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
+    const float* logits, const float* qf, float* r_out, float* hp_out, float* mlp_out,
+    float* route_out, float* qoh, float* qon) {
+  const int ntile = (T + R - 1) / R;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * R;
+  const int c = min(R, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBridge Lb(D, M, 0);
+  float* Rf = (float*)(smem + Lb.Rf);
+  bf16* ARQ = (bf16*)(smem + Lb.ARQ);  // [route bf16 | q bf16]
+  bf16* Hb = (bf16*)(smem + Lb.Hb);
+  bf16* Wbuf = (bf16*)(smem + Lb.Wbuf);
+  float* Of = (float*)(smem + Lb.Of);
+  const int la = ld16(M + D), lh = ld16(2 * M), lm = ld16(M);
+  float w[kMaxIn];
+  edge_weights(in, edge_logits, H, h, w);
+  const float rg = relation_gain[j * H + h];
+  for (int t = warp; t < R; t += nw) {
+    float x[kMaxPerLane];
+    if (t < c) {
+      const int64_t o = row(u, T, t0 + t);
+      reader_row_fwd(x, o, M, in, w, rg, logits);
+      store_vec(r_out + o * M, x, M);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) x[i] = 0.f;
+    }
+    store_vec(Rf + t * M, x, M);
+    store_bf16_row(ARQ + t * la, x, M);
+  }
+  tile_to_bf16(ARQ + M, la, qf + row(u, T, t0) * D, D, c, D, R);
+  tile_to_bf16(Wbuf, lh, route_up + (int64_t)h * M * 2 * M, 2 * M, M, 2 * M, M);
+  __syncthreads();
+  // hp = r U ; hidden = gelu(hp)
+  tiles_n<1, 2>(R, 2 * M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, ARQ, la, Wbuf, lh, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int rr, float& v) {
+      if (t < c) hp_out[row(u, T, t0 + t) * 2 * M + rr] = v;
+      Hb[t * lh + rr] = __float2bfloat16(gelu(v));
+    });
+  });
+  __syncthreads();
+  tile_to_bf16(Wbuf, lm, route_down + (int64_t)h * 2 * M * M, M, 2 * M, M, 2 * M);
+  __syncthreads();
+  const float mg = route_mlp_gain[j * H + h];
+  // mlp = hidden D ; route = r + mg mlp
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Hb, lh, Wbuf, lm, m0, n0, 2 * M);
+    acc.each(m0, n0, [&](int t, int m, float& v) {
+      const float route = Rf[t * M + m] + mg * v;
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * M + m;
+        mlp_out[o] = v;
+        route_out[o] = route;
+      }
+      ARQ[t * la + m] = __float2bfloat16(route);
+    });
+  });
+  __syncthreads();
+  tile_to_bf16(Wbuf, lm, Wrs + (int64_t)h * M * M, M, M, M, M);
+  tile_to_bf16(Wbuf + M * lm, lm, Wqs + (int64_t)h * D * M, M, D, M, D, qs);
+  __syncthreads();
+  // qo = route W_rs + qs q W_qs
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, ARQ, la, Wbuf, lm, m0, n0, M + D);
+    acc.each(m0, n0, [&](int t, int m, float& v) { Of[t * M + m] = v; });
+  });
+  __syncthreads();
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float x[kMaxPerLane];
+    load_vec(x, Of + t * M, M);
+    const float a = warp_norm(x, M);
+    const float ia = 1.f / fmaxf(a, kUnitEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
+    store_vec(qoh + o * M, x, M);
+    if ((threadIdx.x & 31) == 0) qon[o] = a;
+  }
+}
+
+struct LBridgeBwd {
+  size_t Qb, Ql, Rf, Rb, Hb, Hl, Wbuf, red, total;
+  __host__ __device__ LBridgeBwd(int D, int M, int) {
+    Carve c;
+    Qb = c.take(2 * R * ld16(M));
+    Ql = c.take(2 * R * ld16(M));
+    Rf = c.take(4 * R * M);
+    Rb = c.take(2 * R * ld16(M));
+    Hb = c.take(2 * R * ld16(2 * M));
+    Hl = c.take(2 * R * ld16(2 * M));
+    const size_t w1 = 2 * (M + D) * ld16(M), w2 = 2 * (2 * M) * ld16(M), w3 = 2 * M * ld16(2 * M);
+    size_t w = w1 > w2 ? w1 : w2;
+    w = w > w3 ? w : w3;
+    Wbuf = c.take(w);
+    red = c.take(4 * 32);
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_bridge_bwd(
+    int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
+    const float* relation_gain, const float* route_up, const float* route_down,
+    const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
+    const float* logits, const float* r_in, const float* hp, const float* mlp, const float* qoh,
+    const float* qon, const float* dqoh, float* dqo_out, float* droute_out, float* dhp_out,
+    float* dlogits, float* dq_direct, double* scal, double* scalE, int E) {
+  const int ntile = (T + R - 1) / R;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * R;
+  const int c = min(R, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LBridgeBwd Lb(D, M, 0);
+  bf16* Qb = (bf16*)(smem + Lb.Qb);
+  bf16* Ql = (bf16*)(smem + Lb.Ql);
+  float* Rf = (float*)(smem + Lb.Rf);
+  bf16* Rb = (bf16*)(smem + Lb.Rb);
+  bf16* Hb = (bf16*)(smem + Lb.Hb);
+  bf16* Hl = (bf16*)(smem + Lb.Hl);
+  bf16* Wbuf = (bf16*)(smem + Lb.Wbuf);
+  float* red = (float*)(smem + Lb.red);
+  const int lm = ld16(M), lh = ld16(2 * M);
+  for (int t = warp; t < R; t += nw) {
+    float dx[kMaxPerLane];
+    if (t < c) {
+      const int64_t o = row(u, T, t0 + t);
+      float y[kMaxPerLane], dy[kMaxPerLane];
+      load_vec(y, qoh + o * M, M);
+      load_vec(dy, dqoh + o * M, M);
+      unit_bwd(dx, y, dy, qon[o], M);
+      store_vec(dqo_out + o * M, dx, M);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) dx[i] = 0.f;
+    }
+    store_split_row(Qb + t * lm, Ql + t * lm, dx, M);
+  }
+  tile_to_bf16(Wbuf, lm, Wrs + (int64_t)h * M * M, M, M, M, M);
+  tile_to_bf16(Wbuf + M * lm, lm, Wqs + (int64_t)h * D * M, M, D, M, D, qs);
+  __syncthreads();
+  // droute = dqo W_rs^T
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, true>(acc, Qb, Ql, lm, Wbuf, nullptr, lm, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int m, float& v) {
+      Rf[t * M + m] = v;
+      Rb[t * lm + m] = __float2bfloat16(v);
+      if (t < c) droute_out[row(u, T, t0 + t) * M + m] = v;
+    });
+  });
+  // dq_direct += qs dqo W_qs^T
+  tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, true>(acc, Qb, Ql, lm, Wbuf + M * lm, nullptr, lm, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int d, float& v) {
+      if (t < c) dq_direct[row(u, T, t0 + t) * D + d] += v;
+    });
+  });
+  __syncthreads();
+  {
+    float part = 0.f;
+    for (int i = threadIdx.x; i < c * M; i += blockDim.x) {
+      const int t = i / M, m = i - t * M;
+      part += Rf[i] * mlp[row(u, T, t0 + t) * M + m];
+    }
+    const float s = block_sum(part, red);
+    if (threadIdx.x == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_MlpGain], (double)s);
+  }
+  tile_to_bf16(Wbuf, lm, route_down + (int64_t)h * 2 * M * M, M, 2 * M, M, 2 * M);
+  __syncthreads();
+  const float mg = route_mlp_gain[j * H + h];
+  // dhp = mg (droute D^T) o gelu'(hp)
+  tiles_n<1, 2>(R, 2 * M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, true>(acc, Rb, lm, Wbuf, lm, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int rr, float& v) {
+      float x = 0.f;
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * 2 * M + rr;
+        x = mg * v * gelu_grad(hp[o]);
+        dhp_out[o] = x;
+      }
+      tc::split_bf16(x, Hb + t * lh + rr, Hl + t * lh + rr);
+    });
+  });
+  __syncthreads();
+  tile_to_bf16(Wbuf, lh, route_up + (int64_t)h * M * 2 * M, 2 * M, M, 2 * M, M);
+  __syncthreads();
+  // dr = droute + dhp U^T
+  tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    tc::mma_acc3<1, NI, false, true>(acc, Hb, Hl, lh, Wbuf, nullptr, lh, m0, n0, 2 * M);
+    acc.each(m0, n0, [&](int t, int m, float& v) { Rf[t * M + m] += v; });
+  });
+  __syncthreads();
+  float w[kMaxIn];
+  edge_weights(in, edge_logits, H, h, w);
+  const float rg = relation_gain[j * H + h];
+  float rg_acc = 0.f, ew_acc[kMaxIn];
+  for (int a = 0; a < kMaxIn; ++a) ew_acc[a] = 0.f;
+  for (int t = warp; t < c; t += nw) {
+    const int64_t o = row(u, T, t0 + t);
+    float r[kMaxPerLane], dr[kMaxPerLane], db[kMaxPerLane];
+    load_vec(r, r_in + o * M, M);
+    load_vec(dr, Rf + t * M, M);
+    reader_row_bwd(db, r, dr, o, M, in, w, rg, rg_acc, ew_acc);
+    store_vec(dlogits + o * M, db, M);
+  }
+  if (lane == 0 && in.n > 0) {
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], (double)rg_acc);
+    for (int a = 0; a < in.n; ++a)
+      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], (double)ew_acc[a]);
+  }
+}
+
+// ------------------------------------------------------------- post backward
+
+struct LPostBwd {
+  size_t Af, Bf, Wb, Wf, dWf, dKb, dVb, Nk, dLb, red, total;
+  __host__ __device__ LPostBwd(int D, int Dv, int M) {
+    Carve c;
+    Af = c.take(2 * D * ld16(M));
+    Bf = c.take(2 * M * ld16(Dv));
+    Wb = c.take(2 * R * ld16(M));
+    Wf = c.take(4 * R * M);
+    dWf = c.take(4 * R * M);
+    dKb = c.take(2 * R * ld16(D));
+    dVb = c.take(2 * R * ld16(Dv));
+    Nk = c.take(2 * R * ld16(D));
+    dLb = c.take(2 * R * ld16(M));
+    red = c.take(4 * 34);
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_post_bwd(
+    int U, Blocks bl, int post, int offset, int H, int D, int Dv, int M, int L, int j,
+    int with_residual, const float* nk, const float* write, const float* Abnd, const float* Bbnd,
+    const float* fzA, const float* fzB, const float* residual_raw, const float* dkey,
+    const float* dval, float* dwrite, float* dnk, float* extA, float* extB, float* dfzA,
+    float* dfzB, double* scal) {
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LPostBwd Lp(D, Dv, M);
+  bf16* Af = (bf16*)(smem + Lp.Af);
+  bf16* Bf = (bf16*)(smem + Lp.Bf);
+  bf16* Wb = (bf16*)(smem + Lp.Wb);
+  float* Wf = (float*)(smem + Lp.Wf);
+  float* dWf = (float*)(smem + Lp.dWf);
+  bf16* dKb = (bf16*)(smem + Lp.dKb);
+  bf16* dVb = (bf16*)(smem + Lp.dVb);
+  bf16* Nk = (bf16*)(smem + Lp.Nk);
+  bf16* dLb = (bf16*)(smem + Lp.dLb);
+  float* red = (float*)(smem + Lp.red);
+  const int lm = ld16(M), ld = ld16(D), lv = ld16(Dv);
+  const bool fz0 = (n == 0 && offset != 0);
+  const float ek = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 0]);
+  const float ev = 1.f + .25f * tanhf(residual_raw[(j * H + h) * 2 + 1]);
+  tile_to_bf16(Af, lm, frozen_at(Abnd, fz0 ? fzA : nullptr, u, n, bl.nb, post, (int64_t)D * M), M,
+               D, M, D);
+  tile_to_bf16(Wb, lm, write + row(u, T, t0) * M, M, c, M, R);
+  tile_to_bf16(Nk, ld, nk + row(u, T, t0) * D, D, c, D, R);
+  for (int i = threadIdx.x; i < R * M; i += blockDim.x) {
+    const int t = i / M, m = i - t * M;
+    const int64_t o = row(u, T, t0 + t) * M + m;
+    Wf[i] = t < c ? write[o] : 0.f;
+    dWf[i] = t < c ? dwrite[o] : 0.f;
+  }
+  if (with_residual) {
+    tile_to_bf16(Bf, lv, frozen_at(Bbnd, fz0 ? fzB : nullptr, u, n, bl.nb, post, (int64_t)M * Dv),
+                 Dv, M, Dv, M);
+    tile_to_bf16(dKb, ld, dkey + row(u, T, t0) * D, D, c, D, R, -ek);
+    tile_to_bf16(dVb, lv, dval + row(u, T, t0) * Dv, Dv, c, Dv, R, -ev);
+  }
+  if (threadIdx.x < 34) red[threadIdx.x] = 0.f;
+  __syncthreads();
+  if (with_residual) {
+    // d eta_k = -sum dk . (write A_f^T) ; d eta_v = -sum dv . (write B_f)
+    float pk = 0.f, pv = 0.f;
+    tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      mma_acc<1, NI, false, true>(acc, Wb, lm, Af, lm, m0, n0, M);
+      acc.each(m0, n0, [&](int t, int d, float& v) {
+        if (t < c) pk += v * dkey[row(u, T, t0 + t) * D + d];
+      });
+    });
+    tiles_n<1, 2>(R, Dv, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      mma_acc<1, NI, false, false>(acc, Wb, lm, Bf, lv, m0, n0, M);
+      acc.each(m0, n0, [&](int t, int vv, float& v) {
+        if (t < c) pv += v * dval[row(u, T, t0 + t) * Dv + vv];
+      });
+    });
+    pk = warp_sum(pk);
+    pv = warp_sum(pv);
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(&red[32], pk);
+      atomicAdd(&red[33], pv);
+    }
+    // dW += (-ek dk) A_f + (-ev dv) B_f^T
+    tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.each(m0, n0, [&](int t, int m, float& v) { v = dWf[t * M + m]; });
+      mma_acc<1, NI, false, false>(acc, dKb, ld, Af, lm, m0, n0, D);
+      mma_acc<1, NI, false, true>(acc, dVb, lv, Bf, lv, m0, n0, Dv);
+      acc.each(m0, n0, [&](int t, int m, float& v) { dWf[t * M + m] = v; });
+    });
+  }
+  __syncthreads();
+  if (with_residual && threadIdx.x == 0) {
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaK], -(double)red[32]);
+    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaV], -(double)red[33]);
+  }
+  for (int t = warp; t < R; t += nw) {
+    float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+    load_vec(y, Wf + t * M, M);
+    load_vec(dy, dWf + t * M, M);
+    softmax_bwd(dx, y, dy, M);
+    store_bf16_row(dLb + t * lm, dx, M);
+  }
+  __syncthreads();
+  // dnk = dlw A_f^T
+  tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, true>(acc, dLb, lm, Af, lm, m0, n0, M);
+    acc.each(m0, n0, [&](int t, int d, float& v) {
+      if (t < c) dnk[row(u, T, t0 + t) * D + d] = v;
+    });
+  });
+  float* ta = fz0 ? dfzA + (int64_t)u * D * M
+                  : extA + ((int64_t)u * (bl.nb + 1) + n + post) * D * M;
+  float* tb = fz0 ? dfzB + (int64_t)u * M * Dv
+                  : extB + ((int64_t)u * (bl.nb + 1) + n + post) * M * Dv;
+  // dA_f += nk^T dlw + (-ek dk)^T write
+  tiles_n<1, 2>(D, M, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, true, false>(acc, Nk, ld, dLb, lm, m0, n0, R);
+    if (with_residual) mma_acc<1, NI, true, false>(acc, dKb, ld, Wb, lm, m0, n0, R);
+    acc.each(m0, n0, [&](int d, int m, float& v) { ta[d * M + m] += v; });
+  });
+  if (with_residual) {
+    // dB_f += write^T (-ev dv)
+    tiles_n<1, 2>(M, Dv, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      mma_acc<1, NI, true, false>(acc, Wb, lm, dVb, lv, m0, n0, R);
+      acc.each(m0, n0, [&](int m, int vv, float& v) { tb[m * Dv + vv] += v; });
+    });
+  }
+}
+
+// ------------------------------------------------------------- prep backward
+
+struct LPrepBwd {
+  size_t Dsb, Cb, total;
+  __host__ __device__ LPrepBwd(int D, int M, int) {
+    Carve c;
+    Dsb = c.take(2 * R * ld16(M));
+    Cb = c.take(2 * M * ld16(D));
+    total = c.off;
+  }
+};
+
+__global__ void __launch_bounds__(256) tk_prep_bwd(int U, int T, int H, int D, int M,
+                                                   const float* C, const float* Wg,
+                                                   float beta_max, int pos_none, const float* raw4,
+                                                   const float* nk, const float* kn,
+                                                   const float* ns, const float* sn,
+                                                   const float* dgates, const float* dnk,
+                                                   const float* dns, float* dslot, float* d4out,
+                                                   float* dkey) {
+  const int ntile = (T + R - 1) / R;
+  const int u = blockIdx.x / ntile, t0 = (blockIdx.x % ntile) * R;
+  const int c = min(R, T - t0), h = u % H;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LPrepBwd Lp(D, M, 0);
+  bf16* Dsb = (bf16*)(smem + Lp.Dsb);
+  bf16* Cb = (bf16*)(smem + Lp.Cb);
+  const int lm = ld16(M);
+  tile_to_bf16(Cb, ld16(D), C + (int64_t)h * M * D, D, M, D, M);
+  const float* wg = Wg + (int64_t)h * D * 4;
+  for (int t = warp; t < R; t += nw) {
+    float base[kMaxPerLane];
+    if (t < c) {
+      const int64_t o = row(u, T, t0 + t);
+      float d4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float* r4 = raw4 + o * 4;
+      const float* dg = dgates + o * 4;
+      if (!pos_none) {
+        if (softplus(r4[0]) <= 10.f) d4[0] = -dg[0] * sigmoid(r4[0]);
+        if (softplus(r4[2]) <= 10.f) d4[2] = -dg[2] * sigmoid(r4[2]);
+      }
+      const float s1 = sigmoid(r4[1]), s3 = sigmoid(r4[3]);
+      d4[1] = dg[1] * beta_max * s1 * (1.f - s1);
+      d4[3] = dg[3] * beta_max * s3 * (1.f - s3);
+      if (lane < 4) d4out[o * 4 + lane] = d4[lane];
+      float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+      load_vec(y, ns + o * M, M);
+      load_vec(dy, dns + o * M, M);
+      unit_bwd(dx, y, dy, sn[o], M);
+      load_vec(base, dslot + o * M, M);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) base[i] += dx[i];
+      store_vec(dslot + o * M, base, M);
+      float a[kMaxPerLane], da[kMaxPerLane], dkx[kMaxPerLane];
+      load_vec(a, nk + o * D, D);
+      load_vec(da, dnk + o * D, D);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D)
+          da[i] += d4[0] * wg[d * 4] + d4[1] * wg[d * 4 + 1] + d4[2] * wg[d * 4 + 2] +
+                   d4[3] * wg[d * 4 + 3];
+      }
+      unit_bwd(dkx, a, da, kn[o], D);
+      float cur[kMaxPerLane];
+      load_vec(cur, dkey + o * D, D);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) cur[i] += dkx[i];
+      store_vec(dkey + o * D, cur, D);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) base[i] = 0.f;
+    }
+    store_bf16_row(Dsb + t * lm, base, M);
+  }
+  __syncthreads();
+  // dkey += dslot C
+  tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
+    Acc<1, NI> acc;
+    acc.zero();
+    mma_acc<1, NI, false, false>(acc, Dsb, lm, Cb, ld16(D), m0, n0, M);
+    acc.each(m0, n0, [&](int t, int d, float& v) {
+      if (t < c) dkey[row(u, T, t0 + t) * D + d] += v;
+    });
+  });
+}
+
+// -------------------------------------------- parameter-gradient reductions
+
+constexpr int kOTile = 64;     // output tile (P and Q)
+constexpr int kORows = 64;     // token rows per step
+constexpr int kOSplit = 4096;  // tokens per CTA
+
+struct LOuter {
+  size_t Xh, Xl, Yh, Yl, total;
+  __host__ __device__ LOuter(int, int, int) {
+    Carve c;
+    Xh = c.take(2 * kORows * ld16(kOTile));
+    Xl = c.take(2 * kORows * ld16(kOTile));
+    Yh = c.take(2 * kORows * ld16(kOTile));
+    Yl = c.take(2 * kORows * ld16(kOTile));
+    total = c.off;
+  }
+};
+
+// out[h] (P x Q) += cscale * scale[h] * sum_{b,t} X^T Y over the rows of head h; P, Q
+// multiples of 16.  Operands are hi/lo bf16 pairs (sums run over every token).
+__global__ void __launch_bounds__(256) tk_head_outer(int B, int T, int H, const float* X, int P,
+                                                     int xmode, const float* Y, int Q,
+                                                     const float* scale, int64_t scale_stride,
+                                                     float cscale, float* out) {
+  const int h = blockIdx.x;
+  const int tq = (Q + kOTile - 1) / kOTile;
+  const int p0 = (blockIdx.y / tq) * kOTile, q0 = (blockIdx.y % tq) * kOTile;
+  const int pw = min(kOTile, P - p0), qw = min(kOTile, Q - q0);
+  const int64_t total = (int64_t)B * T;
+  const int64_t r0 = (int64_t)blockIdx.z * kOSplit;
+  const int64_t r1 = min(total, r0 + kOSplit);
+  extern __shared__ __align__(16) unsigned char smem[];
+  const LOuter Lo(0, 0, 0);
+  bf16* Xh = (bf16*)(smem + Lo.Xh);
+  bf16* Xl = (bf16*)(smem + Lo.Xl);
+  bf16* Yh = (bf16*)(smem + Lo.Yh);
+  bf16* Yl = (bf16*)(smem + Lo.Yl);
+  const int lo = ld16(kOTile);
+  // the 64x64 output tile is 16 16x16 tiles; warp w owns tiles w and w + 8
+  const int w = threadIdx.x >> 5;
+  Acc<1, 1> acc[2];
+  int tm[2], tn[2];
+  bool act[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int idx = w + 8 * i;
+    tm[i] = (idx >> 2) * 16;
+    tn[i] = (idx & 3) * 16;
+    act[i] = tm[i] < pw && tn[i] < qw;
+    acc[i].zero();
+  }
+  for (int64_t rr = r0; rr < r1; rr += kORows) {
+    const int rows = (int)min((int64_t)kORows, r1 - rr);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kORows * (kOTile / 4); i += blockDim.x) {
+      const int rw = i / (kOTile / 4), cc = (i % (kOTile / 4)) * 4;
+      float4 xv = make_float4(0.f, 0.f, 0.f, 0.f), yv = xv;
+      if (rw < rows) {
+        const int64_t g = rr + rw;
+        const int b = (int)(g / T), t = (int)(g - (int64_t)b * T);
+        const int64_t o = row(b * H + h, T, t);
+        if (cc < pw) {
+          xv = *reinterpret_cast<const float4*>(X + o * P + p0 + cc);
+          if (xmode == 1) {
+            xv.x = gelu(xv.x);
+            xv.y = gelu(xv.y);
+            xv.z = gelu(xv.z);
+            xv.w = gelu(xv.w);
+          }
+        }
+        if (cc < qw) yv = *reinterpret_cast<const float4*>(Y + o * Q + q0 + cc);
+      }
+      tc::put4(Xh, Xl, rw * lo + cc, xv);
+      tc::put4(Yh, Yl, rw * lo + cc, yv);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      if (act[i])
+        tc::mma_acc3<1, 1, true, false>(acc[i], Xh, Xl, lo, Yh, Yl, lo, tm[i], tn[i], kORows);
+  }
+  const float s = cscale * (scale ? scale[(int64_t)h * scale_stride] : 1.f);
+  float* o = out + (int64_t)h * P * Q;
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (act[i])
+      acc[i].each(tm[i], tn[i], [&](int p, int q, float& v) {
+        atomicAdd(&o[(p0 + p) * Q + q0 + q], s * v);
+      });
+}
+
+template <class Kern, class... Args>
+cudaError_t tk_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStream_t st,
+                      Args... args) {
+  if (grid.x == 0 || grid.y == 0 || grid.z == 0) return cudaSuccess;
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  Launch scope(name, st);
+  k<<<grid, 256, smem, st>>>(args...);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t tc_level_prep(int U, int T, int H, int D, int M, const float* key, const float* C,
+                          const float* Wg, const float* gbias, float beta_max, int pos_none,
+                          float* nk, float* kn, float* slot, float* ns, float* sn, float* raw4,
+                          float* gates, cudaStream_t st) {
+  const int ntile = (T + R - 1) / R;
+  return tk_launch("tc_level_prep", tk_level_prep, dim3(U * ntile), smem_of<LPrep>(D, M, 0), st,
+                   U, T, H, D, M, key, C, Wg, gbias, beta_max, pos_none, nk, kn, slot, ns, sn,
+                   raw4, gates);
+}
+
+cudaError_t tc_level_post(int U, const Blocks& bl, int post, int H, int D, int Dv, int M,
+                          int with_residual, const float* nk, const float* key, const float* val,
+                          const float* Abnd, const float* Bbnd, const float* fzA, const float* fzB,
+                          const float* residual_raw, int j, float* write, float* bsum,
+                          float* key_next, float* val_next, cudaStream_t st) {
+  return tk_launch("tc_level_post", tk_level_post, dim3(U * bl.nb), smem_of<LPost>(D, Dv, M), st,
+                   U, bl, post, H, D, Dv, M, with_residual, nk, key, val, Abnd, Bbnd, fzA, fzB,
+                   residual_raw, j, write, bsum, key_next, val_next);
+}
+
+cudaError_t tc_bridge(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                      const float* edge_logits, const float* relation_gain, const float* route_up,
+                      const float* route_down, const float* route_mlp_gain, const float* Wrs,
+                      const float* Wqs, float qs, const float* logits, const float* qf, float* r,
+                      float* hp, float* mlp, float* route, float* qoh, float* qon,
+                      cudaStream_t st) {
+  const int ntile = (T + R - 1) / R;
+  return tk_launch("tc_bridge", tk_bridge, dim3(U * ntile), smem_of<LBridge>(D, M, 0), st, U, T,
+                   H, D, M, L, j, in, edge_logits, relation_gain, route_up, route_down,
+                   route_mlp_gain, Wrs, Wqs, qs, logits, qf, r, hp, mlp, route, qoh, qon);
+}
+
+cudaError_t tc_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
+                          const float* edge_logits, const float* relation_gain,
+                          const float* route_up, const float* route_down,
+                          const float* route_mlp_gain, const float* Wrs, const float* Wqs,
+                          float qs, const float* logits, const float* r, const float* hp,
+                          const float* mlp, const float* qoh, const float* qon, const float* dqoh,
+                          float* dqo, float* droute, float* dhp, float* dlogits, float* dq_direct,
+                          double* scal, double* scalE, int E, cudaStream_t st) {
+  const int ntile = (T + R - 1) / R;
+  return tk_launch("tc_bridge_bwd", tk_bridge_bwd, dim3(U * ntile), smem_of<LBridgeBwd>(D, M, 0),
+                   st, U, T, H, D, M, L, j, in, edge_logits, relation_gain, route_up, route_down,
+                   route_mlp_gain, Wrs, Wqs, qs, logits, r, hp, mlp, qoh, qon, dqoh, dqo, droute,
+                   dhp, dlogits, dq_direct, scal, scalE, E);
+}
+
+cudaError_t tc_post_bwd(int U, const Blocks& bl, int post, int offset, int H, int D, int Dv,
+                        int M, int L, int j, int with_residual, const float* nk,
+                        const float* write, const float* Abnd, const float* Bbnd,
+                        const float* fzA, const float* fzB, const float* residual_raw,
+                        const float* dkey, const float* dval, float* dwrite, float* dnk,
+                        float* extA, float* extB, float* dfzA, float* dfzB, double* scal,
+                        cudaStream_t st) {
+  return tk_launch("tc_post_bwd", tk_post_bwd, dim3(U * bl.nb), smem_of<LPostBwd>(D, Dv, M), st,
+                   U, bl, post, offset, H, D, Dv, M, L, j, with_residual, nk, write, Abnd, Bbnd,
+                   fzA, fzB, residual_raw, dkey, dval, dwrite, dnk, extA, extB, dfzA, dfzB, scal);
+}
+
+cudaError_t tc_prep_bwd(int U, int T, int H, int D, int M, const float* C, const float* Wg,
+                        float beta_max, int pos_none, const float* raw4, const float* nk,
+                        const float* kn, const float* ns, const float* sn, const float* dgates,
+                        const float* dnk, const float* dns, float* dslot, float* d4, float* dkey,
+                        cudaStream_t st) {
+  const int ntile = (T + R - 1) / R;
+  return tk_launch("tc_prep_bwd", tk_prep_bwd, dim3(U * ntile), smem_of<LPrepBwd>(D, M, 0), st, U,
+                   T, H, D, M, C, Wg, beta_max, pos_none, raw4, nk, kn, ns, sn, dgates, dnk, dns,
+                   dslot, d4, dkey);
+}
+
+cudaError_t tc_head_outer(int B, int T, int H, const float* X, int P, int xmode, const float* Y,
+                          int Q, const float* scale, int64_t scale_stride, float cscale,
+                          float* out, cudaStream_t st) {
+  const int64_t total = (int64_t)B * T;
+  const int tp = (P + kOTile - 1) / kOTile, tq = (Q + kOTile - 1) / kOTile;
+  dim3 grid(H, tp * tq, (unsigned)((total + kOSplit - 1) / kOSplit));
+  return tk_launch("tc_head_outer", tk_head_outer, grid, smem_of<LOuter>(0, 0, 0), st, B, T, H,
+                   X, P, xmode, Y, Q, scale, scale_stride, cscale, out);
+}
+
+}  // namespace gpa

@@ -1,0 +1,214 @@
+// Per-row (one warp per token row) helpers of the level kernels: vectors of up
+// to 256 values held lane-strided in registers.
+#pragma once
+#include "level.cuh"
+
+namespace gpa {
+namespace {
+
+constexpr int kRowsPerTile = 64;
+constexpr int kMaxPerLane = 8;  // vectors up to 256 long per warp row
+
+GPA_DEV int64_t row(int u, int T, int t) { return (int64_t)u * T + t; }
+
+// softmax over the lane-strided vector x[0..n) held in registers
+GPA_DEV void warp_softmax(float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) mx = fmaxf(mx, x[i]);
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) {
+      x[i] = __expf(x[i] - mx);
+      s += x[i];
+    }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) x[i] *= inv;
+}
+
+GPA_DEV float warp_norm(const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) s += x[i] * x[i];
+  return sqrtf(warp_sum(s));
+}
+
+GPA_DEV float warp_dot(const float (&x)[kMaxPerLane], const float (&y)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) s += x[i] * y[i];
+  return warp_sum(s);
+}
+
+GPA_DEV void load_vec(float (&x)[kMaxPerLane], const float* p, int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) x[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
+}
+
+GPA_DEV void store_vec(float* p, const float (&x)[kMaxPerLane], int n) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < n) p[lane + 32 * i] = x[i];
+}
+
+// unit-normalisation backward: y = x / max(|x|, eps)
+GPA_DEV void unit_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
+                      const float (&dy)[kMaxPerLane], float nrm, int n) {
+  if (nrm > kUnitEps) {
+    const float yd = warp_dot(y, dy, n);
+    const float inv = 1.f / nrm;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = (dy[i] - y[i] * yd) * inv;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = dy[i] / kUnitEps;
+  }
+}
+
+GPA_DEV void softmax_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
+                         const float (&dy)[kMaxPerLane], int n) {
+  const float yd = warp_dot(y, dy, n);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) dx[i] = y[i] * (dy[i] - yd);
+}
+
+GPA_DEV float block_sum(float x, float* red) {
+  x = warp_sum(x);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+  }
+  return s;  // valid in warp 0
+}
+
+// softmax over the incoming edges' logits for head h
+GPA_DEV void edge_weights(const BridgeIn& in, const float* edge_logits, int H, int h,
+                          float* w) {
+  float mx = -INFINITY;
+  for (int a = 0; a < in.n; ++a) mx = fmaxf(mx, edge_logits[in.edge[a] * H + h]);
+  float s = 0.f;
+  for (int a = 0; a < in.n; ++a) {
+    w[a] = __expf(edge_logits[in.edge[a] * H + h] - mx);
+    s += w[a];
+  }
+  for (int a = 0; a < in.n; ++a) w[a] /= s;
+}
+
+// Dense reader forward of one token row (one warp): base <- softmax(logits + rg *
+// tanh(c / sqrt(mean(c^2) + eps))), c = incoming - mean(incoming),
+// incoming = sum_e w_e msg_e  (src/gpa/attention.py:227-242).
+GPA_DEV void reader_row_fwd(float (&base)[kMaxPerLane], int64_t o, int M, const BridgeIn& in,
+                            const float* w, float rg, const float* logits) {
+  load_vec(base, logits + o * M, M);
+  if (in.n > 0) {
+    const int lane = threadIdx.x & 31;
+    float inc[kMaxPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+    for (int a = 0; a < in.n; ++a) {
+      float x[kMaxPerLane];
+      load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
+    }
+    float mean = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i < M) mean += inc[i];
+    mean = warp_sum(mean) / M;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i < M) {
+        inc[i] -= mean;
+        var += inc[i] * inc[i];
+      }
+    var = warp_sum(var) / M;
+    const float sd = rsqrtf(var + kCenterEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) base[i] += rg * tanhf(inc[i] * sd);
+  }
+  warp_softmax(base, M);
+}
+
+// Backward of reader_row_fwd: db = d(logits) of the row; writes dmsg rows;
+// accumulates the relation-gain and edge-weight partial sums (lane-uniform).
+GPA_DEV void reader_row_bwd(float (&db)[kMaxPerLane], const float (&r)[kMaxPerLane],
+                            const float (&dr)[kMaxPerLane], int64_t o, int M,
+                            const BridgeIn& in, const float* w, float rg, float& rg_acc,
+                            float (&ew_acc)[kMaxIn]) {
+  const int lane = threadIdx.x & 31;
+  softmax_bwd(db, r, dr, M);
+  if (in.n == 0) return;
+  float inc[kMaxPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+  for (int a = 0; a < in.n; ++a) {
+    float x[kMaxPerLane];
+    load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
+  }
+  float mean = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < M) mean += inc[i];
+  mean = warp_sum(mean) / M;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < M) {
+      inc[i] -= mean;
+      var += inc[i] * inc[i];
+    }
+  var = warp_sum(var) / M;
+  const float sd = rsqrtf(var + kCenterEps);
+  float dz[kMaxPerLane], rgp = 0.f, dsum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const float tz = tanhf(inc[i] * sd);
+    if (lane + 32 * i < M) rgp += db[i] * tz;
+    dz[i] = rg * db[i] * (1.f - tz * tz);
+    if (lane + 32 * i < M) dsum += dz[i] * inc[i];
+  }
+  rg_acc += warp_sum(rgp);
+  dsum = warp_sum(dsum);
+  const float dvar = dsum * -0.5f * sd * sd * sd;
+  float dmean = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    dz[i] = dz[i] * sd + dvar * 2.f * inc[i] / M;
+    if (lane + 32 * i < M) dmean += dz[i];
+  }
+  dmean = warp_sum(dmean) / M;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) dz[i] -= dmean;
+  for (int a = 0; a < in.n; ++a) {
+    float x[kMaxPerLane], dm[kMaxPerLane];
+    load_vec(x, in.msg[a] + o * M, M);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) dm[i] = w[a] * dz[i];
+    store_vec(in.dmsg[a] + o * M, dm, M);
+    ew_acc[a] += warp_dot(dz, x, M);
+  }
+}
+
+}  // namespace
+}  // namespace gpa
