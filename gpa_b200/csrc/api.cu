@@ -854,6 +854,66 @@ int gpa_b200_backward(const GpaDims* dims, const GpaParams* params, const GpaSta
                        dparams, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
+// ----------------------------------------------------- no-allocation forward
+// Scratch of gpa_b200_forward_noalloc: one file-scope device array per GPU that
+// loads this library (held until the process exits).  Host code only sees a
+// host-side stand-in under this name; the device address is looked up per
+// device with cudaGetSymbolAddress and cached.
+constexpr size_t kNoAllocBytes = size_t(64) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(GPA_B200_LAUNCH_FAILURE, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(GPA_B200_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(GPA_B200_LAUNCH_FAILURE,
+                  std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GPA_B200_OK;
+}
+}  // namespace
+
+size_t gpa_b200_noalloc_capacity(void) { return kNoAllocBytes; }
+
+int gpa_b200_forward_noalloc(const GpaDims* dims, const GpaParams* params, const void* q,
+                             const void* k, const void* v, const GpaStateRef* state_in,
+                             GpaStateRef* state_out, void* out, void* stream) {
+  g_last_error.clear();
+  Geo g;
+  std::string why;
+  int rc = make_geo(dims, &g, &why);
+  if (rc) return fail(rc, why);
+  if ((rc = check_params(g, params))) return rc;
+  if ((rc = check_state(g, state_in, g.offset != 0, "state_in"))) return rc;
+  if ((rc = check_state(g, state_out, false, "state_out"))) return rc;
+  if (g.T == 0) return fail(GPA_B200_BAD_ARGUMENT, "length must be positive (empty calls are host-side)");
+  if (!q || !k || !v || !out) return fail(GPA_B200_BAD_ARGUMENT, "q/k/v/out must not be NULL");
+  Saved sz;
+  layout_saved(g, nullptr, &sz);
+  if (sz.bytes > kNoAllocBytes)
+    return fail(GPA_B200_UNSUPPORTED,
+                "this call needs " + std::to_string(sz.bytes) + " bytes of scratch; the "
+                "no-allocation entry point holds " + std::to_string(kNoAllocBytes) +
+                " (use gpa_b200_forward with a caller buffer)");
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
+  return forward_impl(g, params, q, k, v, state_in, state_out, out, scratch, kNoAllocBytes,
+                      static_cast<cudaStream_t>(stream));
+}
+
 int gpa_b200_routes(const GpaDims* dims, const void* saved, void* const* routes, void* stream) {
   g_last_error.clear();
   Geo g;

@@ -120,6 +120,23 @@ int gpa_b200_backward(const GpaDims* dims, const GpaParams* params, const GpaSta
                       void* dq, void* dk, void* dv, GpaStateRef* dstate_in,
                       GpaParamGrads* dparams, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Forward of one call (same results as gpa_b200_forward) for callers that
+ * cannot allocate device memory: code running inside another runtime's
+ * stream capture or memory pool, or a decode loop whose memory is fixed up
+ * front.  No counterpart in the reference, which allocates through PyTorch.
+ * The workspace is a file-scope device array of gpa_b200_noalloc_capacity()
+ * bytes (64 MiB) that every GPU loading this library holds until the process
+ * exits; calls whose workspace would exceed it return GPA_B200_UNSUPPORTED.
+ * The first call on a device looks the array's address up (with that device
+ * current); make that first call before any stream capture.  Every call shares
+ * the array and overwrites all of it that it reads, so nothing needs clearing,
+ * but calls that overlap on the GPU (other streams, other threads) race.  The
+ * array is reused by the next call, so this entry point has no backward. */
+int gpa_b200_forward_noalloc(const GpaDims* dims, const GpaParams* params, const void* q,
+                             const void* k, const void* v, const GpaStateRef* state_in,
+                             GpaStateRef* state_out, void* out, void* stream);
+size_t gpa_b200_noalloc_capacity(void);
+
 /* Diagnostics: copy the per-level post-MLP routes of a forward call out of its
  * saved buffer into routes[j] ([B,T,H,M_j], input dtype).  Replaces the
  * return_diagnostics routes of DenseGPA.forward (src/gpa/attention.py:407-413). */
