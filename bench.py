@@ -207,22 +207,9 @@ def make_inputs(batch, length, seed, device="cpu", dtype=torch.bfloat16, cfg=CFG
     return [x.to(dtype).to(device) for x in (q, k, v)]
 
 
-def allreduce_grads(model, world):
-    if world == 1:
-        return
-    grads = [p.grad for p in model.parameters() if p.grad is not None]
-    flat = torch.cat([g.reshape(-1) for g in grads])
-    dist.all_reduce(flat)
-    flat /= world
-    off = 0
-    for g in grads:
-        n = g.numel()
-        g.copy_(flat[off:off + n].view_as(g))
-        off += n
-
-
 def run_b200(args, rank, world, local):
     from gpa_b200 import _lib
+    from gpa_b200.dist import allreduce_gradients
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     model = make_model(device)
@@ -237,7 +224,7 @@ def run_b200(args, rank, world, local):
         out, _ = model(q, k, v)
         loss = out.float().square().mean()
         loss.backward()
-        allreduce_grads(model, world)
+        allreduce_gradients(model)
         return loss
 
     def barrier():
@@ -280,7 +267,7 @@ def run_b200(args, rank, world, local):
         out, _ = model(*xs)
         loss = out.float().square().mean()
         loss.backward()
-        allreduce_grads(model, world)
+        allreduce_gradients(model)
         return loss.item()
 
     for _ in range(max(1, args.warmup // 2)):
