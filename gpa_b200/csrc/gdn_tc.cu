@@ -33,6 +33,7 @@ using tc::tile_to_bf16;
 using tc::tiles_n;
 
 constexpr int C = kMaxChunk;  // 64 rows per block tile (zero padded)
+constexpr int kThreads = 512;  // 16 warps: global-load latency of the tile loads is the limiter
 
 // block gates with padding: rows >= c keep G = G[c-1] and beta = 0
 GPA_DEV void load_gates_pad(const ScanDesc& d, int u, int t0, int c, float* G, float* bt) {
@@ -125,7 +126,7 @@ struct LFwdChunk {
 };
 
 // grid (U*NB, nscan): U = T diag(b) V and Wk = T diag(b e^G) K of every block.
-__global__ void __launch_bounds__(256) tc_fwd_chunk(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
@@ -195,7 +196,7 @@ struct LFwdState {
 };
 
 // grid (U, nscan): sequential over blocks, full state [K x V] fp32 in shared memory.
-__global__ void __launch_bounds__(256) tc_fwd_state(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
   const int ldk = ld16(K), ldv = ld16(V);
@@ -277,7 +278,7 @@ struct LFwdOut {
 };
 
 // grid (U*NB, nscan): O = e^G (Q S_n) + (Q K^T o Gamma) W
-__global__ void __launch_bounds__(256) tc_fwd_out(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   if (!d.q || !d.O) return;
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
@@ -348,7 +349,7 @@ struct LBwdLocal {
 };
 
 // grid (U*NB, nscan): read-path gradients of O = e^G Q S_n + P W.
-__global__ void __launch_bounds__(256) tc_bwd_local(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
@@ -472,7 +473,7 @@ struct LBwdState {
 
 // grid (U, nscan): reverse sweep; D = dS at block ends; dW = dW_local + lambda K D.
 // D is carried as a hi/lo bf16 pair (~16 significant bits) between blocks.
-__global__ void __launch_bounds__(256) tc_bwd_state(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
   const int ldk = ld16(K), ldv = ld16(V);
@@ -598,7 +599,7 @@ struct LBwdA {
 };
 
 // grid (U*NB, nscan): state-update terms and the U path of the block backward.
-__global__ void __launch_bounds__(256) tc_bwd_chunk_a(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
@@ -759,7 +760,7 @@ struct LBwdB {
 };
 
 // grid (U*NB, nscan): Wk path, dA consequences, final dK / dg / dbeta of every block.
-__global__ void __launch_bounds__(256) tc_bwd_chunk_b(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads) tc_bwd_chunk_b(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K;
@@ -907,7 +908,7 @@ cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStre
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   Launch scope(name, st);
-  k<<<grid, 256, smem, st>>>(b, U, bl);
+  k<<<grid, kThreads, smem, st>>>(b, U, bl);
   return cudaGetLastError();
 }
 
