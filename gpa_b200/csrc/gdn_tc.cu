@@ -24,6 +24,8 @@ using tc::bf16;
 using tc::Carve;
 using tc::copy_f4;
 using tc::for_tiles;
+using tc::ld2;
+using tc::st2;
 using tc::ld16;
 using tc::LDT;
 using tc::mma_acc;
@@ -231,16 +233,17 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blo
     // W = U - Wk S
     tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 ub[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+        ub[p] = t < c ? ld2(d.Ub + row(u, T, t0 + t) * V + col) : make_float2(0.f, 0.f);
+      });
       acc.zero();
       tc::mma_acc3<1, NI, false, false>(acc, Wkh, Wkl, ldk, Sb, nullptr, ldv, m0, n0, K);
-      acc.each(m0, n0, [&](int t, int col, float& v) {
-        float w = 0.f;
-        if (t < c) {
-          const int64_t o = row(u, T, t0 + t) * V + col;
-          w = d.Ub[o] - v;
-          d.W[o] = w;
-        }
-        tc::split_bf16(w * lam[t], Wch + t * ldv + col, Wcl + t * ldv + col);
+      acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+        const float w0 = t < c ? ub[p].x - v0 : 0.f, w1 = t < c ? ub[p].y - v1 : 0.f;
+        if (t < c) st2(d.W + row(u, T, t0 + t) * V + col, w0, w1);
+        tc::split_bf16(w0 * lam[t], Wch + t * ldv + col, Wcl + t * ldv + col);
+        tc::split_bf16(w1 * lam[t], Wch + t * ldv + col + 1, Wcl + t * ldv + col + 1);
       });
     });
     __syncthreads();
@@ -425,12 +428,16 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
   if (d.dq) {
     tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 dq[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+        if (t < c) dq[p] = ld2(d.dq + row(u, T, t0 + t) * K + col);
+      });
       acc.zero();
       mma_acc<1, NI, false, true>(acc, dOs, ldv, Ss, ldv, m0, n0, V);
       acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
       tc::mma_acc3<1, NI, false, false>(acc, dXh, dXl, LDT, Ks, nullptr, ldk, m0, n0, C);
-      acc.each(m0, n0, [&](int t, int col, float& v) {
-        if (t < c) d.dq[row(u, T, t0 + t) * K + col] += v;
+      acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+        if (t < c) st2(d.dq + row(u, T, t0 + t) * K + col, dq[p].x + v0, dq[p].y + v1);
       });
     });
   }
@@ -523,16 +530,18 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
     // dW = dW_local + lambda (K D)
     tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 dw[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+        dw[p] = t < c ? ld2(d.sc_dW + row(u, T, t0 + t) * V + col) : make_float2(0.f, 0.f);
+      });
       acc.zero();
       tc::mma_acc3<1, NI, false, false>(acc, Ks, nullptr, ldk, Dh, Dl, ldv, m0, n0, K);
-      acc.each(m0, n0, [&](int t, int col, float& v) {
-        float w = 0.f;
-        if (t < c) {
-          const int64_t o = row(u, T, t0 + t) * V + col;
-          w = d.sc_dW[o] + lam[t] * v;
-          d.sc_dW[o] = w;
-        }
-        tc::split_bf16(w, dWh + t * ldv + col, dWl + t * ldv + col);
+      acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+        const float w0 = t < c ? dw[p].x + lam[t] * v0 : 0.f;
+        const float w1 = t < c ? dw[p].y + lam[t] * v1 : 0.f;
+        if (t < c) st2(d.sc_dW + row(u, T, t0 + t) * V + col, w0, w1);
+        tc::split_bf16(w0, dWh + t * ldv + col, dWl + t * ldv + col);
+        tc::split_bf16(w1, dWh + t * ldv + col + 1, dWl + t * ldv + col + 1);
       });
     });
     __syncthreads();
@@ -643,15 +652,20 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, B
   // WD = W D^T: dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 dk[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+      if (t < c) dk[p] = ld2(d.sc_dK + row(u, T, t0 + t) * K + col);
+    });
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Wb, ldv, Db, ldv, m0, n0, V);
     float part[2] = {0.f, 0.f};
-    acc.each(m0, n0, [&](int t, int col, float& v) {
+    acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * K + col;
-        d.sc_dK[o] += __expf(G[c - 1] - G[t]) * v;
+        const float lm = __expf(G[c - 1] - G[t]);
+        st2(d.sc_dK + row(u, T, t0 + t) * K + col, dk[p].x + lm * v0, dk[p].y + lm * v1);
       }
-      part[(t - m0) >> 3 & 1] += v * __bfloat162float(Ks[t * ldk + col]);
+      part[(t - m0) >> 3 & 1] += v0 * __bfloat162float(Ks[t * ldk + col]) +
+                                 v1 * __bfloat162float(Ks[t * ldk + col + 1]);
     });
     const int g = (threadIdx.x & 31) >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
@@ -662,7 +676,11 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, B
   });
   {  // <D, S> in fp32
     float part = 0.f;
-    for (int i = threadIdx.x; i < K * V; i += blockDim.x) part += dg[i] * sg[i];
+    for (int i = 4 * threadIdx.x; i < K * V; i += 4 * blockDim.x) {
+      const float4 a = *reinterpret_cast<const float4*>(dg + i);
+      const float4 b4 = *reinterpret_cast<const float4*>(sg + i);
+      part += a.x * b4.x + a.y * b4.y + a.z * b4.z + a.w * b4.w;
+    }
     part = warp_sum(part);
     if ((threadIdx.x & 31) == 0) atomicAdd(&red[0], part);
   }
@@ -700,15 +718,21 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, B
   // dRu = T^T dW ; dV = b dRu ; db += rowsum(dRu o V)
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 vv[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+      if (t < c) vv[p] = ld2(d.v + row(u, T, t0 + t) * V + col);
+    });
     acc.zero();
     tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWh, dWl, ldv, m0, n0, C);
     float part[2] = {0.f, 0.f};
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      tc::split_bf16(v, dRuh + t * ldv + col, dRul + t * ldv + col);
+    acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+      tc::split_bf16(v0, dRuh + t * ldv + col, dRul + t * ldv + col);
+      tc::split_bf16(v1, dRuh + t * ldv + col + 1, dRul + t * ldv + col + 1);
       if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * V + col;
-        atomicAdd(&d.dv[o], bt[t] * v);
-        part[(t - m0) >> 3 & 1] += v * d.v[o];
+        float* o = d.dv + row(u, T, t0 + t) * V + col;
+        atomicAdd(o, bt[t] * v0);
+        atomicAdd(o + 1, bt[t] * v1);
+        part[(t - m0) >> 3 & 1] += v0 * vv[p].x + v1 * vv[p].y;
       }
     });
     const int g = (threadIdx.x & 31) >> 2;
@@ -813,14 +837,23 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_b(ScanBatch b, int U, B
   // dRw = T^T dWk ; sc_dK += b e^G dRw ; rw_t = dRw_t . k_t
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 dk[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+      if (t < c) dk[p] = ld2(d.sc_dK + row(u, T, t0 + t) * K + col);
+    });
     acc.zero();
     tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWkh, dWkl, ldk, m0, n0, C);
     float part[2] = {0.f, 0.f};
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      tc::split_bf16(v, dRwh + t * ldk + col, dRwl + t * ldk + col);
-      if (t < c) d.sc_dK[row(u, T, t0 + t) * K + col] += bt[t] * __expf(G[t]) * v;
-      part[(t - m0) >> 3 & 1] += v * (__bfloat162float(Ks[t * ldk + col]) +
-                                      __bfloat162float(Kl[t * ldk + col]));
+    acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+      tc::split_bf16(v0, dRwh + t * ldk + col, dRwl + t * ldk + col);
+      tc::split_bf16(v1, dRwh + t * ldk + col + 1, dRwl + t * ldk + col + 1);
+      if (t < c) {
+        const float be = bt[t] * __expf(G[t]);
+        st2(d.sc_dK + row(u, T, t0 + t) * K + col, dk[p].x + be * v0, dk[p].y + be * v1);
+      }
+      const int o = t * ldk + col;
+      part[(t - m0) >> 3 & 1] += v0 * (__bfloat162float(Ks[o]) + __bfloat162float(Kl[o])) +
+                                 v1 * (__bfloat162float(Ks[o + 1]) + __bfloat162float(Kl[o + 1]));
     });
     const int g = (threadIdx.x & 31) >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
@@ -862,14 +895,20 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_b(ScanBatch b, int U, B
   // dK = sc_dK + Mm K + Mm^T K
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 a[Acc<1, NI>::kPairs], b2[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
+      if (t < c) {
+        const int64_t o = row(u, T, t0 + t) * K + col;
+        a[p] = ld2(d.dk + o);
+        b2[p] = ld2(d.sc_dK + o);
+      }
+    });
     acc.zero();
     tc::mma_acc3<1, NI, false, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
     tc::mma_acc3<1, NI, true, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * K + col;
-        d.dk[o] += d.sc_dK[o] + v;
-      }
+    acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
+      if (t < c)
+        st2(d.dk + row(u, T, t0 + t) * K + col, a[p].x + b2[p].x + v0, a[p].y + b2[p].y + v1);
     });
   });
   __syncthreads();

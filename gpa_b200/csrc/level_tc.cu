@@ -196,25 +196,27 @@ __global__ void __launch_bounds__(256) tk_level_post(
   // rk = write A_f^T, key_{j+1} = key - ek rk
   tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 kk[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int d, float&, float&) {
+      if (t < c) kk[p] = tc::ld2(key + row(u, T, t0 + t) * D + d);
+    });
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Wb, lm, Af, lm, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int d, float& v) {
-      if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * D + d;
-        key_next[o] = key[o] - ek * v;
-      }
+    acc.each2(m0, n0, [&](int p, int t, int d, float& v0, float& v1) {
+      if (t < c) tc::st2(key_next + row(u, T, t0 + t) * D + d, kk[p].x - ek * v0, kk[p].y - ek * v1);
     });
   });
   // rv = write B_f, val_{j+1} = val - ev rv
   tiles_n<1, 2>(R, Dv, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 xv[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int vv, float&, float&) {
+      if (t < c) xv[p] = tc::ld2(val + row(u, T, t0 + t) * Dv + vv);
+    });
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Wb, lm, Bf, lv, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int vv, float& v) {
-      if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * Dv + vv;
-        val_next[o] = val[o] - ev * v;
-      }
+    acc.each2(m0, n0, [&](int p, int t, int vv, float& v0, float& v1) {
+      if (t < c) tc::st2(val_next + row(u, T, t0 + t) * Dv + vv, xv[p].x - ev * v0, xv[p].y - ev * v1);
     });
   });
 }
@@ -401,10 +403,14 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   // dq_direct += qs dqo W_qs^T
   tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 dq[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int d, float&, float&) {
+      if (t < c) dq[p] = tc::ld2(dq_direct + row(u, T, t0 + t) * D + d);
+    });
     acc.zero();
     tc::mma_acc3<1, NI, false, true>(acc, Qb, Ql, lm, Wbuf + M * lm, nullptr, lm, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int d, float& v) {
-      if (t < c) dq_direct[row(u, T, t0 + t) * D + d] += v;
+    acc.each2(m0, n0, [&](int p, int t, int d, float& v0, float& v1) {
+      if (t < c) tc::st2(dq_direct + row(u, T, t0 + t) * D + d, dq[p].x + v0, dq[p].y + v1);
     });
   });
   __syncthreads();
@@ -592,18 +598,28 @@ __global__ void __launch_bounds__(256) tk_post_bwd(
   // dA_f += nk^T dlw + (-ek dk)^T write
   tiles_n<1, 2>(D, M, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 pa[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int d, int m, float&, float&) { pa[p] = tc::ld2(ta + d * M + m); });
     acc.zero();
     mma_acc<1, NI, true, false>(acc, Nk, ld, dLb, lm, m0, n0, R);
     if (with_residual) mma_acc<1, NI, true, false>(acc, dKb, ld, Wb, lm, m0, n0, R);
-    acc.each(m0, n0, [&](int d, int m, float& v) { ta[d * M + m] += v; });
+    acc.each2(m0, n0, [&](int p, int d, int m, float& v0, float& v1) {
+      tc::st2(ta + d * M + m, pa[p].x + v0, pa[p].y + v1);
+    });
   });
   if (with_residual) {
     // dB_f += write^T (-ev dv)
     tiles_n<1, 2>(M, Dv, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 pb[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int m, int vv, float&, float&) {
+        pb[p] = tc::ld2(tb + m * Dv + vv);
+      });
       acc.zero();
       mma_acc<1, NI, true, false>(acc, Wb, lm, dVb, lv, m0, n0, R);
-      acc.each(m0, n0, [&](int m, int vv, float& v) { tb[m * Dv + vv] += v; });
+      acc.each2(m0, n0, [&](int p, int m, int vv, float& v0, float& v1) {
+        tc::st2(tb + m * Dv + vv, pb[p].x + v0, pb[p].y + v1);
+      });
     });
   }
 }
@@ -688,10 +704,14 @@ __global__ void __launch_bounds__(256) tk_prep_bwd(int U, int T, int H, int D, i
   // dkey += dslot C
   tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 dk[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int d, float&, float&) {
+      if (t < c) dk[p] = tc::ld2(dkey + row(u, T, t0 + t) * D + d);
+    });
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Dsb, lm, Cb, ld16(D), m0, n0, M);
-    acc.each(m0, n0, [&](int t, int d, float& v) {
-      if (t < c) dkey[row(u, T, t0 + t) * D + d] += v;
+    acc.each2(m0, n0, [&](int p, int t, int d, float& v0, float& v1) {
+      if (t < c) tc::st2(dkey + row(u, T, t0 + t) * D + d, dk[p].x + v0, dk[p].y + v1);
     });
   });
 }

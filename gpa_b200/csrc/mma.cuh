@@ -74,6 +74,23 @@ struct Acc {
 #pragma unroll
         for (int r = 0; r < 4; ++r) v[i][j][r] = 0.f;
   }
+  // Column pairs (col, col + 1) of the warp's elements, with a pair index p in
+  // [0, kPairs) that is a compile-time constant after unrolling: f(p, row, col, v0, v1).
+  // Epilogues that read global memory first gather every pair they need into a
+  // float2[kPairs] (all loads in flight at once), then compute and store.
+  static constexpr int kPairs = MI * 2 * NI * 2;
+  template <class F>
+  GPA_DEV void each2(int m0, int n0, F f) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int i = 0; i < MI; ++i)
+#pragma unroll
+      for (int j = 0; j < 2 * NI; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          f((i * 2 * NI + j) * 2 + h, m0 + 16 * i + g + 8 * h, n0 + 8 * j + 2 * q, v[i][j][2 * h],
+            v[i][j][2 * h + 1]);
+  }
   // f(row, col, float& value) over the warp's elements
   template <class F>
   GPA_DEV void each(int m0, int n0, F f) {
@@ -151,6 +168,9 @@ GPA_DEV void mma_acc3(Acc<MI, NI>& acc, const bf16* Ah, const bf16* Al, int lda,
     }
   }
 }
+
+GPA_DEV float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+GPA_DEV void st2(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
 
 // hi / lo bf16 pair of an fp32 value
 GPA_DEV void split_bf16(float x, bf16* hi, bf16* lo) {
