@@ -170,7 +170,9 @@ struct Saved {
   float *qoh[kMaxLevels], *qon[kMaxLevels], *y[kMaxLevels];
   float *Rbnd[kMaxEdges], *WR[kMaxEdges], *msg[kMaxEdges];
   float *ge, *be;
-  float* wk[kMaxScans];  // forward transient (chunk WY keys)
+  // chunk WY terms of every scan (U = T diag(b) V, Wk = T diag(b e^G) K), kept for the backward
+  float *UA[kMaxLevels], *KA[kMaxLevels], *UB[kMaxLevels], *KB[kMaxLevels];
+  float *UR[kMaxEdges], *KR[kMaxEdges];
   size_t bytes;
 };
 
@@ -220,9 +222,16 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
   }
   s->ge = b.take((size_t)g.E * g.U);
   s->be = b.take((size_t)g.E * g.U);
-  const int kw = g.D > g.Mmax ? g.D : g.Mmax;
-  const int nwk = g.L - 1 > 2 ? g.L - 1 : 2;  // widest scan batch: a relation group or a level pair
-  for (int i = 0; i < kMaxScans; ++i) s->wk[i] = i < nwk ? b.take(UT * kw) : nullptr;
+  for (int j = 0; j < g.L; ++j) {
+    s->UA[j] = b.take(UT * g.M[j]);
+    s->KA[j] = b.take(UT * g.D);
+    s->UB[j] = b.take(UT * g.Dv);
+    s->KB[j] = b.take(UT * g.M[j]);
+  }
+  for (int e = 0; e < g.E; ++e) {
+    s->UR[e] = b.take(UT * g.M[g.ed[e]]);
+    s->KR[e] = b.take(UT * g.M[g.es[e]]);
+  }
   s->bytes = b.off + 256;
 }
 
@@ -237,7 +246,7 @@ struct Scratch {
   float *draw, *dn, *dnsum, *extA, *extB, *dnk, *dslot, *dns, *dgates, *d4;
   float *dfzA, *dfzB;
   // GDN group slots
-  float *Ub[kMaxScans], *Wk[kMaxScans], *dWk[kMaxScans], *db[kMaxScans], *dA[kMaxScans];
+  float *dWk[kMaxScans], *db[kMaxScans], *dA[kMaxScans];
   float *Dend[kMaxScans], *dK[kMaxScans], *dW[kMaxScans], *dG[kMaxScans];
   size_t bytes;
 };
@@ -284,8 +293,6 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
   const size_t K = g.D > Mx ? g.D : Mx, V = g.Dv > Mx ? g.Dv : Mx;
   const int slots = g.L - 1 > 2 ? g.L - 1 : 2;
   for (int i = 0; i < slots; ++i) {
-    s->Ub[i] = b.take(UT * V);
-    s->Wk[i] = b.take(UT * K);
     s->dWk[i] = b.take(UT * K);
     s->db[i] = b.take(UT);
     s->dA[i] = b.take((size_t)g.U * nb * kMaxChunk * kMaxChunk);
@@ -385,8 +392,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     in.S0 = si->inner[j];
     in.Sb = s.Abnd[j];
     in.W = s.WA[j];
-    in.Ub = s.WA[j];
-    in.Wk = s.wk[0];
+    in.Ub = s.UA[j];
+    in.Wk = s.KA[j];
     in.O = s.raw[j];
     in.S_final = so->inner[j];
     ou = blank_scan();
@@ -401,8 +408,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     ou.S0 = si->outer[j];
     ou.Sb = s.Bbnd[j];
     ou.W = s.WB[j];
-    ou.Ub = s.WB[j];
-    ou.Wk = s.wk[1];
+    ou.Ub = s.UB[j];
+    ou.Wk = s.KB[j];
     ou.S_final = so->outer[j];
     CK(gdn_forward(sb, U, bl, true, st));
     const int with_res = j + 1 < g.L;
@@ -438,8 +445,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
       d.S0 = si->relation[e];
       d.Sb = s.Rbnd[e];
       d.W = s.WR[e];
-      d.Ub = s.WR[e];
-      d.Wk = s.wk[sb.n];
+      d.Ub = s.UR[e];
+      d.Wk = s.KR[e];
       d.O = s.msg[e];
       d.S_final = so->relation[e];
       ++sb.n;
@@ -620,8 +627,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
       d.g_st = 0;
       d.Sb = s.Rbnd[e];
       d.W = s.WR[e];
-      d.Ub = x.Ub[slot];
-      d.Wk = x.Wk[slot];
+      d.Ub = s.UR[e];
+      d.Wk = s.KR[e];
       d.dO = x.dmsg[e];
       d.dS_final = ds.relation[e];
       d.dq = x.dlh[i];
@@ -710,8 +717,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     in.g_st = 4;
     in.Sb = s.Abnd[j];
     in.W = s.WA[j];
-    in.Ub = x.Ub[0];
-    in.Wk = x.Wk[0];
+    in.Ub = s.UA[j];
+    in.Wk = s.KA[j];
     in.dO = x.draw;
     in.ext = x.extA;
     in.dS_final = ds.inner[j];
@@ -734,8 +741,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     sb.n = 2;
     ScanDesc& ou = sb.s[1];
     ou = outer_desc(j);
-    ou.Ub = x.Ub[1];
-    ou.Wk = x.Wk[1];
+    ou.Ub = s.UB[j];
+    ou.Wk = s.KB[j];
     ou.ext = x.extB;
     ou.dS_final = ds.outer[j];
     ou.dk = x.dns;

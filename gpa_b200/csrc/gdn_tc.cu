@@ -987,11 +987,9 @@ cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaS
                    st, b, U, bl);
 }
 
+// U and Wk of every block come from the forward (kept in the saved buffer).
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  cudaError_t e = tc_launch("tc_fwd_chunk", tc_fwd_chunk, dim3(U * bl.nb, b.n),
-                            max_smem<LFwdChunk>(b), st, b, U, bl);
-  if (e != cudaSuccess) return e;
-  e = tc_launch("tc_bwd_state", tc_bwd_state, dim3(U, b.n), max_smem<LBwdState>(b), st, b, U, bl);
+  cudaError_t e = tc_launch("tc_bwd_state", tc_bwd_state, dim3(U, b.n), max_smem<LBwdState>(b), st, b, U, bl);
   if (e != cudaSuccess) return e;
   e = tc_launch("tc_bwd_chunk_a", tc_bwd_chunk_a, dim3(U * bl.nb, b.n), max_smem<LBwdA>(b), st,
                 b, U, bl);
