@@ -107,7 +107,7 @@ def kernel_flops(cfg, units, length):
     allscans = inner + outer + rel
     use = {
         # forward: chunk + state for all scans; out for inner, outer reads, relations
-        "gdn_fwd_chunk": allscans + allscans,   # forward + backward recompute
+        "gdn_fwd_chunk": allscans + allscans,   # SIMT path: forward + backward recompute
         "gdn_fwd_state": allscans,
         "gdn_fwd_out": allscans,
         "gdn_bwd_local": allscans,
@@ -116,12 +116,13 @@ def kernel_flops(cfg, units, length):
         "gdn_bwd_chunk_k": allscans,
     }
     out = {k: units * nb * sum(per[k](K, V) for K, V in use[k]) for k in per}
-    # tensor-core variants of the same phases (bf16 path)
-    for tk, sk in (("tc_fwd_chunk", "gdn_fwd_chunk"), ("tc_fwd_state", "gdn_fwd_state"),
-                   ("tc_fwd_out", "gdn_fwd_out"), ("tc_bwd_local", "gdn_bwd_local"),
-                   ("tc_bwd_state", "gdn_bwd_state"), ("tc_bwd_chunk_a", "gdn_bwd_chunk_v"),
-                   ("tc_bwd_chunk_b", "gdn_bwd_chunk_k")):
+    # tensor-core variants (bf16 path): the forward keeps U and Wk, so the backward does not
+    # recompute fwd_chunk, and one fused kernel does both chunk phases of the backward
+    for tk, sk in (("tc_fwd_state", "gdn_fwd_state"), ("tc_fwd_out", "gdn_fwd_out"),
+                   ("tc_bwd_local", "gdn_bwd_local"), ("tc_bwd_state", "gdn_bwd_state")):
         out[tk] = out[sk]
+    out["tc_fwd_chunk"] = out["gdn_fwd_chunk"] // 2
+    out["tc_bwd_chunk"] = out["gdn_bwd_chunk_v"] + out["gdn_bwd_chunk_k"]
     return out
 
 

@@ -647,11 +647,13 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
       d.sc_dA = x.dA[slot];
       d.Dend = x.Dend[slot];
       const size_t K = d.K, V = d.V;
-      CK(zero(x.dK[slot], UT * K, st));
-      CK(zero(x.dWk[slot], UT * K, st));
-      CK(zero(x.dG[slot], UT, st));
-      CK(zero(x.db[slot], UT, st));
-      CK(zero(x.dA[slot], (size_t)U * bl.nb * kMaxChunk * kMaxChunk, st));
+      if (!g.fast) {  // the SIMT kernels accumulate into these; the tensor-core ones overwrite
+        CK(zero(x.dK[slot], UT * K, st));
+        CK(zero(x.dWk[slot], UT * K, st));
+        CK(zero(x.dG[slot], UT, st));
+        CK(zero(x.db[slot], UT, st));
+        CK(zero(x.dA[slot], (size_t)U * bl.nb * kMaxChunk * kMaxChunk, st));
+      }
       (void)V;
       ++sb.n;
     }
@@ -694,13 +696,15 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     CK(zero(x.dslot, UT * M, st));
     CK(zero(x.dns, UT * M, st));
     CK(zero(x.dgates, UT * 4, st));
-    for (int sl = 0; sl < 2; ++sl) {
-      CK(zero(x.dWk[sl], UT * (D > M ? D : M), st));
-      CK(zero(x.db[sl], UT, st));
-      CK(zero(x.dA[sl], (size_t)U * bl.nb * kMaxChunk * kMaxChunk, st));
+    if (!g.fast) {  // the SIMT kernels accumulate into these; the tensor-core ones overwrite
+      for (int sl = 0; sl < 2; ++sl) {
+        CK(zero(x.dWk[sl], UT * (D > M ? D : M), st));
+        CK(zero(x.db[sl], UT, st));
+        CK(zero(x.dA[sl], (size_t)U * bl.nb * kMaxChunk * kMaxChunk, st));
+      }
+      CK(zero(x.dK[0], UT * D, st));
+      CK(zero(x.dG[0], UT, st));
     }
-    CK(zero(x.dK[0], UT * D, st));
-    CK(zero(x.dG[0], UT, st));
     ScanBatch sb;
     sb.tc = g.fast;
     sb.n = 1;

@@ -571,90 +571,129 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
   }
 }
 
-struct LBwdA {
-  // phase 1 region R: Sb, Db; phase 2 reuses it for Kl, A, Tm, Tth, Ttl
-  size_t Ks, R, Sb, Db, Kl, A, Tm, Tth, Ttl, Wb, dWh, dWl, Uh, Ul, Xs, dRuh, dRul, G, bt, dlam, dbacc,
-      red, total;
-  __host__ __device__ LBwdA(int K, int V) {
+struct LBwdChunk {
+  // fixed buffers, then Y (dW hi/lo) and a pool X whose contents change by stage:
+  //   T build: Tm, Xs | state terms: Sb, Db, Wb | U path: Uh, Ul | Wk path: Wkh, Wkl, dWkh, dWkl
+  //   | final: Mmb
+  size_t Ks, Kl, Th, Tl, A, dAf, Mh, Ml, G, bt, dG, db, dlam, rw, red, dWh, dWl, X, total;
+  size_t Tm, Xs, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mmb;
+  __host__ __device__ LBwdChunk(int K, int V) {
     Carve c;
-    Ks = c.take(2 * C * ld16(K));
-    const size_t sbytes = 2 * K * ld16(V);
-    const size_t p2 = 2 * C * ld16(K) + 2 * (4 * C * kAStride) + 2 * (2 * C * LDT) + 64;
-    R = c.take(2 * sbytes > p2 ? 2 * sbytes : p2);
-    Sb = R;
-    Db = R + sbytes;
-    Carve r2;
-    r2.off = R;
-    Kl = r2.take(2 * C * ld16(K));
-    A = r2.take(4 * C * kAStride);
-    Tm = r2.take(4 * C * kAStride);
-    Tth = r2.take(2 * C * LDT);
-    Ttl = r2.take(2 * C * LDT);
-    Wb = c.take(2 * C * ld16(V));
-    dWh = c.take(2 * C * ld16(V));
-    dWl = c.take(2 * C * ld16(V));
-    Uh = c.take(2 * C * ld16(V));
-    Ul = c.take(2 * C * ld16(V));
-    Xs = c.take(4 * 768);
-    dRuh = c.take(2 * C * ld16(V));
-    dRul = c.take(2 * C * ld16(V));
+    const size_t sK = 2 * C * ld16(K), sV = 2 * C * ld16(V), sS = 2 * K * ld16(V);
+    const size_t sA = 4 * C * kAStride, sT = 2 * C * LDT;
+    Ks = c.take(sK);
+    Kl = c.take(sK);
+    Th = c.take(sT);
+    Tl = c.take(sT);
+    A = c.take(sA);
+    dAf = c.take(sA);
+    Mh = c.take(sT);
+    Ml = c.take(sT);
     G = c.take(4 * C);
     bt = c.take(4 * C);
+    dG = c.take(4 * C);
+    db = c.take(4 * C);
     dlam = c.take(4 * C);
-    dbacc = c.take(4 * C);
+    rw = c.take(4 * C);
     red = c.take(4 * 32);
+    dWh = c.take(sV);
+    dWl = c.take(sV);
+    size_t pool = sA + 4 * 768;
+    pool = pool > 2 * sS + sV ? pool : 2 * sS + sV;
+    pool = pool > 2 * sV ? pool : 2 * sV;
+    pool = pool > 4 * sK ? pool : 4 * sK;
+    X = c.take(pool);
+    Tm = X;
+    Xs = X + sA;
+    Sb = X;
+    Db = X + sS;
+    Wb = X + 2 * sS;
+    Uh = X;
+    Ul = X + sV;
+    Wkh = X;
+    Wkl = X + sK;
+    dWkh = X + 2 * sK;
+    dWkl = X + 3 * sK;
+    Mmb = X;
     total = c.off;
   }
 };
 
-// grid (U*NB, nscan): state-update terms and the U path of the block backward.
-__global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, Blocks bl) {
+// grid (U*NB, nscan): the whole block backward after the state sweep (dW and D known):
+// state-update terms, U path, Wk path, dA consequences, final dK / dg / dbeta.
+// The dA of both paths is formed as -T^T (dW U^T + dWk Wk^T) (strictly lower part).
+__global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
   const int ldk = ld16(K), ldv = ld16(V);
   const int64_t KV = (int64_t)K * V;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   extern __shared__ __align__(16) unsigned char smem[];
-  const LBwdA L(K, V);
+  const LBwdChunk L(K, V);
   bf16* Ks = (bf16*)(smem + L.Ks);
-  bf16* Sb = (bf16*)(smem + L.Sb);
-  bf16* Db = (bf16*)(smem + L.Db);
   bf16* Kl = (bf16*)(smem + L.Kl);
+  bf16* Th = (bf16*)(smem + L.Th);
+  bf16* Tl = (bf16*)(smem + L.Tl);
   float* A = (float*)(smem + L.A);
-  float* Tm = (float*)(smem + L.Tm);
-  bf16* Tth = (bf16*)(smem + L.Tth);
-  bf16* Ttl = (bf16*)(smem + L.Ttl);
-  bf16* Wb = (bf16*)(smem + L.Wb);
-  bf16* dWh = (bf16*)(smem + L.dWh);
-  bf16* dWl = (bf16*)(smem + L.dWl);
-  bf16* Uh = (bf16*)(smem + L.Uh);
-  bf16* Ul = (bf16*)(smem + L.Ul);
-  float* Xs = (float*)(smem + L.Xs);
-  bf16* dRuh = (bf16*)(smem + L.dRuh);
-  bf16* dRul = (bf16*)(smem + L.dRul);
+  float* dAf = (float*)(smem + L.dAf);
+  bf16* Mh = (bf16*)(smem + L.Mh);
+  bf16* Ml = (bf16*)(smem + L.Ml);
   float* G = (float*)(smem + L.G);
   float* bt = (float*)(smem + L.bt);
+  float* dG = (float*)(smem + L.dG);
+  float* db = (float*)(smem + L.db);
   float* dlam = (float*)(smem + L.dlam);
-  float* dbacc = (float*)(smem + L.dbacc);
+  float* rw = (float*)(smem + L.rw);
   float* red = (float*)(smem + L.red);
+  bf16* dWh = (bf16*)(smem + L.dWh);
+  bf16* dWl = (bf16*)(smem + L.dWl);
+  float* Tm = (float*)(smem + L.Tm);
+  float* Xs = (float*)(smem + L.Xs);
+  bf16* Sb = (bf16*)(smem + L.Sb);
+  bf16* Db = (bf16*)(smem + L.Db);
+  bf16* Wb = (bf16*)(smem + L.Wb);
+  bf16* Uh = (bf16*)(smem + L.Uh);
+  bf16* Ul = (bf16*)(smem + L.Ul);
+  bf16* Wkh = (bf16*)(smem + L.Wkh);
+  bf16* Wkl = (bf16*)(smem + L.Wkl);
+  bf16* dWkh = (bf16*)(smem + L.dWkh);
+  bf16* dWkl = (bf16*)(smem + L.dWkl);
+  bf16* Mmb = (bf16*)(smem + L.Mmb);
   const float* sg = d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV;
   const float* dg = d.Dend + ((int64_t)u * bl.nb + n) * KV;
-  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Sb, ldv, sg, V, K, V, K);
-  tile_to_bf16(Db, ldv, dg, V, K, V, K);
-  tile_to_bf16(Wb, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
-  tile_split(dWh, dWl, ldv, d.sc_dW + row(u, T, t0) * V, V, c, V, C);
-  tile_split(Uh, Ul, ldv, d.Ub + row(u, T, t0) * V, V, c, V, C);
-  for (int t = threadIdx.x; t < C; t += blockDim.x) dlam[t] = dbacc[t] = 0.f;
+  const int64_t r0 = row(u, T, t0);
+
+  // ---- T = (I + A)^-1 of the block
+  tile_split(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C);
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    dG[t] = t < c ? d.sc_dG[r0 + t] : 0.f;
+    db[t] = dlam[t] = rw[t] = 0.f;
+  }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
   load_gates_pad(d, u, t0, c, G, bt);
   __syncthreads();
-  // WD = W D^T: dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
+  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
+  __syncthreads();
+  invert_unit_lower(A, Tm, Xs);
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    tc::split_bf16(Tm[t * kAStride + s], Th + t * LDT + s, Tl + t * LDT + s);
+  }
+  __syncthreads();  // pool X (Tm) is reused below
+
+  // ---- state-update terms: WD = W D^T, <D, S>, dWk = -dW S^T
+  tile_to_bf16(Sb, ldv, sg, V, K, V, K);
+  tile_to_bf16(Db, ldv, dg, V, K, V, K);
+  tile_to_bf16(Wb, ldv, d.W + r0 * V, V, c, V, C);
+  tile_split(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C);
+  __syncthreads();
+  // sc_dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     float2 dk[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-      if (t < c) dk[p] = ld2(d.sc_dK + row(u, T, t0 + t) * K + col);
+      if (t < c) dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
     });
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Wb, ldv, Db, ldv, m0, n0, V);
@@ -662,14 +701,14 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, B
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) {
         const float lm = __expf(G[c - 1] - G[t]);
-        st2(d.sc_dK + row(u, T, t0 + t) * K + col, dk[p].x + lm * v0, dk[p].y + lm * v1);
+        st2(d.sc_dK + (r0 + t) * K + col, dk[p].x + lm * v0, dk[p].y + lm * v1);
       }
       part[(t - m0) >> 3 & 1] += v0 * __bfloat162float(Ks[t * ldk + col]) +
                                  v1 * __bfloat162float(Ks[t * ldk + col + 1]);
     });
-    const int g = (threadIdx.x & 31) >> 2;
+    const int g = lane >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
-    if ((threadIdx.x & 3) == 0) {
+    if ((lane & 3) == 0) {
       atomicAdd(&dlam[m0 + g], p0);
       atomicAdd(&dlam[m0 + g + 8], p1);
     }
@@ -678,189 +717,104 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_a(ScanBatch b, int U, B
     float part = 0.f;
     for (int i = 4 * threadIdx.x; i < K * V; i += 4 * blockDim.x) {
       const float4 a = *reinterpret_cast<const float4*>(dg + i);
-      const float4 b4 = *reinterpret_cast<const float4*>(sg + i);
-      part += a.x * b4.x + a.y * b4.y + a.z * b4.z + a.w * b4.w;
+      const float4 s4 = *reinterpret_cast<const float4*>(sg + i);
+      part += a.x * s4.x + a.y * s4.y + a.z * s4.z + a.w * s4.w;
     }
     part = warp_sum(part);
-    if ((threadIdx.x & 31) == 0) atomicAdd(&red[0], part);
+    if (lane == 0) atomicAdd(&red[0], part);
   }
-  // dWk = -dW S^T
+  // dWk = -dW S^T, staged through global memory (L2) for the Wk path
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
     tc::mma_acc3<1, NI, false, true>(acc, dWh, dWl, ldv, Sb, nullptr, ldv, m0, n0, V);
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      if (t < c) d.sc_dWk[row(u, T, t0 + t) * K + col] = -v;
+    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+      if (t < c) st2(d.sc_dWk + (r0 + t) * K + col, -v0, -v1);
     });
   });
-  __syncthreads();  // phase 1 done: region R (Sb, Db) is reused below
-  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
   __syncthreads();
-  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
-  __syncthreads();
-  invert_unit_lower(A, Tm, Xs);
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    tc::split_bf16(Tm[t * kAStride + s], Tth + t * LDT + s, Ttl + t * LDT + s);
-  }
-  if (threadIdx.x < 32) {  // dG from the state update (lambda and gamma_c terms)
+  if (w == 0) {  // dG from the state update (lambda and gamma_c terms)
     float tot = 0.f;
-    for (int t = threadIdx.x; t < c; t += 32) {
+    for (int t = lane; t < c; t += 32) {
       const float x = dlam[t] * __expf(G[c - 1] - G[t]);
       tot += x;
-      d.sc_dG[row(u, T, t0 + t)] -= x;
+      dG[t] -= x;
     }
     tot = warp_sum(tot);
-    __syncwarp();
-    if (threadIdx.x == 0) d.sc_dG[row(u, T, t0 + c - 1)] += tot + __expf(G[c - 1]) * red[0];
+    if (lane == 0) dG[c - 1] += tot + __expf(G[c - 1]) * red[0];
   }
+
+  // ---- U path: dRu = T^T dW ; dV += b dRu ; db += rowsum(dRu o V) ; M = dW U^T
+  tile_split(Uh, Ul, ldv, d.Ub + r0 * V, V, c, V, C);
   __syncthreads();
-  // dRu = T^T dW ; dV = b dRu ; db += rowsum(dRu o V)
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     float2 vv[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-      if (t < c) vv[p] = ld2(d.v + row(u, T, t0 + t) * V + col);
+      if (t < c) vv[p] = ld2(d.v + (r0 + t) * V + col);
     });
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWh, dWl, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWh, dWl, ldv, m0, n0, C);
     float part[2] = {0.f, 0.f};
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
-      tc::split_bf16(v0, dRuh + t * ldv + col, dRul + t * ldv + col);
-      tc::split_bf16(v1, dRuh + t * ldv + col + 1, dRul + t * ldv + col + 1);
       if (t < c) {
-        float* o = d.dv + row(u, T, t0 + t) * V + col;
+        float* o = d.dv + (r0 + t) * V + col;
         atomicAdd(o, bt[t] * v0);
         atomicAdd(o + 1, bt[t] * v1);
         part[(t - m0) >> 3 & 1] += v0 * vv[p].x + v1 * vv[p].y;
       }
     });
-    const int g = (threadIdx.x & 31) >> 2;
+    const int g = lane >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
-    if ((threadIdx.x & 3) == 0) {
-      atomicAdd(&dbacc[m0 + g], p0);
-      atomicAdd(&dbacc[m0 + g + 8], p1);
+    if ((lane & 3) == 0) {
+      atomicAdd(&db[m0 + g], p0);
+      atomicAdd(&db[m0 + g + 8], p1);
     }
   });
-  __syncthreads();
-  // dA (U path) = -dRu U^T, strictly lower
-  float* dA = d.sc_dA + ((int64_t)u * bl.nb + n) * C * C;
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {
     Acc<1, 2> acc;
     acc.zero();
-    tc::mma_acc3<1, 2, false, true>(acc, dRuh, dRul, ldv, Uh, Ul, ldv, m0, n0, V);
-    acc.each(m0, n0, [&](int t, int s, float& v) { dA[t * C + s] = s < t ? -v : 0.f; });
+    tc::mma_acc3<1, 2, false, true>(acc, dWh, dWl, ldv, Uh, Ul, ldv, m0, n0, V);
+    acc.each(m0, n0, [&](int t, int s, float& v) { dAf[t * kAStride + s] = v; });
   });
-  for (int t = threadIdx.x; t < c; t += blockDim.x) d.sc_db[row(u, T, t0 + t)] = dbacc[t];
-}
+  __syncthreads();
 
-struct LBwdB {
-  size_t Ks, Kl, Wkh, Wkl, dWkh, dWkl, A, Tm, Xs, Tth, Ttl, dAf, Mmb, dRwh, dRwl, G, bt, dG, db, rw,
-      total;
-  __host__ __device__ LBwdB(int K, int) {
-    Carve c;
-    Ks = c.take(2 * C * ld16(K));
-    Kl = c.take(2 * C * ld16(K));
-    Wkh = c.take(2 * C * ld16(K));
-    Wkl = c.take(2 * C * ld16(K));
-    dWkh = c.take(2 * C * ld16(K));
-    dWkl = c.take(2 * C * ld16(K));
-    A = c.take(4 * C * kAStride);
-    Tm = c.take(4 * C * kAStride);
-    Xs = c.take(4 * 768);
-    Tth = c.take(2 * C * LDT);
-    Ttl = c.take(2 * C * LDT);
-    dAf = c.take(4 * C * kAStride);
-    Mmb = c.take(2 * C * LDT);
-    dRwh = c.take(2 * C * ld16(K));
-    dRwl = c.take(2 * C * ld16(K));
-    G = c.take(4 * C);
-    bt = c.take(4 * C);
-    dG = c.take(4 * C);
-    db = c.take(4 * C);
-    rw = c.take(4 * C);
-    total = c.off;
-  }
-};
-
-// grid (U*NB, nscan): Wk path, dA consequences, final dK / dg / dbeta of every block.
-__global__ void __launch_bounds__(kThreads) tc_bwd_chunk_b(ScanBatch b, int U, Blocks bl) {
-  const ScanDesc& d = b.s[blockIdx.y];
-  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
-  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K;
-  const int ldk = ld16(K);
-  extern __shared__ __align__(16) unsigned char smem[];
-  const LBwdB L(K, d.V);
-  bf16* Ks = (bf16*)(smem + L.Ks);
-  bf16* Kl = (bf16*)(smem + L.Kl);
-  bf16* Wkh = (bf16*)(smem + L.Wkh);
-  bf16* Wkl = (bf16*)(smem + L.Wkl);
-  bf16* dWkh = (bf16*)(smem + L.dWkh);
-  bf16* dWkl = (bf16*)(smem + L.dWkl);
-  float* A = (float*)(smem + L.A);
-  float* Tm = (float*)(smem + L.Tm);
-  float* Xs = (float*)(smem + L.Xs);
-  bf16* Tth = (bf16*)(smem + L.Tth);
-  bf16* Ttl = (bf16*)(smem + L.Ttl);
-  float* dAf = (float*)(smem + L.dAf);
-  bf16* Mmb = (bf16*)(smem + L.Mmb);
-  bf16* dRwh = (bf16*)(smem + L.dRwh);
-  bf16* dRwl = (bf16*)(smem + L.dRwl);
-  float* G = (float*)(smem + L.G);
-  float* bt = (float*)(smem + L.bt);
-  float* dG = (float*)(smem + L.dG);
-  float* db = (float*)(smem + L.db);
-  float* rw = (float*)(smem + L.rw);
-  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-  tile_split(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C);
-  tile_split(dWkh, dWkl, ldk, d.sc_dWk + row(u, T, t0) * K, K, c, K, C);
-  const float* dAg = d.sc_dA + ((int64_t)u * bl.nb + n) * C * C;
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    dAf[t * kAStride + s] = (t < c && s < c) ? dAg[i] : 0.f;
-  }
-  for (int t = threadIdx.x; t < C; t += blockDim.x) {
-    dG[t] = t < c ? d.sc_dG[row(u, T, t0 + t)] : 0.f;
-    db[t] = t < c ? d.sc_db[row(u, T, t0 + t)] : 0.f;
-    rw[t] = 0.f;
-  }
-  load_gates_pad(d, u, t0, c, G, bt);
+  // ---- Wk path: dRw = T^T dWk ; sc_dK += b e^G dRw ; rw = rowsum(dRw o K) ; M += dWk Wk^T
+  tile_split(Wkh, Wkl, ldk, d.Wk + r0 * K, K, c, K, C);
+  tile_split(dWkh, dWkl, ldk, d.sc_dWk + r0 * K, K, c, K, C);
   __syncthreads();
-  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
-  __syncthreads();
-  invert_unit_lower(A, Tm, Xs);
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    tc::split_bf16(Tm[t * kAStride + s], Tth + t * LDT + s, Ttl + t * LDT + s);
-  }
-  __syncthreads();
-  // dRw = T^T dWk ; sc_dK += b e^G dRw ; rw_t = dRw_t . k_t
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     float2 dk[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-      if (t < c) dk[p] = ld2(d.sc_dK + row(u, T, t0 + t) * K + col);
+      if (t < c) dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
     });
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, Tth, Ttl, LDT, dWkh, dWkl, ldk, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWkh, dWkl, ldk, m0, n0, C);
     float part[2] = {0.f, 0.f};
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
-      tc::split_bf16(v0, dRwh + t * ldk + col, dRwl + t * ldk + col);
-      tc::split_bf16(v1, dRwh + t * ldk + col + 1, dRwl + t * ldk + col + 1);
       if (t < c) {
         const float be = bt[t] * __expf(G[t]);
-        st2(d.sc_dK + row(u, T, t0 + t) * K + col, dk[p].x + be * v0, dk[p].y + be * v1);
+        st2(d.sc_dK + (r0 + t) * K + col, dk[p].x + be * v0, dk[p].y + be * v1);
       }
       const int o = t * ldk + col;
       part[(t - m0) >> 3 & 1] += v0 * (__bfloat162float(Ks[o]) + __bfloat162float(Kl[o])) +
                                  v1 * (__bfloat162float(Ks[o + 1]) + __bfloat162float(Kl[o + 1]));
     });
-    const int g = (threadIdx.x & 31) >> 2;
+    const int g = lane >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
-    if ((threadIdx.x & 3) == 0) {
+    if ((lane & 3) == 0) {
       atomicAdd(&rw[m0 + g], p0);
       atomicAdd(&rw[m0 + g + 8], p1);
     }
+  });
+  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
+    Acc<1, 2> acc;
+    acc.each(m0, n0, [&](int t, int s, float& v) { v = dAf[t * kAStride + s]; });
+    tc::mma_acc3<1, 2, false, true>(acc, dWkh, dWkl, ldk, Wkh, Wkl, ldk, m0, n0, K);
+    acc.each(m0, n0, [&](int t, int s, float& v) {
+      tc::split_bf16(v, Mh + t * LDT + s, Ml + t * LDT + s);
+    });
   });
   __syncthreads();
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
@@ -868,74 +822,87 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk_b(ScanBatch b, int U, B
     db[t] += e * rw[t];
     dG[t] += bt[t] * e * rw[t];
   }
-  // dA -= dRw Wk^T (strictly lower)
+  // dA = -T^T M, strictly lower
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {
     Acc<1, 2> acc;
     acc.zero();
-    tc::mma_acc3<1, 2, false, true>(acc, dRwh, dRwl, ldk, Wkh, Wkl, ldk, m0, n0, K);
+    tc::mma_acc3<1, 2, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
     acc.each(m0, n0, [&](int t, int s, float& v) {
-      dAf[t * kAStride + s] = s < t ? dAf[t * kAStride + s] - v : 0.f;
+      dAf[t * kAStride + s] = (s < t && t < c) ? -v : 0.f;
     });
   });
   __syncthreads();
-  if (threadIdx.x < C) {
-    const int t = threadIdx.x;
-    // A = b_t Atil: rowsum(dA o Atil) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
+  // A = b_t Atil: rowsum(dA o Atil) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
+  for (int t = w; t < C; t += nw) {
     float r2 = 0.f, c2 = 0.f;
-    for (int s = 0; s < t; ++s) r2 += dAf[t * kAStride + s] * A[t * kAStride + s];
-    for (int s = t + 1; s < C; ++s) c2 += dAf[s * kAStride + t] * A[s * kAStride + t];
-    if (t < c) db[t] += r2 / bt[t];
-    dG[t] += r2 - c2;
+    for (int s = lane; s < C; s += 32) {
+      r2 += dAf[t * kAStride + s] * A[t * kAStride + s];
+      c2 += dAf[s * kAStride + t] * A[s * kAStride + t];
+    }
+    r2 = warp_sum(r2);
+    c2 = warp_sum(c2);
+    if (lane == 0) {
+      if (t < c) db[t] += r2 / bt[t];
+      dG[t] += r2 - c2;
+    }
   }
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
     const int t = i / C, s = i - t * C;
-    Mmb[t * LDT + s] = __float2bfloat16(s < t ? dAf[t * kAStride + s] * bt[t] * __expf(G[t] - G[s]) : 0.f);
+    Mmb[t * LDT + s] =
+        __float2bfloat16(s < t ? dAf[t * kAStride + s] * bt[t] * __expf(G[t] - G[s]) : 0.f);
   }
   __syncthreads();
   // dK = sc_dK + Mm K + Mm^T K
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
-    float2 a[Acc<1, NI>::kPairs], b2[Acc<1, NI>::kPairs];
+    float2 a[Acc<1, NI>::kPairs], s2[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
       if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * K + col;
-        a[p] = ld2(d.dk + o);
-        b2[p] = ld2(d.sc_dK + o);
+        a[p] = ld2(d.dk + (r0 + t) * K + col);
+        s2[p] = ld2(d.sc_dK + (r0 + t) * K + col);
       }
     });
     acc.zero();
     tc::mma_acc3<1, NI, false, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
     tc::mma_acc3<1, NI, true, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
-      if (t < c)
-        st2(d.dk + row(u, T, t0 + t) * K + col, a[p].x + b2[p].x + v0, a[p].y + b2[p].y + v1);
+      if (t < c) st2(d.dk + (r0 + t) * K + col, a[p].x + s2[p].x + v0, a[p].y + s2[p].y + v1);
     });
   });
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float acc = 0.f;
-    for (int t = c - 1; t >= 0; --t) {
-      acc += dG[t];
-      dG[t] = acc;
+  // dg_t = sum_{s >= t} dG_s (reverse cumsum over the block), then per-token or scalar output
+  if (w == 0) {
+    const int ta = 2 * lane, tb = 2 * lane + 1;
+    const float x0 = ta < c ? dG[ta] : 0.f, x1 = tb < c ? dG[tb] : 0.f;
+    const float pr = x0 + x1;
+    float suf = pr;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_down_sync(0xffffffffu, suf, o);
+      if (lane + o < 32) suf += y;
     }
-  }
-  __syncthreads();
-  if (d.dg64) {
-    if (threadIdx.x == 0) {
-      double sgm = 0.0, sbt = 0.0;
-      for (int t = 0; t < c; ++t) {
-        sgm += dG[t];
-        sbt += db[t];
+    const float after = suf - pr;
+    const float g0 = x0 + x1 + after, g1 = x1 + after;
+    if (d.dg64) {
+      float sg_ = (ta < c ? g0 : 0.f) + (tb < c ? g1 : 0.f);
+      float sb_ = (ta < c ? db[ta] : 0.f) + (tb < c ? db[tb] : 0.f);
+      sg_ = warp_sum(sg_);
+      sb_ = warp_sum(sb_);
+      if (lane == 0) {
+        atomicAdd(&d.dg64[(int64_t)u * d.dg_su], (double)sg_);
+        atomicAdd(&d.dbeta64[(int64_t)u * d.dg_su], (double)sb_);
       }
-      atomicAdd(&d.dg64[(int64_t)u * d.dg_su], sgm);
-      atomicAdd(&d.dbeta64[(int64_t)u * d.dg_su], sbt);
+    } else {
+      if (ta < c) {
+        const int64_t gi = (int64_t)u * d.dg_su + (int64_t)(t0 + ta) * d.dg_st;
+        d.dg[gi] += g0;
+        d.dbeta[gi] += db[ta];
+      }
+      if (tb < c) {
+        const int64_t gi = (int64_t)u * d.dg_su + (int64_t)(t0 + tb) * d.dg_st;
+        d.dg[gi] += g1;
+        d.dbeta[gi] += db[tb];
+      }
     }
-    return;
-  }
-  for (int t = threadIdx.x; t < c; t += blockDim.x) {
-    const int64_t gi = (int64_t)u * d.dg_su + (int64_t)(t0 + t) * d.dg_st;
-    d.dg[gi] += dG[t];
-    d.dbeta[gi] += db[t];
   }
 }
 
@@ -991,11 +958,8 @@ cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaS
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
   cudaError_t e = tc_launch("tc_bwd_state", tc_bwd_state, dim3(U, b.n), max_smem<LBwdState>(b), st, b, U, bl);
   if (e != cudaSuccess) return e;
-  e = tc_launch("tc_bwd_chunk_a", tc_bwd_chunk_a, dim3(U * bl.nb, b.n), max_smem<LBwdA>(b), st,
-                b, U, bl);
-  if (e != cudaSuccess) return e;
-  return tc_launch("tc_bwd_chunk_b", tc_bwd_chunk_b, dim3(U * bl.nb, b.n), max_smem<LBwdB>(b), st,
-                   b, U, bl);
+  return tc_launch("tc_bwd_chunk", tc_bwd_chunk, dim3(U * bl.nb, b.n), max_smem<LBwdChunk>(b),
+                   st, b, U, bl);
 }
 
 }  // namespace gpa
