@@ -33,6 +33,7 @@ using tc::quad_sum;
 using tc::tile_split;
 using tc::tile_to_bf16;
 using tc::tiles_n;
+using tc::TileJob;
 
 constexpr int C = kMaxChunk;  // 64 rows per block tile (zero padded)
 constexpr int kThreads = 512;  // 16 warps: global-load latency of the tile loads is the limiter
@@ -45,6 +46,56 @@ GPA_DEV void load_gates_pad(const ScanDesc& d, int u, int t0, int c, float* G, f
     G[t] = G[c - 1];
     if (bt) bt[t] = 0.f;
   }
+}
+
+// Gates of one block in registers of warp 0 (t = lane, lane + 32), fetched before the tile
+// loads so that their latency overlaps them; gate_finish writes the inclusive cumsum G and
+// beta with the padding of load_gates_pad.
+struct GateRegs {
+  float g0, g1, b0, b1;
+};
+
+GPA_DEV GateRegs gate_fetch(const ScanDesc& d, int u, int t0, int c, bool beta) {
+  GateRegs r{0.f, 0.f, 0.f, 0.f};
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    if (t < c) {
+      r.g0 = gate_at(d.g, d, u, t0 + t);
+      if (beta) r.b0 = gate_at(d.beta, d, u, t0 + t);
+    }
+    if (t + 32 < c) {
+      r.g1 = gate_at(d.g, d, u, t0 + t + 32);
+      if (beta) r.b1 = gate_at(d.beta, d, u, t0 + t + 32);
+    }
+  }
+  return r;
+}
+
+// Ends with __syncthreads (G, bt visible to the block).
+GPA_DEV void gate_finish(const GateRegs& r, int c, float* G, float* bt) {
+  static_assert(C == 64, "two gates per lane");
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    float x0 = r.g0, x1 = r.g1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (t >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    const float last = __shfl_sync(0xffffffffu, c - 1 < 32 ? x0 : x1, (c - 1) & 31);
+    G[t] = t < c ? x0 : last;
+    G[t + 32] = t + 32 < c ? x1 : last;
+    if (bt) {
+      bt[t] = t < c ? r.b0 : 0.f;
+      bt[t + 32] = t + 32 < c ? r.b1 : 0.f;
+    }
+  }
+  __syncthreads();
 }
 
 // T = (I + A)^-1 for a strictly lower 64x64 A (row stride kAStride).  Xs: 768 floats.
@@ -147,10 +198,13 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   bf16* Tgl = (bf16*)(smem + L.Tgl);
   float* G = (float*)(smem + L.G);
   float* bt = (float*)(smem + L.bt);
-  tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Vs, ldv, d.v + row(u, T, t0) * V, V, c, V, C);
-  load_gates_pad(d, u, t0, c, G, bt);
-  __syncthreads();
+  {
+    const GateRegs gr = gate_fetch(d, u, t0, c, true);
+    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
+                            tc::job(Vs, nullptr, ldv, d.v + row(u, T, t0) * V, V, c, V, C)};
+    tc::load_tiles(jobs);
+    gate_finish(gr, c, G, bt);
+  }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
   __syncthreads();
   invert_unit_lower(A, Tm, Xs);
@@ -221,13 +275,15 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blo
     Sb[(i / V) * ldv + (i % V)] = __float2bfloat16(x);
   }
   __syncthreads();
+  GateRegs gr = gate_fetch(d, u, bl.start(0), bl.end(0) - bl.start(0), false);
   for (int n = 0; n < bl.nb; ++n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
     copy_f4(d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, Sf, K * V);
-    tile_split(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C);
-    tile_split(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-    load_gates_pad(d, u, t0, c, G, nullptr);
-    __syncthreads();
+    const TileJob jobs[] = {tc::job(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C),
+                            tc::job(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C)};
+    tc::load_tiles(jobs);
+    gate_finish(gr, c, G, nullptr);
+    if (n + 1 < bl.nb) gr = gate_fetch(d, u, bl.start(n + 1), bl.end(n + 1) - bl.start(n + 1), false);
     for (int t = threadIdx.x; t < C; t += blockDim.x) lam[t] = __expf(G[c - 1] - G[t]);
     __syncthreads();
     // W = U - Wk S
@@ -298,12 +354,16 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
   bf16* Ph = (bf16*)(smem + L.Ph);
   bf16* Pl = (bf16*)(smem + L.Pl);
   float* G = (float*)(smem + L.G);
-  tile_to_bf16(Qs, ldk, d.q + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Ss, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K);
-  tile_split(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
-  load_gates_pad(d, u, t0, c, G, nullptr);
-  __syncthreads();
+  {
+    const GateRegs gr = gate_fetch(d, u, t0, c, false);
+    const TileJob jobs[] = {
+        tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
+        tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
+        tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
+        tc::job(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C)};
+    tc::load_tiles(jobs);
+    gate_finish(gr, c, G, nullptr);
+  }
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {
     Acc<1, 2> acc;
     acc.zero();
@@ -374,14 +434,18 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
   bf16* dXl = (bf16*)(smem + L.dXl);
   float* G = (float*)(smem + L.G);
   float* racc = (float*)(smem + L.racc);
-  tile_to_bf16(Qs, ldk, d.q + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-  tile_to_bf16(Ss, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K);
-  tile_split(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C);
-  tile_to_bf16(dOs, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, dscale(d, u));
   for (int t = threadIdx.x; t < C; t += blockDim.x) racc[t] = 0.f;
-  load_gates_pad(d, u, t0, c, G, nullptr);
-  __syncthreads();
+  {
+    const GateRegs gr = gate_fetch(d, u, t0, c, false);
+    const TileJob jobs[] = {
+        tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
+        tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
+        tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
+        tc::job(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C),
+        tc::job(dOs, nullptr, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, dscale(d, u))};
+    tc::load_tiles(jobs);
+    gate_finish(gr, c, G, nullptr);
+  }
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {
     Acc<1, 2> acc;
     acc.zero();
@@ -460,7 +524,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
 }
 
 struct LBwdState {
-  size_t Dh, Dl, Ks, Qg, Wknh, Wknl, dOs, dWh, dWl, G, lam, total;
+  size_t Dh, Dl, Ks, Qg, Wknh, Wknl, dOs, dWh, dWl, G, lam, eG, total;
   __host__ __device__ LBwdState(int K, int V) {
     Carve c;
     Dh = c.take(2 * K * ld16(V));
@@ -474,6 +538,7 @@ struct LBwdState {
     dWl = c.take(2 * C * ld16(V));
     G = c.take(4 * C);
     lam = c.take(4 * C);
+    eG = c.take(4 * C);
     total = c.off;
   }
 };
@@ -498,6 +563,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
   bf16* dWl = (bf16*)(smem + L.dWl);
   float* G = (float*)(smem + L.G);
   float* lam = (float*)(smem + L.lam);
+  float* eG = (float*)(smem + L.eG);
   const float sc = dscale(d, u);
   for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
     float x = d.ext ? d.ext[((int64_t)u * (bl.nb + 1) + bl.nb) * KV + i] : 0.f;
@@ -505,7 +571,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
     const int o = (i / V) * ldv + (i % V);
     tc::split_bf16(x, Dh + o, Dl + o);
   }
-  __syncthreads();
+  GateRegs gr = gate_fetch(d, u, bl.start(bl.nb - 1), bl.end(bl.nb - 1) - bl.start(bl.nb - 1),
+                           false);
   for (int n = bl.nb - 1; n >= 0; --n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
     float* de = d.Dend + ((int64_t)u * bl.nb + n) * KV;
@@ -513,19 +580,21 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
       const int o = (i / V) * ldv + (i % V);
       de[i] = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
     }
-    load_gates_pad(d, u, t0, c, G, nullptr);
-    __syncthreads();
-    for (int t = threadIdx.x; t < C; t += blockDim.x) lam[t] = __expf(G[c - 1] - G[t]);
-    tile_to_bf16(Ks, ldk, d.k + row(u, T, t0) * K, K, c, K, C);
-    {
-      const float* qr = d.q + row(u, T, t0) * K;
-      for (int i = threadIdx.x; i < C * K; i += blockDim.x) {
-        const int t = i / K, k = i - t * K;
-        Qg[t * ldk + k] = __float2bfloat16(t < c ? qr[(int64_t)t * K + k] * __expf(G[t]) : 0.f);
-      }
+    gate_finish(gr, c, G, nullptr);
+    for (int t = threadIdx.x; t < C; t += blockDim.x) {
+      lam[t] = __expf(G[c - 1] - G[t]);
+      eG[t] = __expf(G[t]);
     }
-    tile_split(Wknh, Wknl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C, -1.f);
-    tile_to_bf16(dOs, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, sc);
+    __syncthreads();
+    if (n > 0) gr = gate_fetch(d, u, bl.start(n - 1), bl.end(n - 1) - bl.start(n - 1), false);
+    {
+      const TileJob jobs[] = {
+          tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
+          tc::job(Qg, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C, 1.f, eG),
+          tc::job(Wknh, Wknl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C, -1.f),
+          tc::job(dOs, nullptr, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, sc)};
+      tc::load_tiles(jobs);
+    }
     __syncthreads();
     // dW = dW_local + lambda (K D)
     tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
@@ -665,14 +734,17 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   const int64_t r0 = row(u, T, t0);
 
   // ---- T = (I + A)^-1 of the block
-  tile_split(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C);
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     dG[t] = t < c ? d.sc_dG[r0 + t] : 0.f;
     db[t] = dlam[t] = rw[t] = 0.f;
   }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
-  load_gates_pad(d, u, t0, c, G, bt);
-  __syncthreads();
+  {
+    const GateRegs gr = gate_fetch(d, u, t0, c, true);
+    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C)};
+    tc::load_tiles(jobs);
+    gate_finish(gr, c, G, bt);
+  }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
   __syncthreads();
   invert_unit_lower(A, Tm, Xs);
@@ -683,10 +755,13 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   __syncthreads();  // pool X (Tm) is reused below
 
   // ---- state-update terms: WD = W D^T, <D, S>, dWk = -dW S^T
-  tile_to_bf16(Sb, ldv, sg, V, K, V, K);
-  tile_to_bf16(Db, ldv, dg, V, K, V, K);
-  tile_to_bf16(Wb, ldv, d.W + r0 * V, V, c, V, C);
-  tile_split(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C);
+  {
+    const TileJob jobs[] = {tc::job(Sb, nullptr, ldv, sg, V, K, V, K),
+                            tc::job(Db, nullptr, ldv, dg, V, K, V, K),
+                            tc::job(Wb, nullptr, ldv, d.W + r0 * V, V, c, V, C),
+                            tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C)};
+    tc::load_tiles(jobs);
+  }
   __syncthreads();
   // sc_dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
@@ -780,8 +855,11 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   __syncthreads();
 
   // ---- Wk path: dRw = T^T dWk ; sc_dK += b e^G dRw ; rw = rowsum(dRw o K) ; M += dWk Wk^T
-  tile_split(Wkh, Wkl, ldk, d.Wk + r0 * K, K, c, K, C);
-  tile_split(dWkh, dWkl, ldk, d.sc_dWk + r0 * K, K, c, K, C);
+  {
+    const TileJob jobs[] = {tc::job(Wkh, Wkl, ldk, d.Wk + r0 * K, K, c, K, C),
+                            tc::job(dWkh, dWkl, ldk, d.sc_dWk + r0 * K, K, c, K, C)};
+    tc::load_tiles(jobs);
+  }
   __syncthreads();
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;

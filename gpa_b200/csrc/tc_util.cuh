@@ -73,6 +73,59 @@ GPA_DEV void tile_split(bf16* hi, bf16* lo, int ld, const float* src, int src_ld
   tile_load(hi, lo, ld, src, src_ld, rows, cols, rows_pad, scale);
 }
 
+// One tile of a batched load: fp32 rows [rows x cols] (row stride src_ld) -> bf16 (hi, and lo
+// when given) [rows_pad x ld], zero padded; each value times `scale` and, when given, the
+// shared-memory row factor rowmul[r].
+struct TileJob {
+  bf16* hi;
+  bf16* lo;
+  int ld;
+  const float* src;
+  int src_ld, rows, cols, rows_pad;
+  float scale;
+  const float* rowmul;
+};
+
+GPA_DEV TileJob job(bf16* hi, bf16* lo, int ld, const float* src, int src_ld, int rows, int cols,
+                    int rows_pad, float scale = 1.f, const float* rowmul = nullptr) {
+  return TileJob{hi, lo, ld, src, src_ld, rows, cols, rows_pad, scale, rowmul};
+}
+
+// Load the tiles one after another (kLoadIlp float4 in flight per thread).  Loading all
+// tiles of a phase in one round (16 float4 per thread) measured slower on B200.
+template <int N>
+GPA_DEV void load_tiles(const TileJob (&jobs)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const TileJob& J = jobs[j];
+    const int c4 = J.cols >> 2, n4 = J.rows_pad * c4;
+    for (int base = threadIdx.x; base < n4; base += blockDim.x * kLoadIlp) {
+      float4 v[kLoadIlp];
+#pragma unroll
+      for (int q = 0; q < kLoadIlp; ++q) {
+        const int i = base + q * blockDim.x;
+        const int r = i / c4, cc = (i - r * c4) << 2;
+        v[q] = (i < n4 && r < J.rows)
+                   ? *reinterpret_cast<const float4*>(J.src + (int64_t)r * J.src_ld + cc)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < kLoadIlp; ++q) {
+        const int i = base + q * blockDim.x;
+        if (i >= n4) break;
+        const int r = i / c4, cc = (i - r * c4) << 2;
+        const float f = J.rowmul ? J.scale * J.rowmul[r] : J.scale;
+        float4 x = v[q];
+        x.x *= f;
+        x.y *= f;
+        x.z *= f;
+        x.w *= f;
+        put4(J.hi, J.lo, r * J.ld + cc, x);
+      }
+    }
+  }
+}
+
 // dst[i] = src[i] for n floats (n multiple of 4, 16-byte aligned), float4 copies
 GPA_DEV void copy_f4(float* dst, const float* src, int n) {
   for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
