@@ -159,22 +159,21 @@ GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const fl
 // ------------------------------------------------------------------ forward
 
 struct LFwdChunk {
-  size_t Ks, Kl, Vs, A, Tm, Xs, Tbh, Tbl, Tgh, Tgl, G, bt, total;
+  // after the inversion, the A + Xs region holds the hi/lo factor of one product at a time
+  size_t Ks, Kl, Vs, A, Xs, Tm, Fh, Fl, G, bt, total;
   __host__ __device__ LFwdChunk(int K, int V) {
     Carve c;
     Ks = c.take(2 * C * ld16(K));
     Kl = c.take(2 * C * ld16(K));
     Vs = c.take(2 * C * ld16(V));
     A = c.take(4 * C * kAStride);
-    Tm = c.take(4 * C * kAStride);
     Xs = c.take(4 * 768);
-    Tbh = c.take(2 * C * LDT);
-    Tbl = c.take(2 * C * LDT);
-    Tgh = c.take(2 * C * LDT);
-    Tgl = c.take(2 * C * LDT);
+    Tm = c.take(4 * C * kAStride);
     G = c.take(4 * C);
     bt = c.take(4 * C);
     total = c.off;
+    Fh = A;
+    Fl = A + 2 * C * LDT;  // 2 * 2 * C * LDT <= 4 * C * kAStride + 4 * 768
   }
 };
 
@@ -192,10 +191,8 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   float* A = (float*)(smem + L.A);
   float* Tm = (float*)(smem + L.Tm);
   float* Xs = (float*)(smem + L.Xs);
-  bf16* Tbh = (bf16*)(smem + L.Tbh);
-  bf16* Tbl = (bf16*)(smem + L.Tbl);
-  bf16* Tgh = (bf16*)(smem + L.Tgh);
-  bf16* Tgl = (bf16*)(smem + L.Tgl);
+  bf16* Fh = (bf16*)(smem + L.Fh);
+  bf16* Fl = (bf16*)(smem + L.Fl);
   float* G = (float*)(smem + L.G);
   float* bt = (float*)(smem + L.bt);
   {
@@ -207,28 +204,33 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
   __syncthreads();
-  invert_unit_lower(A, Tm, Xs);
+  invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
     const int t = i / C, s = i - t * C;
-    const float x = Tm[t * kAStride + s] * bt[s];
-    tc::split_bf16(x, Tbh + t * LDT + s, Tbl + t * LDT + s);
-    tc::split_bf16(x * __expf(G[s]), Tgh + t * LDT + s, Tgl + t * LDT + s);
+    tc::split_bf16(Tm[t * kAStride + s] * bt[s], Fh + t * LDT + s, Fl + t * LDT + s);
   }
   __syncthreads();
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, false, false>(acc, Tbh, Tbl, LDT, Vs, nullptr, ldv, m0, n0, C);
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      if (t < c) d.Ub[row(u, T, t0 + t) * V + col] = v;
+    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Vs, nullptr, ldv, m0, n0, C);
+    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+      if (t < c) st2(d.Ub + row(u, T, t0 + t) * V + col, v0, v1);
     });
   });
+  __syncthreads();
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i - t * C;
+    tc::split_bf16(Tm[t * kAStride + s] * bt[s] * __expf(G[s]), Fh + t * LDT + s,
+                   Fl + t * LDT + s);
+  }
+  __syncthreads();
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, false, false>(acc, Tgh, Tgl, LDT, Ks, Kl, ldk, m0, n0, C);
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      if (t < c) d.Wk[row(u, T, t0 + t) * K + col] = v;
+    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Ks, Kl, ldk, m0, n0, C);
+    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+      if (t < c) st2(d.Wk + row(u, T, t0 + t) * K + col, v0, v1);
     });
   });
 }
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
 GPA_DEV float dscale(const ScanDesc& d, int u) { return d.dO_scale ? d.dO_scale[u] : 1.f; }
 
 struct LBwdLocal {
-  size_t Qs, Ks, Ss, Wh, Wl, dOs, Pf, dPf, Ph, Pl, dXh, dXl, G, racc, total;
+  size_t Qs, Ks, Ss, Wh, Wl, dOs, Ph, Pl, dXh, dXl, G, racc, rs, cs, total;
   __host__ __device__ LBwdLocal(int K, int V) {
     Carve c;
     Qs = c.take(2 * C * ld16(K));
@@ -399,14 +401,14 @@ struct LBwdLocal {
     Wh = c.take(2 * C * ld16(V));
     Wl = c.take(2 * C * ld16(V));
     dOs = c.take(2 * C * ld16(V));
-    Pf = c.take(4 * C * kAStride);
-    dPf = c.take(4 * C * kAStride);
     Ph = c.take(2 * C * LDT);
     Pl = c.take(2 * C * LDT);
     dXh = c.take(2 * C * LDT);
     dXl = c.take(2 * C * LDT);
     G = c.take(4 * C);
     racc = c.take(4 * C);
+    rs = c.take(4 * C);
+    cs = c.take(4 * C);
     total = c.off;
   }
 };
@@ -426,15 +428,15 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
   bf16* Wh = (bf16*)(smem + L.Wh);
   bf16* Wl = (bf16*)(smem + L.Wl);
   bf16* dOs = (bf16*)(smem + L.dOs);
-  float* Pf = (float*)(smem + L.Pf);
-  float* dPf = (float*)(smem + L.dPf);
   bf16* Ph = (bf16*)(smem + L.Ph);
   bf16* Pl = (bf16*)(smem + L.Pl);
   bf16* dXh = (bf16*)(smem + L.dXh);
   bf16* dXl = (bf16*)(smem + L.dXl);
   float* G = (float*)(smem + L.G);
   float* racc = (float*)(smem + L.racc);
-  for (int t = threadIdx.x; t < C; t += blockDim.x) racc[t] = 0.f;
+  float* rs = (float*)(smem + L.rs);
+  float* cs = (float*)(smem + L.cs);
+  for (int t = threadIdx.x; t < C; t += blockDim.x) racc[t] = rs[t] = cs[t] = 0.f;
   {
     const GateRegs gr = gate_fetch(d, u, t0, c, false);
     const TileJob jobs[] = {
@@ -446,18 +448,46 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
     tc::load_tiles(jobs);
     gate_finish(gr, c, G, nullptr);
   }
+  // P = (Q K^T) o Gamma and dP = dO W^T on the same tile: rowsum / colsum of P o dP and
+  // dX = dP o Gamma straight from the accumulators
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
-    acc.zero();
-    mma_acc<1, 2, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
-    acc.each(m0, n0, [&](int t, int s, float& v) {
-      const float p = s <= t ? __expf(G[t] - G[s]) * v : 0.f;
-      Pf[t * kAStride + s] = p;
-      tc::split_bf16(p, Ph + t * LDT + s, Pl + t * LDT + s);
+    Acc<1, 2> pa, da;
+    pa.zero();
+    mma_acc<1, 2, false, true>(pa, Qs, ldk, Ks, ldk, m0, n0, K);
+    pa.each(m0, n0, [&](int t, int s, float& v) {
+      v = s <= t ? __expf(G[t] - G[s]) * v : 0.f;
+      tc::split_bf16(v, Ph + t * LDT + s, Pl + t * LDT + s);
     });
-    acc.zero();
-    tc::mma_acc3<1, 2, false, true>(acc, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
-    acc.each(m0, n0, [&](int t, int s, float& v) { dPf[t * kAStride + s] = s <= t ? v : 0.f; });
+    da.zero();
+    tc::mma_acc3<1, 2, false, true>(da, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    float rsum[2] = {0.f, 0.f}, csum[4][2] = {};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = m0 + g + 8 * (r >> 1), s = n0 + 8 * j + 2 * q + (r & 1);
+        const float dp = s <= t ? da.v[0][j][r] : 0.f;
+        const float pr = pa.v[0][j][r] * dp;
+        rsum[r >> 1] += pr;
+        csum[j][r & 1] += pr;
+        tc::split_bf16(s <= t ? dp * __expf(G[t] - G[s]) : 0.f, dXh + t * LDT + s, dXl + t * LDT + s);
+      }
+    const float r0s = quad_sum(rsum[0]), r1s = quad_sum(rsum[1]);
+    if (q == 0) {
+      atomicAdd(&rs[m0 + g], r0s);
+      atomicAdd(&rs[m0 + g + 8], r1s);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float x = csum[j][h];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        if (g == 0) atomicAdd(&cs[n0 + 8 * j + 2 * q + h], x);
+      }
   });
   // rowsum(dO o (Q S_n))
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
@@ -476,19 +506,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
     }
   });
   __syncthreads();
-  if (threadIdx.x < C) {
-    const int t = threadIdx.x;
-    float rs = 0.f, cs = 0.f;
-    for (int s = 0; s <= t; ++s) rs += dPf[t * kAStride + s] * Pf[t * kAStride + s];
-    for (int r = t; r < C; ++r) cs += dPf[r * kAStride + t] * Pf[r * kAStride + t];
-    if (t < c) d.sc_dG[row(u, T, t0 + t)] = __expf(G[t]) * racc[t] + rs - cs;
-  }
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    const float x = s <= t ? dPf[t * kAStride + s] * __expf(G[t] - G[s]) : 0.f;
-    tc::split_bf16(x, dXh + t * LDT + s, dXl + t * LDT + s);
-  }
-  __syncthreads();
+  for (int t = threadIdx.x; t < c; t += blockDim.x)
+    d.sc_dG[row(u, T, t0 + t)] = __expf(G[t]) * racc[t] + rs[t] - cs[t];
   if (d.dq) {
     tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
@@ -996,14 +1015,27 @@ cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStre
   return cudaGetLastError();
 }
 
-template <class Lay>
-size_t max_smem(const ScanBatch& b) {
-  size_t m = 0;
+// Launch one kernel per group of scans with the same (K, V): each group gets the shared
+// memory its own shape needs, so narrow scans fit more CTAs per SM.
+template <class Lay, class Kern>
+cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& b, int U,
+                             const Blocks& bl, cudaStream_t st) {
+  bool done[kMaxScans] = {};
   for (int i = 0; i < b.n; ++i) {
-    const size_t s = Lay(b.s[i].K, b.s[i].V).total;
-    m = s > m ? s : m;
+    if (done[i]) continue;
+    ScanBatch sub;
+    sub.tc = b.tc;
+    sub.n = 0;
+    for (int j = i; j < b.n; ++j)
+      if (!done[j] && b.s[j].K == b.s[i].K && b.s[j].V == b.s[i].V) {
+        sub.s[sub.n++] = b.s[j];
+        done[j] = true;
+      }
+    const cudaError_t e = tc_launch(name, k, dim3(gx, sub.n), Lay(b.s[i].K, b.s[i].V).total, st,
+                                    sub, U, bl);
+    if (e != cudaSuccess) return e;
   }
-  return m;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -1014,30 +1046,26 @@ bool tc_supported(int K, int V) {
 
 cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
                        cudaStream_t st) {
-  cudaError_t e = tc_launch("tc_fwd_chunk", tc_fwd_chunk, dim3(U * bl.nb, b.n),
-                            max_smem<LFwdChunk>(b), st, b, U, bl);
+  cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st);
   if (e != cudaSuccess) return e;
-  e = tc_launch("tc_fwd_state", tc_fwd_state, dim3(U, b.n), max_smem<LFwdState>(b), st, b, U, bl);
+  e = tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U, bl, st);
   if (e != cudaSuccess || !with_output) return e;
   return tc_output(b, U, bl, st);
 }
 
 cudaError_t tc_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  return tc_launch("tc_fwd_out", tc_fwd_out, dim3(U * bl.nb, b.n), max_smem<LFwdOut>(b), st, b,
-                   U, bl);
+  return tc_launch_groups<LFwdOut>("tc_fwd_out", tc_fwd_out, U * bl.nb, b, U, bl, st);
 }
 
 cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  return tc_launch("tc_bwd_local", tc_bwd_local, dim3(U * bl.nb, b.n), max_smem<LBwdLocal>(b),
-                   st, b, U, bl);
+  return tc_launch_groups<LBwdLocal>("tc_bwd_local", tc_bwd_local, U * bl.nb, b, U, bl, st);
 }
 
 // U and Wk of every block come from the forward (kept in the saved buffer).
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  cudaError_t e = tc_launch("tc_bwd_state", tc_bwd_state, dim3(U, b.n), max_smem<LBwdState>(b), st, b, U, bl);
+  cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st);
   if (e != cudaSuccess) return e;
-  return tc_launch("tc_bwd_chunk", tc_bwd_chunk, dim3(U * bl.nb, b.n), max_smem<LBwdChunk>(b),
-                   st, b, U, bl);
+  return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st);
 }
 
 }  // namespace gpa
