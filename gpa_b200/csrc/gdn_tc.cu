@@ -235,29 +235,56 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   });
 }
 
+// The state sweeps are split over value columns: W = U - Wk S and S <- e^{G_c} S + K^T
+// diag(lambda) W (and the same for D, dW) never mix columns, so each CTA carries one slice
+// of VS columns of the state.  VS keeps the shared memory of a CTA at or under 113 KB (two
+// CTAs per SM) for widths up to 128.
+constexpr int kStateThreads = 256;
+
+__host__ __device__ inline int state_slice(int K, int V) {
+  const int cap = K > 64 ? 32 : 64;  // V is a multiple of 16
+  for (int vs = cap; vs > 16; vs >>= 1)
+    if (V % vs == 0) return vs;
+  return 16;
+}
+
+__host__ __device__ inline int state_slices(int K, int V) { return V / state_slice(K, V); }
+
+// 16x32 tiles when they keep every warp busy, else 16x16
+template <class Body>
+GPA_DEV void tiles_spread(int M, int N, Body body) {
+  if (N % 32 == 0 && (M / 16) * (N / 32) >= (int)(blockDim.x >> 5))
+    tc::for_tiles<1, 2>(M, N, [&](int m0, int n0) { body.template operator()<2>(m0, n0); });
+  else
+    tc::for_tiles<1, 1>(M, N, [&](int m0, int n0) { body.template operator()<1>(m0, n0); });
+}
+
 struct LFwdState {
   size_t Sf, Sb, Wkh, Wkl, Ks, Kl, Wch, Wcl, G, lam, total;
   __host__ __device__ LFwdState(int K, int V) {
+    const int VS = state_slice(K, V);
     Carve c;
-    Sf = c.take(4 * K * V);
-    Sb = c.take(2 * K * ld16(V));
+    Sf = c.take(4 * K * VS);
+    Sb = c.take(2 * K * ld16(VS));
     Wkh = c.take(2 * C * ld16(K));
     Wkl = c.take(2 * C * ld16(K));
     Ks = c.take(2 * C * ld16(K));
     Kl = c.take(2 * C * ld16(K));
-    Wch = c.take(2 * C * ld16(V));
-    Wcl = c.take(2 * C * ld16(V));
+    Wch = c.take(2 * C * ld16(VS));
+    Wcl = c.take(2 * C * ld16(VS));
     G = c.take(4 * C);
     lam = c.take(4 * C);
     total = c.off;
   }
 };
 
-// grid (U, nscan): sequential over blocks, full state [K x V] fp32 in shared memory.
-__global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blocks bl) {
+// grid (U * slices, nscan): sequential over blocks, one column slice of the state [K x VS]
+// fp32 in shared memory.
+__global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
-  const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
-  const int ldk = ld16(K), ldv = ld16(V);
+  const int K = d.K, V = d.V, VS = state_slice(K, V), nvs = V / VS;
+  const int u = blockIdx.x / nvs, v0 = (blockIdx.x % nvs) * VS, T = bl.T;
+  const int ldk = ld16(K), lds = ld16(VS);
   const int64_t KV = (int64_t)K * V;
   extern __shared__ __align__(16) unsigned char smem[];
   const LFwdState L(K, V);
@@ -271,16 +298,26 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blo
   bf16* Wcl = (bf16*)(smem + L.Wcl);
   float* G = (float*)(smem + L.G);
   float* lam = (float*)(smem + L.lam);
-  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
-    const float x = d.S0[u * KV + i];
-    Sf[i] = x;
-    Sb[(i / V) * ldv + (i % V)] = __float2bfloat16(x);
+  const int q4 = VS >> 2;  // float4 per slice row
+  // state slice rows k: global [k * V + v0, + VS)
+  auto put_slice = [&](float* dst) {
+    for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
+      const int k = i / q4, j = (i - k * q4) << 2;
+      *reinterpret_cast<float4*>(dst + (int64_t)k * V + v0 + j) =
+          *reinterpret_cast<const float4*>(Sf + k * VS + j);
+    }
+  };
+  for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
+    const int k = i / q4, j = (i - k * q4) << 2;
+    const float4 x = *reinterpret_cast<const float4*>(d.S0 + u * KV + (int64_t)k * V + v0 + j);
+    *reinterpret_cast<float4*>(Sf + k * VS + j) = x;
+    tc::put4(Sb, nullptr, k * lds + j, x);
   }
   __syncthreads();
   GateRegs gr = gate_fetch(d, u, bl.start(0), bl.end(0) - bl.start(0), false);
   for (int n = 0; n < bl.nb; ++n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
-    copy_f4(d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, Sf, K * V);
+    put_slice(d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV);
     const TileJob jobs[] = {tc::job(Wkh, Wkl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C),
                             tc::job(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C)};
     tc::load_tiles(jobs);
@@ -288,38 +325,38 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_state(ScanBatch b, int U, Blo
     if (n + 1 < bl.nb) gr = gate_fetch(d, u, bl.start(n + 1), bl.end(n + 1) - bl.start(n + 1), false);
     for (int t = threadIdx.x; t < C; t += blockDim.x) lam[t] = __expf(G[c - 1] - G[t]);
     __syncthreads();
-    // W = U - Wk S
-    tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    // W = U - Wk S (slice columns)
+    tiles_spread(C, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
       float2 ub[Acc<1, NI>::kPairs];
       acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-        ub[p] = t < c ? ld2(d.Ub + row(u, T, t0 + t) * V + col) : make_float2(0.f, 0.f);
+        ub[p] = t < c ? ld2(d.Ub + row(u, T, t0 + t) * V + v0 + col) : make_float2(0.f, 0.f);
       });
       acc.zero();
-      tc::mma_acc3<1, NI, false, false>(acc, Wkh, Wkl, ldk, Sb, nullptr, ldv, m0, n0, K);
-      acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
-        const float w0 = t < c ? ub[p].x - v0 : 0.f, w1 = t < c ? ub[p].y - v1 : 0.f;
-        if (t < c) st2(d.W + row(u, T, t0 + t) * V + col, w0, w1);
-        tc::split_bf16(w0 * lam[t], Wch + t * ldv + col, Wcl + t * ldv + col);
-        tc::split_bf16(w1 * lam[t], Wch + t * ldv + col + 1, Wcl + t * ldv + col + 1);
+      tc::mma_acc3<1, NI, false, false>(acc, Wkh, Wkl, ldk, Sb, nullptr, lds, m0, n0, K);
+      acc.each2(m0, n0, [&](int p, int t, int col, float& x0, float& x1) {
+        const float w0 = t < c ? ub[p].x - x0 : 0.f, w1 = t < c ? ub[p].y - x1 : 0.f;
+        if (t < c) st2(d.W + row(u, T, t0 + t) * V + v0 + col, w0, w1);
+        tc::split_bf16(w0 * lam[t], Wch + t * lds + col, Wcl + t * lds + col);
+        tc::split_bf16(w1 * lam[t], Wch + t * lds + col + 1, Wcl + t * lds + col + 1);
       });
     });
     __syncthreads();
     const float gc = __expf(G[c - 1]);
     // S = e^{G_c} S + K^T diag(lambda) W
-    tiles_n<1, 2>(K, V, [&]<int NI>(int m0, int n0) {
+    tiles_spread(K, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
-      acc.each(m0, n0, [&](int k, int col, float& v) { v = gc * Sf[k * V + col]; });
-      tc::mma_acc3<1, NI, true, false>(acc, Ks, Kl, ldk, Wch, Wcl, ldv, m0, n0, C);
-      acc.each(m0, n0, [&](int k, int col, float& v) {
-        Sf[k * V + col] = v;
-        Sb[k * ldv + col] = __float2bfloat16(v);
+      acc.each(m0, n0, [&](int k, int col, float& x) { x = gc * Sf[k * VS + col]; });
+      tc::mma_acc3<1, NI, true, false>(acc, Ks, Kl, ldk, Wch, Wcl, lds, m0, n0, C);
+      acc.each(m0, n0, [&](int k, int col, float& x) {
+        Sf[k * VS + col] = x;
+        Sb[k * lds + col] = __float2bfloat16(x);
       });
     });
     __syncthreads();
   }
-  copy_f4(d.Sb + ((int64_t)u * (bl.nb + 1) + bl.nb) * KV, Sf, K * V);
-  if (d.S_final) copy_f4(d.S_final + u * KV, Sf, K * V);
+  put_slice(d.Sb + ((int64_t)u * (bl.nb + 1) + bl.nb) * KV);
+  if (d.S_final) put_slice(d.S_final + u * KV);
 }
 
 struct LFwdOut {
@@ -545,16 +582,17 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
 struct LBwdState {
   size_t Dh, Dl, Ks, Qg, Wknh, Wknl, dOs, dWh, dWl, G, lam, eG, total;
   __host__ __device__ LBwdState(int K, int V) {
+    const int VS = state_slice(K, V);
     Carve c;
-    Dh = c.take(2 * K * ld16(V));
-    Dl = c.take(2 * K * ld16(V));
+    Dh = c.take(2 * K * ld16(VS));
+    Dl = c.take(2 * K * ld16(VS));
     Ks = c.take(2 * C * ld16(K));
     Qg = c.take(2 * C * ld16(K));
     Wknh = c.take(2 * C * ld16(K));
     Wknl = c.take(2 * C * ld16(K));
-    dOs = c.take(2 * C * ld16(V));
-    dWh = c.take(2 * C * ld16(V));
-    dWl = c.take(2 * C * ld16(V));
+    dOs = c.take(2 * C * ld16(VS));
+    dWh = c.take(2 * C * ld16(VS));
+    dWl = c.take(2 * C * ld16(VS));
     G = c.take(4 * C);
     lam = c.take(4 * C);
     eG = c.take(4 * C);
@@ -562,12 +600,13 @@ struct LBwdState {
   }
 };
 
-// grid (U, nscan): reverse sweep; D = dS at block ends; dW = dW_local + lambda K D.
-// D is carried as a hi/lo bf16 pair (~16 significant bits) between blocks.
-__global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blocks bl) {
+// grid (U * slices, nscan): reverse sweep over one column slice; D = dS at block ends;
+// dW = dW_local + lambda K D.  D is carried as a hi/lo bf16 pair (~16 significant bits).
+__global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
-  const int u = blockIdx.x, T = bl.T, K = d.K, V = d.V;
-  const int ldk = ld16(K), ldv = ld16(V);
+  const int K = d.K, V = d.V, VS = state_slice(K, V), nvs = V / VS;
+  const int u = blockIdx.x / nvs, v0 = (blockIdx.x % nvs) * VS, T = bl.T;
+  const int ldk = ld16(K), lds = ld16(VS);
   const int64_t KV = (int64_t)K * V;
   extern __shared__ __align__(16) unsigned char smem[];
   const LBwdState L(K, V);
@@ -584,21 +623,39 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
   float* lam = (float*)(smem + L.lam);
   float* eG = (float*)(smem + L.eG);
   const float sc = dscale(d, u);
-  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
-    float x = d.ext ? d.ext[((int64_t)u * (bl.nb + 1) + bl.nb) * KV + i] : 0.f;
-    if (d.dS_final) x += d.dS_final[u * KV + i];
-    const int o = (i / V) * ldv + (i % V);
-    tc::split_bf16(x, Dh + o, Dl + o);
+  const int q4 = VS >> 2;
+  for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
+    const int k = i / q4, j = (i - k * q4) << 2;
+    const int64_t o = (int64_t)k * V + v0 + j;
+    float4 x = d.ext ? *reinterpret_cast<const float4*>(d.ext + ((int64_t)u * (bl.nb + 1) + bl.nb) * KV + o)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (d.dS_final) {
+      const float4 y = *reinterpret_cast<const float4*>(d.dS_final + u * KV + o);
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
+    tc::put4(Dh, Dl, k * lds + j, x);
   }
+  // D (hi + lo) -> fp32 rows of a global [K x V] array, this slice's columns
+  auto get_slice = [&](float* dst) {
+    for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
+      const int k = i / q4, j = (i - k * q4) << 2, o = k * lds + j;
+      float4 x;
+      x.x = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
+      x.y = __bfloat162float(Dh[o + 1]) + __bfloat162float(Dl[o + 1]);
+      x.z = __bfloat162float(Dh[o + 2]) + __bfloat162float(Dl[o + 2]);
+      x.w = __bfloat162float(Dh[o + 3]) + __bfloat162float(Dl[o + 3]);
+      *reinterpret_cast<float4*>(dst + (int64_t)k * V + v0 + j) = x;
+    }
+  };
+  __syncthreads();
   GateRegs gr = gate_fetch(d, u, bl.start(bl.nb - 1), bl.end(bl.nb - 1) - bl.start(bl.nb - 1),
                            false);
   for (int n = bl.nb - 1; n >= 0; --n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
-    float* de = d.Dend + ((int64_t)u * bl.nb + n) * KV;
-    for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
-      const int o = (i / V) * ldv + (i % V);
-      de[i] = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
-    }
+    get_slice(d.Dend + ((int64_t)u * bl.nb + n) * KV);
     gate_finish(gr, c, G, nullptr);
     for (int t = threadIdx.x; t < C; t += blockDim.x) {
       lam[t] = __expf(G[c - 1] - G[t]);
@@ -611,52 +668,49 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_state(ScanBatch b, int U, Blo
           tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
           tc::job(Qg, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C, 1.f, eG),
           tc::job(Wknh, Wknl, ldk, d.Wk + row(u, T, t0) * K, K, c, K, C, -1.f),
-          tc::job(dOs, nullptr, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, sc)};
+          tc::job(dOs, nullptr, lds, d.dO + row(u, T, t0) * V + v0, V, c, VS, C, sc)};
       tc::load_tiles(jobs);
     }
     __syncthreads();
     // dW = dW_local + lambda (K D)
-    tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+    tiles_spread(C, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
       float2 dw[Acc<1, NI>::kPairs];
       acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-        dw[p] = t < c ? ld2(d.sc_dW + row(u, T, t0 + t) * V + col) : make_float2(0.f, 0.f);
+        dw[p] = t < c ? ld2(d.sc_dW + row(u, T, t0 + t) * V + v0 + col) : make_float2(0.f, 0.f);
       });
       acc.zero();
-      tc::mma_acc3<1, NI, false, false>(acc, Ks, nullptr, ldk, Dh, Dl, ldv, m0, n0, K);
-      acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
-        const float w0 = t < c ? dw[p].x + lam[t] * v0 : 0.f;
-        const float w1 = t < c ? dw[p].y + lam[t] * v1 : 0.f;
-        if (t < c) st2(d.sc_dW + row(u, T, t0 + t) * V + col, w0, w1);
-        tc::split_bf16(w0, dWh + t * ldv + col, dWl + t * ldv + col);
-        tc::split_bf16(w1, dWh + t * ldv + col + 1, dWl + t * ldv + col + 1);
+      tc::mma_acc3<1, NI, false, false>(acc, Ks, nullptr, ldk, Dh, Dl, lds, m0, n0, K);
+      acc.each2(m0, n0, [&](int p, int t, int col, float& x0, float& x1) {
+        const float w0 = t < c ? dw[p].x + lam[t] * x0 : 0.f;
+        const float w1 = t < c ? dw[p].y + lam[t] * x1 : 0.f;
+        if (t < c) st2(d.sc_dW + row(u, T, t0 + t) * V + v0 + col, w0, w1);
+        tc::split_bf16(w0, dWh + t * lds + col, dWl + t * lds + col);
+        tc::split_bf16(w1, dWh + t * lds + col + 1, dWl + t * lds + col + 1);
       });
     });
     __syncthreads();
     const float gc = __expf(G[c - 1]);
-    const float* ext = d.ext ? d.ext + ((int64_t)u * (bl.nb + 1) + n) * KV : nullptr;
+    const float* ext = d.ext ? d.ext + ((int64_t)u * (bl.nb + 1) + n) * KV + v0 : nullptr;
     // D <- e^{G_c} D + (e^G Q)^T dO - Wk^T dW + ext_n
-    tiles_n<1, 2>(K, V, [&]<int NI>(int m0, int n0) {
+    tiles_spread(K, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
-      acc.each(m0, n0, [&](int k, int col, float& v) {
-        const int o = k * ldv + col;
-        v = gc * (__bfloat162float(Dh[o]) + __bfloat162float(Dl[o])) +
-            (ext ? ext[k * V + col] : 0.f);
+      acc.each(m0, n0, [&](int k, int col, float& x) {
+        const int o = k * lds + col;
+        x = gc * (__bfloat162float(Dh[o]) + __bfloat162float(Dl[o])) +
+            (ext ? ext[(int64_t)k * V + col] : 0.f);
       });
-      mma_acc<1, NI, true, false>(acc, Qg, ldk, dOs, ldv, m0, n0, C);
-      tc::mma_acc3<1, NI, true, false>(acc, Wknh, Wknl, ldk, dWh, dWl, ldv, m0, n0, C);
+      mma_acc<1, NI, true, false>(acc, Qg, ldk, dOs, lds, m0, n0, C);
+      tc::mma_acc3<1, NI, true, false>(acc, Wknh, Wknl, ldk, dWh, dWl, lds, m0, n0, C);
       __syncwarp();
-      acc.each(m0, n0, [&](int k, int col, float& v) {
-        const int o = k * ldv + col;
-        tc::split_bf16(v, Dh + o, Dl + o);
+      acc.each(m0, n0, [&](int k, int col, float& x) {
+        const int o = k * lds + col;
+        tc::split_bf16(x, Dh + o, Dl + o);
       });
     });
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < K * V; i += blockDim.x) {
-    const int o = (i / V) * ldv + (i % V);
-    d.dS0[u * KV + i] = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
-  }
+  get_slice(d.dS0 + u * KV);
 }
 
 struct LBwdChunk {
@@ -1005,21 +1059,22 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
 
 template <class Kern>
 cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStream_t st,
-                      const ScanBatch& b, int U, const Blocks& bl) {
+                      const ScanBatch& b, int U, const Blocks& bl, int threads = kThreads) {
   if (grid.x == 0 || grid.y == 0) return cudaSuccess;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   Launch scope(name, st);
-  k<<<grid, kThreads, smem, st>>>(b, U, bl);
+  k<<<grid, threads, smem, st>>>(b, U, bl);
   return cudaGetLastError();
 }
 
 // Launch one kernel per group of scans with the same (K, V): each group gets the shared
 // memory its own shape needs, so narrow scans fit more CTAs per SM.
+// gx: CTAs per scan along x; with `sliced`, times the state slices of the group's shape.
 template <class Lay, class Kern>
 cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& b, int U,
-                             const Blocks& bl, cudaStream_t st) {
+                             const Blocks& bl, cudaStream_t st, bool sliced = false) {
   bool done[kMaxScans] = {};
   for (int i = 0; i < b.n; ++i) {
     if (done[i]) continue;
@@ -1031,8 +1086,10 @@ cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& 
         sub.s[sub.n++] = b.s[j];
         done[j] = true;
       }
-    const cudaError_t e = tc_launch(name, k, dim3(gx, sub.n), Lay(b.s[i].K, b.s[i].V).total, st,
-                                    sub, U, bl);
+    const int K = b.s[i].K, V = b.s[i].V;
+    const int x = sliced ? gx * state_slices(K, V) : gx;
+    const cudaError_t e = tc_launch(name, k, dim3(x, sub.n), Lay(K, V).total, st, sub, U, bl,
+                                    sliced ? kStateThreads : kThreads);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -1048,7 +1105,7 @@ cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_ou
                        cudaStream_t st) {
   cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st);
   if (e != cudaSuccess) return e;
-  e = tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U, bl, st);
+  e = tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess || !with_output) return e;
   return tc_output(b, U, bl, st);
 }
@@ -1063,7 +1120,7 @@ cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaS
 
 // U and Wk of every block come from the forward (kept in the saved buffer).
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st);
+  cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess) return e;
   return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st);
 }
