@@ -44,12 +44,13 @@ size_t smem_of(int a, int b, int c) { return Lay(a, b, c).total; }
 // ------------------------------------------------------------------ prep
 
 struct LPrep {
-  size_t Kb, Cb, St, total;
+  size_t Kb, Cb, St, Wg4, total;
   __host__ __device__ LPrep(int D, int M, int) {
     Carve c;
     Kb = c.take(2 * R * ld16(D));
     Cb = c.take(2 * M * ld16(D));
     St = c.take(4 * R * M);
+    Wg4 = c.take(4 * 4 * D);
     total = c.off;
   }
 };
@@ -71,19 +72,27 @@ __global__ void __launch_bounds__(256) tk_level_prep(int U, int T, int H, int D,
   float* St = (float*)(smem + L.St);
   tile_to_bf16(Kb, ld16(D), key + row(u, T, t0) * D, D, c, D, R);
   tile_to_bf16(Cb, ld16(D), C + (int64_t)h * M * D, D, M, D, M);
-  const float* wg = Wg + (int64_t)h * D * 4;
+  float* Wg4 = (float*)(smem + L.Wg4);
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    *reinterpret_cast<float4*>(Wg4 + 4 * i) = *reinterpret_cast<const float4*>(Wg + ((int64_t)h * D + i) * 4);
+  __syncthreads();
   for (int t = warp; t < c; t += nw) {
-    const float* kr = key + row(u, T, t0 + t) * D;
-    float ss = 0.f;
-    for (int d = lane; d < D; d += 32) ss += kr[d] * kr[d];
-    const float nrm = sqrtf(warp_sum(ss));
+    float kx[kMaxPerLane];
+    load_vec(kx, key + row(u, T, t0 + t) * D, D);
+    const float nrm = warp_norm(kx, D);
     const float inv = 1.f / fmaxf(nrm, kUnitEps);
     float r[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int d = lane; d < D; d += 32) {
-      const float x = kr[d] * inv;
-      nk[row(u, T, t0 + t) * D + d] = x;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) r[cc] += x * wg[d * 4 + cc];
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int d = lane + 32 * i;
+      if (d >= D) break;
+      const float x = kx[i] * inv;
+      nk[row(u, T, t0 + t) * D + d] = x;
+      const float4 w4 = *reinterpret_cast<const float4*>(Wg4 + 4 * d);
+      r[0] += x * w4.x;
+      r[1] += x * w4.y;
+      r[2] += x * w4.z;
+      r[3] += x * w4.w;
     }
 #pragma unroll
     for (int cc = 0; cc < 4; ++cc) r[cc] = warp_sum(r[cc]) + gbias[h * 4 + cc];
@@ -416,9 +425,11 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   __syncthreads();
   {
     float part = 0.f;
-    for (int i = threadIdx.x; i < c * M; i += blockDim.x) {
-      const int t = i / M, m = i - t * M;
-      part += Rf[i] * mlp[row(u, T, t0 + t) * M + m];
+    const float* mr = mlp + row(u, T, t0) * M;  // c rows, contiguous
+    for (int i = 4 * threadIdx.x; i < c * M; i += 4 * blockDim.x) {
+      const float4 a = *reinterpret_cast<const float4*>(mr + i);
+      const float4 r4 = *reinterpret_cast<const float4*>(Rf + i);
+      part += a.x * r4.x + a.y * r4.y + a.z * r4.z + a.w * r4.w;
     }
     const float s = block_sum(part, red);
     if (threadIdx.x == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_MlpGain], (double)s);
@@ -429,16 +440,21 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   // dhp = mg (droute D^T) o gelu'(hp)
   tiles_n<1, 2>(R, 2 * M, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
+    float2 hv[Acc<1, NI>::kPairs];
+    acc.each2(m0, n0, [&](int p, int t, int rr, float&, float&) {
+      if (t < c) hv[p] = tc::ld2(hp + row(u, T, t0 + t) * 2 * M + rr);
+    });
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Rb, lm, Wbuf, lm, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int rr, float& v) {
-      float x = 0.f;
+    acc.each2(m0, n0, [&](int p, int t, int rr, float& v0, float& v1) {
+      float x0 = 0.f, x1 = 0.f;
       if (t < c) {
-        const int64_t o = row(u, T, t0 + t) * 2 * M + rr;
-        x = mg * v * gelu_grad(hp[o]);
-        dhp_out[o] = x;
+        x0 = mg * v0 * gelu_grad(hv[p].x);
+        x1 = mg * v1 * gelu_grad(hv[p].y);
+        tc::st2(dhp_out + row(u, T, t0 + t) * 2 * M + rr, x0, x1);
       }
-      tc::split_bf16(x, Hb + t * lh + rr, Hl + t * lh + rr);
+      tc::split_bf16(x0, Hb + t * lh + rr, Hl + t * lh + rr);
+      tc::split_bf16(x1, Hb + t * lh + rr + 1, Hl + t * lh + rr + 1);
     });
   });
   __syncthreads();
@@ -521,11 +537,13 @@ __global__ void __launch_bounds__(256) tk_post_bwd(
                D, M, D);
   tile_to_bf16(Wb, lm, write + row(u, T, t0) * M, M, c, M, R);
   tile_to_bf16(Nk, ld, nk + row(u, T, t0) * D, D, c, D, R);
-  for (int i = threadIdx.x; i < R * M; i += blockDim.x) {
-    const int t = i / M, m = i - t * M;
-    const int64_t o = row(u, T, t0 + t) * M + m;
-    Wf[i] = t < c ? write[o] : 0.f;
-    dWf[i] = t < c ? dwrite[o] : 0.f;
+  for (int i = 4 * threadIdx.x; i < R * M; i += 4 * blockDim.x) {
+    const bool in = i < c * M;  // rows t < c are contiguous from t0
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 a = in ? *reinterpret_cast<const float4*>(write + row(u, T, t0) * M + i) : z;
+    const float4 b4 = in ? *reinterpret_cast<const float4*>(dwrite + row(u, T, t0) * M + i) : z;
+    *reinterpret_cast<float4*>(Wf + i) = a;
+    *reinterpret_cast<float4*>(dWf + i) = b4;
   }
   if (with_residual) {
     tile_to_bf16(Bf, lv, frozen_at(Bbnd, fz0 ? fzB : nullptr, u, n, bl.nb, post, (int64_t)M * Dv),
@@ -627,11 +645,12 @@ __global__ void __launch_bounds__(256) tk_post_bwd(
 // ------------------------------------------------------------- prep backward
 
 struct LPrepBwd {
-  size_t Dsb, Cb, total;
+  size_t Dsb, Cb, Wg4, total;
   __host__ __device__ LPrepBwd(int D, int M, int) {
     Carve c;
     Dsb = c.take(2 * R * ld16(M));
     Cb = c.take(2 * M * ld16(D));
+    Wg4 = c.take(4 * 4 * D);
     total = c.off;
   }
 };
@@ -654,43 +673,50 @@ __global__ void __launch_bounds__(256) tk_prep_bwd(int U, int T, int H, int D, i
   bf16* Cb = (bf16*)(smem + Lp.Cb);
   const int lm = ld16(M);
   tile_to_bf16(Cb, ld16(D), C + (int64_t)h * M * D, D, M, D, M);
-  const float* wg = Wg + (int64_t)h * D * 4;
+  float* Wg4 = (float*)(smem + Lp.Wg4);
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    *reinterpret_cast<float4*>(Wg4 + 4 * i) = *reinterpret_cast<const float4*>(Wg + ((int64_t)h * D + i) * 4);
+  __syncthreads();
   for (int t = warp; t < R; t += nw) {
     float base[kMaxPerLane];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
-      float d4[4] = {0.f, 0.f, 0.f, 0.f};
-      const float* r4 = raw4 + o * 4;
-      const float* dg = dgates + o * 4;
-      if (!pos_none) {
-        if (softplus(r4[0]) <= 10.f) d4[0] = -dg[0] * sigmoid(r4[0]);
-        if (softplus(r4[2]) <= 10.f) d4[2] = -dg[2] * sigmoid(r4[2]);
-      }
-      const float s1 = sigmoid(r4[1]), s3 = sigmoid(r4[3]);
-      d4[1] = dg[1] * beta_max * s1 * (1.f - s1);
-      d4[3] = dg[3] * beta_max * s3 * (1.f - s3);
-      if (lane < 4) d4out[o * 4 + lane] = d4[lane];
+      // every global read of the row first (the stores below may alias the inputs)
+      const float4 r4 = *reinterpret_cast<const float4*>(raw4 + o * 4);
+      const float4 g4 = *reinterpret_cast<const float4*>(dgates + o * 4);
       float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
       load_vec(y, ns + o * M, M);
       load_vec(dy, dns + o * M, M);
-      unit_bwd(dx, y, dy, sn[o], M);
       load_vec(base, dslot + o * M, M);
+      float a[kMaxPerLane], da[kMaxPerLane], dkx[kMaxPerLane], cur[kMaxPerLane];
+      load_vec(a, nk + o * D, D);
+      load_vec(da, dnk + o * D, D);
+      load_vec(cur, dkey + o * D, D);
+      const float sno = sn[o], kno = kn[o];
+      float d4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float r4v[4] = {r4.x, r4.y, r4.z, r4.w};
+      const float dg[4] = {g4.x, g4.y, g4.z, g4.w};
+      if (!pos_none) {
+        if (softplus(r4v[0]) <= 10.f) d4[0] = -dg[0] * sigmoid(r4v[0]);
+        if (softplus(r4v[2]) <= 10.f) d4[2] = -dg[2] * sigmoid(r4v[2]);
+      }
+      const float s1 = sigmoid(r4v[1]), s3 = sigmoid(r4v[3]);
+      d4[1] = dg[1] * beta_max * s1 * (1.f - s1);
+      d4[3] = dg[3] * beta_max * s3 * (1.f - s3);
+      if (lane < 4) d4out[o * 4 + lane] = d4[lane];
+      unit_bwd(dx, y, dy, sno, M);
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) base[i] += dx[i];
       store_vec(dslot + o * M, base, M);
-      float a[kMaxPerLane], da[kMaxPerLane], dkx[kMaxPerLane];
-      load_vec(a, nk + o * D, D);
-      load_vec(da, dnk + o * D, D);
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) {
         const int d = lane + 32 * i;
-        if (d < D)
-          da[i] += d4[0] * wg[d * 4] + d4[1] * wg[d * 4 + 1] + d4[2] * wg[d * 4 + 2] +
-                   d4[3] * wg[d * 4 + 3];
+        if (d < D) {
+          const float4 w4 = *reinterpret_cast<const float4*>(Wg4 + d * 4);
+          da[i] += d4[0] * w4.x + d4[1] * w4.y + d4[2] * w4.z + d4[3] * w4.w;
+        }
       }
-      unit_bwd(dkx, a, da, kn[o], D);
-      float cur[kMaxPerLane];
-      load_vec(cur, dkey + o * D, D);
+      unit_bwd(dkx, a, da, kno, D);
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) cur[i] += dkx[i];
       store_vec(dkey + o * D, cur, D);
