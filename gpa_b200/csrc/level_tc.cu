@@ -230,6 +230,116 @@ __global__ void __launch_bounds__(256) tk_level_post(
   });
 }
 
+// Cooperative staging of the reader inputs of a 64-token tile (all warps, float4, every
+// incoming message's loads in flight together): inc[t][m] = sum_a w_a msg_a[t][m] and, when
+// given, a second [rows x M] fp32 tile; rows t >= c are zero.
+GPA_DEV void stage_incoming(float* inc, const BridgeIn& in, const float* w, int64_t r0, int c,
+                            int M) {
+  const int m4 = M >> 2;
+  for (int i = threadIdx.x; i < R * m4; i += blockDim.x) {
+    const int t = i / m4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < c) {
+      float4 x[kMaxIn];
+#pragma unroll
+      for (int a = 0; a < kMaxIn; ++a)
+        if (a < in.n) x[a] = *reinterpret_cast<const float4*>(in.msg[a] + r0 * M + 4 * i);
+#pragma unroll
+      for (int a = 0; a < kMaxIn; ++a)
+        if (a < in.n) {
+          acc.x += w[a] * x[a].x;
+          acc.y += w[a] * x[a].y;
+          acc.z += w[a] * x[a].z;
+          acc.w += w[a] * x[a].w;
+        }
+    }
+    *reinterpret_cast<float4*>(inc + 4 * i) = acc;
+  }
+}
+
+GPA_DEV void stage_rows(float* dst, const float* src, int c, int M) {
+  const int m4 = M >> 2;
+  for (int i = threadIdx.x; i < R * m4; i += blockDim.x)
+    *reinterpret_cast<float4*>(dst + 4 * i) =
+        i / m4 < c ? *reinterpret_cast<const float4*>(src + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// reader_row_fwd with the row's logits and weighted incoming message in shared memory
+GPA_DEV void reader_row_fwd_s(float (&base)[kMaxPerLane], const float* lg, const float* incr,
+                              int M, bool has_in, float rg) {
+  load_vec(base, lg, M);
+  if (has_in) {
+    const int lane = threadIdx.x & 31;
+    float inc[kMaxPerLane];
+    load_vec(inc, incr, M);
+    float mean = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i < M) mean += inc[i];
+    mean = warp_sum(mean) / M;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i < M) {
+        inc[i] -= mean;
+        var += inc[i] * inc[i];
+      }
+    var = warp_sum(var) / M;
+    const float sd = rsqrtf(var + kCenterEps);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) base[i] += rg * tanhf(inc[i] * sd);
+  }
+  warp_softmax(base, M);
+}
+
+// reader_row_bwd up to dz (the gradient of the weighted incoming message), which the caller
+// scatters to the messages and edge weights tile-wise.
+GPA_DEV void reader_row_bwd_s(float (&db)[kMaxPerLane], float (&dz)[kMaxPerLane],
+                              const float (&r)[kMaxPerLane], const float (&dr)[kMaxPerLane],
+                              const float* incr, int M, bool has_in, float rg, float& rg_acc) {
+  const int lane = threadIdx.x & 31;
+  softmax_bwd(db, r, dr, M);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) dz[i] = 0.f;
+  if (!has_in) return;
+  float inc[kMaxPerLane];
+  load_vec(inc, incr, M);
+  float mean = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < M) mean += inc[i];
+  mean = warp_sum(mean) / M;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i)
+    if (lane + 32 * i < M) {
+      inc[i] -= mean;
+      var += inc[i] * inc[i];
+    }
+  var = warp_sum(var) / M;
+  const float sd = rsqrtf(var + kCenterEps);
+  float rgp = 0.f, dsum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const float tz = tanhf(inc[i] * sd);
+    if (lane + 32 * i < M) rgp += db[i] * tz;
+    dz[i] = rg * db[i] * (1.f - tz * tz);
+    if (lane + 32 * i < M) dsum += dz[i] * inc[i];
+  }
+  rg_acc += warp_sum(rgp);
+  dsum = warp_sum(dsum);
+  const float dvar = dsum * -0.5f * sd * sd * sd;
+  float dmean = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    dz[i] = dz[i] * sd + dvar * 2.f * inc[i] / M;
+    if (lane + 32 * i < M) dmean += dz[i];
+  }
+  dmean = warp_sum(dmean) / M;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) dz[i] -= dmean;
+}
+
 // ------------------------------------------------------------------ bridge
 
 struct LBridge {
@@ -269,11 +379,17 @@ __global__ void __launch_bounds__(256) tk_bridge(
   float w[kMaxIn];
   edge_weights(in, edge_logits, H, h, w);
   const float rg = relation_gain[j * H + h];
+  {
+    float* Lg = (float*)(smem + Lb.Hb);  // Hb and Of are free until their GEMMs
+    stage_rows(Lg, logits + row(u, T, t0) * M, c, M);
+    if (in.n > 0) stage_incoming(Of, in, w, row(u, T, t0), c, M);
+  }
+  __syncthreads();
   for (int t = warp; t < R; t += nw) {
     float x[kMaxPerLane];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
-      reader_row_fwd(x, o, M, in, w, rg, logits);
+      reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * M, M, in.n > 0, rg);
       store_vec(r_out + o * M, x, M);
     } else {
 #pragma unroll
@@ -284,7 +400,7 @@ __global__ void __launch_bounds__(256) tk_bridge(
   }
   tile_to_bf16(ARQ + M, la, qf + row(u, T, t0) * D, D, c, D, R);
   tile_to_bf16(Wbuf, lh, route_up + (int64_t)h * M * 2 * M, 2 * M, M, 2 * M, M);
-  __syncthreads();
+  __syncthreads();  // the staged rows in Hb are dead below
   // hp = r U ; hidden = gelu(hp)
   tiles_n<1, 2>(R, 2 * M, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
@@ -340,7 +456,7 @@ __global__ void __launch_bounds__(256) tk_bridge(
 }
 
 struct LBridgeBwd {
-  size_t Qb, Ql, Rf, Rb, Hb, Hl, Wbuf, red, total;
+  size_t Qb, Ql, Rf, Rb, Hb, Hl, Wbuf, red, qn, total;
   __host__ __device__ LBridgeBwd(int D, int M, int) {
     Carve c;
     Qb = c.take(2 * R * ld16(M));
@@ -352,8 +468,10 @@ struct LBridgeBwd {
     const size_t w1 = 2 * (M + D) * ld16(M), w2 = 2 * (2 * M) * ld16(M), w3 = 2 * M * ld16(2 * M);
     size_t w = w1 > w2 ? w1 : w2;
     w = w > w3 ? w : w3;
+    w = w > 4 * R * M ? w : 4 * R * M;  // also holds the dz rows of the reader backward
     Wbuf = c.take(w);
     red = c.take(4 * 32);
+    qn = c.take(4 * R);
     total = c.off;
   }
 };
@@ -379,15 +497,21 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   bf16* Hl = (bf16*)(smem + Lb.Hl);
   bf16* Wbuf = (bf16*)(smem + Lb.Wbuf);
   float* red = (float*)(smem + Lb.red);
+  float* qn = (float*)(smem + Lb.qn);
   const int lm = ld16(M), lh = ld16(2 * M);
+  // qoh, dqoh and qon of the tile staged in Rf / Hb / qn (free until their GEMMs)
+  stage_rows(Rf, qoh + row(u, T, t0) * M, c, M);
+  stage_rows((float*)Hb, dqoh + row(u, T, t0) * M, c, M);
+  for (int t = threadIdx.x; t < R; t += blockDim.x) qn[t] = t < c ? qon[row(u, T, t0 + t)] : 0.f;
+  __syncthreads();
   for (int t = warp; t < R; t += nw) {
     float dx[kMaxPerLane];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
       float y[kMaxPerLane], dy[kMaxPerLane];
-      load_vec(y, qoh + o * M, M);
-      load_vec(dy, dqoh + o * M, M);
-      unit_bwd(dx, y, dy, qon[o], M);
+      load_vec(y, Rf + t * M, M);
+      load_vec(dy, (const float*)Hb + t * M, M);
+      unit_bwd(dx, y, dy, qn[t], M);
       store_vec(dqo_out + o * M, dx, M);
     } else {
 #pragma unroll
@@ -397,7 +521,7 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   }
   tile_to_bf16(Wbuf, lm, Wrs + (int64_t)h * M * M, M, M, M, M);
   tile_to_bf16(Wbuf + M * lm, lm, Wqs + (int64_t)h * D * M, M, D, M, D, qs);
-  __syncthreads();
+  __syncthreads();  // staged rows in Rf / Hb are dead below
   // droute = dqo W_rs^T
   tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
@@ -471,20 +595,46 @@ __global__ void __launch_bounds__(256) tk_bridge_bwd(
   float w[kMaxIn];
   edge_weights(in, edge_logits, H, h, w);
   const float rg = relation_gain[j * H + h];
-  float rg_acc = 0.f, ew_acc[kMaxIn];
-  for (int a = 0; a < kMaxIn; ++a) ew_acc[a] = 0.f;
-  for (int t = warp; t < c; t += nw) {
-    const int64_t o = row(u, T, t0 + t);
-    float r[kMaxPerLane], dr[kMaxPerLane], db[kMaxPerLane];
-    load_vec(r, r_in + o * M, M);
-    load_vec(dr, Rf + t * M, M);
-    reader_row_bwd(db, r, dr, o, M, in, w, rg, rg_acc, ew_acc);
-    store_vec(dlogits + o * M, db, M);
+  // reader backward: incoming and route rows staged in Hb / Hl, dz rows into Wbuf
+  float* Inc = (float*)Hb;
+  float* Rr = (float*)Hl;
+  float* DZ = (float*)Wbuf;
+  if (in.n > 0) stage_incoming(Inc, in, w, row(u, T, t0), c, M);
+  stage_rows(Rr, r_in + row(u, T, t0) * M, c, M);
+  __syncthreads();
+  float rg_acc = 0.f;
+  for (int t = warp; t < R; t += nw) {
+    float dz[kMaxPerLane];
+    if (t < c) {
+      float r[kMaxPerLane], dr[kMaxPerLane], db[kMaxPerLane];
+      load_vec(r, Rr + t * M, M);
+      load_vec(dr, Rf + t * M, M);
+      reader_row_bwd_s(db, dz, r, dr, Inc + t * M, M, in.n > 0, rg, rg_acc);
+      store_vec(dlogits + row(u, T, t0 + t) * M, db, M);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) dz[i] = 0.f;
+    }
+    store_vec(DZ + t * M, dz, M);
   }
-  if (lane == 0 && in.n > 0) {
-    atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], (double)rg_acc);
-    for (int a = 0; a < in.n; ++a)
-      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], (double)ew_acc[a]);
+  if (in.n == 0) return;
+  if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], (double)rg_acc);
+  __syncthreads();
+  // dmsg_a = w_a dz ; d edge-weight_a = sum dz o msg_a
+  const int m4 = M >> 2;
+  const int64_t r0 = row(u, T, t0) * M;
+  for (int a = 0; a < in.n; ++a) {
+    float part = 0.f;
+    for (int i = threadIdx.x; i < c * m4; i += blockDim.x) {
+      const float4 z = *reinterpret_cast<const float4*>(DZ + 4 * i);
+      const float4 x = *reinterpret_cast<const float4*>(in.msg[a] + r0 + 4 * i);
+      *reinterpret_cast<float4*>(in.dmsg[a] + r0 + 4 * i) =
+          make_float4(w[a] * z.x, w[a] * z.y, w[a] * z.z, w[a] * z.w);
+      part += z.x * x.x + z.y * x.y + z.z * x.z + z.w * x.w;
+    }
+    const float tot = block_sum(part, red);
+    if (threadIdx.x == 0)
+      atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], (double)tot);
   }
 }
 
