@@ -131,6 +131,10 @@ class _DenseGPACore(torch.autograd.Function):
         ctx.saved_ws = saved
         ctx.in_dtype = q.dtype
         ctx.save_for_backward(*params, *state_in)
+        # the workspace has no gradient, and unused outputs get None instead of a zero tensor
+        # (a materialized zero gradient of the workspace would be as large as the workspace)
+        ctx.mark_non_differentiable(saved)
+        ctx.set_materialize_grads(False)
         return (out, *state_out, saved)
 
     @staticmethod
@@ -141,9 +145,17 @@ class _DenseGPACore(torch.autograd.Function):
         tensors = ctx.saved_tensors
         params = tensors[:plan.n_params]
         state_in = tensors[plan.n_params:]
-        dev = dout.device
+        dev = ctx.saved_ws.device
+        if dout is None:
+            dout = torch.zeros(plan.B, plan.T, plan.H, plan.Dv, device=dev, dtype=ctx.in_dtype)
         dout = dout.contiguous().to(ctx.in_dtype)
         dstate = [None if g is None else g.contiguous().float() for g in dstate]
+        if plan.fz_out:  # frozen-snapshot gradients are consumed in (inner, outer) pairs
+            base = 3 * plan.L + plan.E
+            shapes = plan.state_shapes(True)
+            for i in range(base, len(dstate)):
+                if dstate[i] is None:
+                    dstate[i] = torch.zeros(shapes[i], device=dev, dtype=torch.float32)
         dq = torch.empty(plan.B, plan.T, plan.H, plan.D, device=dev, dtype=ctx.in_dtype)
         dk = torch.empty_like(dq)
         dv = torch.empty(plan.B, plan.T, plan.H, plan.Dv, device=dev, dtype=ctx.in_dtype)

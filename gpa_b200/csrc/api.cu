@@ -173,6 +173,9 @@ struct Saved {
   // chunk WY terms of every scan (U = T diag(b) V, Wk = T diag(b e^G) K), kept for the backward
   float *UA[kMaxLevels], *KA[kMaxLevels], *UB[kMaxLevels], *KB[kMaxLevels];
   float *UR[kMaxEdges], *KR[kMaxEdges];
+  // A and T = (I + A)^-1 of every block of every scan (tensor-core path only)
+  float *AA[kMaxLevels], *TA[kMaxLevels], *AB[kMaxLevels], *TB[kMaxLevels];
+  float *AR[kMaxEdges], *TR[kMaxEdges];
   size_t bytes;
 };
 
@@ -231,6 +234,17 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
   for (int e = 0; e < g.E; ++e) {
     s->UR[e] = b.take(UT * g.M[g.ed[e]]);
     s->KR[e] = b.take(UT * g.M[g.es[e]]);
+  }
+  const size_t nAT = g.fast ? (size_t)g.U * g.bl.nb * kMaxChunk * kMaxChunk : 0;
+  for (int j = 0; j < g.L; ++j) {
+    s->AA[j] = g.fast ? b.take(nAT) : nullptr;
+    s->TA[j] = g.fast ? b.take(nAT) : nullptr;
+    s->AB[j] = g.fast ? b.take(nAT) : nullptr;
+    s->TB[j] = g.fast ? b.take(nAT) : nullptr;
+  }
+  for (int e = 0; e < g.E; ++e) {
+    s->AR[e] = g.fast ? b.take(nAT) : nullptr;
+    s->TR[e] = g.fast ? b.take(nAT) : nullptr;
   }
   s->bytes = b.off + 256;
 }
@@ -394,6 +408,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     in.W = s.WA[j];
     in.Ub = s.UA[j];
     in.Wk = s.KA[j];
+    in.Asv = s.AA[j];
+    in.Tsv = s.TA[j];
     in.O = s.raw[j];
     in.S_final = so->inner[j];
     ou = blank_scan();
@@ -410,6 +426,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     ou.W = s.WB[j];
     ou.Ub = s.UB[j];
     ou.Wk = s.KB[j];
+    ou.Asv = s.AB[j];
+    ou.Tsv = s.TB[j];
     ou.S_final = so->outer[j];
     CK(gdn_forward(sb, U, bl, true, st));
     const int with_res = j + 1 < g.L;
@@ -447,6 +465,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
       d.W = s.WR[e];
       d.Ub = s.UR[e];
       d.Wk = s.KR[e];
+      d.Asv = s.AR[e];
+      d.Tsv = s.TR[e];
       d.O = s.msg[e];
       d.S_final = so->relation[e];
       ++sb.n;
@@ -629,6 +649,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
       d.W = s.WR[e];
       d.Ub = s.UR[e];
       d.Wk = s.KR[e];
+      d.Asv = s.AR[e];
+      d.Tsv = s.TR[e];
       d.dO = x.dmsg[e];
       d.dS_final = ds.relation[e];
       d.dq = x.dlh[i];
@@ -723,6 +745,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     in.W = s.WA[j];
     in.Ub = s.UA[j];
     in.Wk = s.KA[j];
+    in.Asv = s.AA[j];
+    in.Tsv = s.TA[j];
     in.dO = x.draw;
     in.ext = x.extA;
     in.dS_final = ds.inner[j];
@@ -747,6 +771,8 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     ou = outer_desc(j);
     ou.Ub = s.UB[j];
     ou.Wk = s.KB[j];
+    ou.Asv = s.AB[j];
+    ou.Tsv = s.TB[j];
     ou.ext = x.extB;
     ou.dS_final = ds.outer[j];
     ou.dk = x.dns;

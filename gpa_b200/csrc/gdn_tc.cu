@@ -204,7 +204,11 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
   __syncthreads();
+  float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) As[i] = A[(i / C) * kAStride + (i % C)];
   invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
+  float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) Ts[i] = Tm[(i / C) * kAStride + (i % C)];
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
     const int t = i / C, s = i - t * C;
     tc::split_bf16(Tm[t * kAStride + s] * bt[s], Fh + t * LDT + s, Fl + t * LDT + s);
@@ -715,10 +719,9 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
 
 struct LBwdChunk {
   // fixed buffers, then Y (dW hi/lo) and a pool X whose contents change by stage:
-  //   T build: Tm, Xs | state terms: Sb, Db, Wb | U path: Uh, Ul | Wk path: Wkh, Wkl, dWkh, dWkl
-  //   | final: Mmb
+  //   state terms: Sb, Db, Wb | U path: Uh, Ul | Wk path: Wkh, Wkl, dWkh, dWkl | final: Mmb
   size_t Ks, Kl, Th, Tl, A, dAf, Mh, Ml, G, bt, dG, db, dlam, rw, red, dWh, dWl, X, total;
-  size_t Tm, Xs, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mmb;
+  size_t Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mmb;
   __host__ __device__ LBwdChunk(int K, int V) {
     Carve c;
     const size_t sK = 2 * C * ld16(K), sV = 2 * C * ld16(V), sS = 2 * K * ld16(V);
@@ -740,13 +743,10 @@ struct LBwdChunk {
     red = c.take(4 * 32);
     dWh = c.take(sV);
     dWl = c.take(sV);
-    size_t pool = sA + 4 * 768;
-    pool = pool > 2 * sS + sV ? pool : 2 * sS + sV;
+    size_t pool = 2 * sS + sV;
     pool = pool > 2 * sV ? pool : 2 * sV;
     pool = pool > 4 * sK ? pool : 4 * sK;
     X = c.take(pool);
-    Tm = X;
-    Xs = X + sA;
     Sb = X;
     Db = X + sS;
     Wb = X + 2 * sS;
@@ -790,8 +790,6 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   float* red = (float*)(smem + L.red);
   bf16* dWh = (bf16*)(smem + L.dWh);
   bf16* dWl = (bf16*)(smem + L.dWl);
-  float* Tm = (float*)(smem + L.Tm);
-  float* Xs = (float*)(smem + L.Xs);
   bf16* Sb = (bf16*)(smem + L.Sb);
   bf16* Db = (bf16*)(smem + L.Db);
   bf16* Wb = (bf16*)(smem + L.Wb);
@@ -812,20 +810,22 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     db[t] = dlam[t] = rw[t] = 0.f;
   }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
-  {
+  {  // K, gates, and A, T of the block as the forward formed them
     const GateRegs gr = gate_fetch(d, u, t0, c, true);
-    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C)};
+    const float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
+    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C),
+                            tc::job(Th, Tl, LDT, d.Tsv + ((int64_t)u * bl.nb + n) * C * C, C, C, C, C)};
     tc::load_tiles(jobs);
+    for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
+      const float4 a = *reinterpret_cast<const float4*>(As + 4 * i);
+      float* dst = A + (4 * i / C) * kAStride + (4 * i) % C;
+      dst[0] = a.x;
+      dst[1] = a.y;
+      dst[2] = a.z;
+      dst[3] = a.w;
+    }
     gate_finish(gr, c, G, bt);
   }
-  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
-  __syncthreads();
-  invert_unit_lower(A, Tm, Xs);
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    tc::split_bf16(Tm[t * kAStride + s], Th + t * LDT + s, Tl + t * LDT + s);
-  }
-  __syncthreads();  // pool X (Tm) is reused below
 
   // ---- state-update terms: WD = W D^T, <D, S>, dWk = -dW S^T
   {
@@ -906,9 +906,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     float part[2] = {0.f, 0.f};
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) {
-        float* o = d.dv + (r0 + t) * V + col;
-        atomicAdd(o, bt[t] * v0);
-        atomicAdd(o + 1, bt[t] * v1);
+        atomicAdd(reinterpret_cast<float2*>(d.dv + (r0 + t) * V + col),
+                  make_float2(bt[t] * v0, bt[t] * v1));
         part[(t - m0) >> 3 & 1] += v0 * vv[p].x + v1 * vv[p].y;
       }
     });
