@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
     const GateRegs gr = gate_fetch(d, u, t0, c, true);
     const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
                             tc::job(Vs, nullptr, ldv, d.v + row(u, T, t0) * V, V, c, V, C)};
-    tc::load_tiles(jobs);
+    tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, bt);
   }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
         tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
         tc::job(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C)};
-    tc::load_tiles(jobs);
+    tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, nullptr);
   }
   for_tiles<1, 2>(C, C, [&](int m0, int n0) {

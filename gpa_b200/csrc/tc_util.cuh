@@ -91,38 +91,65 @@ GPA_DEV TileJob job(bf16* hi, bf16* lo, int ld, const float* src, int src_ld, in
   return TileJob{hi, lo, ld, src, src_ld, rows, cols, rows_pad, scale, rowmul};
 }
 
-// Load the tiles one after another (kLoadIlp float4 in flight per thread).  Loading all
-// tiles of a phase in one round (16 float4 per thread) measured slower on B200.
-template <int N>
-GPA_DEV void load_tiles(const TileJob (&jobs)[N]) {
+// Load the tiles two at a time: each thread keeps kLoadIlp float4 of each of the two tiles in
+// flight before converting any of them.
+GPA_DEV void tile_pair(const TileJob& A, const TileJob* B) {
+  const int ca = A.cols >> 2, na = A.rows_pad * ca;
+  const int cb = B ? B->cols >> 2 : 1, nb = B ? B->rows_pad * cb : 0;
+  const int n = na > nb ? na : nb;
+  for (int base = threadIdx.x; base < n; base += blockDim.x * kLoadIlp) {
+    float4 va[kLoadIlp], vb[kLoadIlp];
 #pragma unroll
-  for (int j = 0; j < N; ++j) {
-    const TileJob& J = jobs[j];
-    const int c4 = J.cols >> 2, n4 = J.rows_pad * c4;
-    for (int base = threadIdx.x; base < n4; base += blockDim.x * kLoadIlp) {
-      float4 v[kLoadIlp];
-#pragma unroll
-      for (int q = 0; q < kLoadIlp; ++q) {
-        const int i = base + q * blockDim.x;
-        const int r = i / c4, cc = (i - r * c4) << 2;
-        v[q] = (i < n4 && r < J.rows)
-                   ? *reinterpret_cast<const float4*>(J.src + (int64_t)r * J.src_ld + cc)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < kLoadIlp; ++q) {
+      const int i = base + q * blockDim.x;
+      const int ra = i / ca, xa = (i - ra * ca) << 2;
+      va[q] = (i < na && ra < A.rows)
+                  ? *reinterpret_cast<const float4*>(A.src + (int64_t)ra * A.src_ld + xa)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (B) {
+        const int rb = i / cb, xb = (i - rb * cb) << 2;
+        vb[q] = (i < nb && rb < B->rows)
+                    ? *reinterpret_cast<const float4*>(B->src + (int64_t)rb * B->src_ld + xb)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    }
 #pragma unroll
-      for (int q = 0; q < kLoadIlp; ++q) {
-        const int i = base + q * blockDim.x;
-        if (i >= n4) break;
-        const int r = i / c4, cc = (i - r * c4) << 2;
-        const float f = J.rowmul ? J.scale * J.rowmul[r] : J.scale;
-        float4 x = v[q];
+    for (int q = 0; q < kLoadIlp; ++q) {
+      const int i = base + q * blockDim.x;
+      if (i < na) {
+        const int r = i / ca, cc = (i - r * ca) << 2;
+        const float f = A.rowmul ? A.scale * A.rowmul[r] : A.scale;
+        float4 x = va[q];
         x.x *= f;
         x.y *= f;
         x.z *= f;
         x.w *= f;
-        put4(J.hi, J.lo, r * J.ld + cc, x);
+        put4(A.hi, A.lo, r * A.ld + cc, x);
+      }
+      if (B && i < nb) {
+        const int r = i / cb, cc = (i - r * cb) << 2;
+        const float f = B->rowmul ? B->scale * B->rowmul[r] : B->scale;
+        float4 x = vb[q];
+        x.x *= f;
+        x.y *= f;
+        x.z *= f;
+        x.w *= f;
+        put4(B->hi, B->lo, r * B->ld + cc, x);
       }
     }
+  }
+}
+
+// Paired loads help kernels with one CTA per SM; with two CTAs per SM (little L1 left beside
+// their shared memory) one tile at a time measured faster.
+template <bool kPaired = true, int N>
+GPA_DEV void load_tiles(const TileJob (&jobs)[N]) {
+  if (kPaired) {
+#pragma unroll
+    for (int j = 0; j < N; j += 2) tile_pair(jobs[j], j + 1 < N ? &jobs[j + 1] : nullptr);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) tile_pair(jobs[j], nullptr);
   }
 }
 

@@ -281,3 +281,28 @@ def test_diagnostics_empty_input_and_errors():
         model(q.cpu(), k.cpu(), v.cpu())
     with pytest.raises(ValueError):
         DenseGPA(GPAConfig(heads=2, key_dim=8, value_dim=6, slots=(4, 8), chunk_size=1)).cuda()(q, k, v, st)
+
+
+def test_backward_peak_memory_is_workspaces_plus_io():
+    """A forward + backward holds the saved buffer, the backward scratch and the tensor I/O, and
+    nothing of the saved buffer's size besides: the autograd wrapper marks the workspace output
+    non-differentiable and does not materialize zero gradients for unused outputs."""
+    from gpa_b200 import _lib
+    from gpa_b200.core import _Plan
+    torch.manual_seed(0)
+    cfg = GPAConfig(heads=4, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
+    model = DenseGPA(cfg).cuda()
+    q, k, v = (torch.randn(2, 1024, 4, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+               for _ in range(3))
+    lib = _lib.load()
+    plan = _Plan(cfg, q, v, model.initial_state(2, device="cuda", dtype=q.dtype))
+    work = lib.gpa_b200_saved_bytes(plan.dims) + lib.gpa_b200_scratch_bytes(plan.dims)
+    io = 8 * q.numel() * 4  # q, k, v, out, their gradients and fp32 temporaries
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    out, state = model(q, k, v)
+    out.float().square().mean().backward()
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    assert peak <= work + io + (64 << 20), (peak, work, io)
