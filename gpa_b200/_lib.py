@@ -51,7 +51,8 @@ class GpaStateRef(ctypes.Structure):
 EXPORTS = ("gpa_b200_saved_bytes", "gpa_b200_scratch_bytes", "gpa_b200_forward",
            "gpa_b200_backward", "gpa_b200_routes", "gpa_b200_last_error",
            "gpa_b200_abi_version", "gpa_b200_launch_count", "gpa_b200_profile_start",
-           "gpa_b200_profile_stop", "gpa_b200_forward_noalloc", "gpa_b200_noalloc_capacity")
+           "gpa_b200_profile_stop", "gpa_b200_forward_noalloc", "gpa_b200_noalloc_capacity",
+           "gpa_b200_step")
 
 _lib = None
 
@@ -82,6 +83,9 @@ def load():
                                              c_void_p, c_void_p, POINTER(GpaStateRef),
                                              POINTER(GpaStateRef), c_void_p, c_void_p]
     lib.gpa_b200_forward_noalloc.restype = c_int
+    lib.gpa_b200_step.argtypes = [POINTER(GpaDims), POINTER(GpaParams), c_void_p, c_void_p,
+                                  c_void_p, POINTER(GpaStateRef), c_void_p, c_void_p, c_void_p]
+    lib.gpa_b200_step.restype = c_int
     lib.gpa_b200_noalloc_capacity.argtypes = []
     lib.gpa_b200_noalloc_capacity.restype = c_size_t
     lib.gpa_b200_routes.argtypes = [POINTER(GpaDims), c_void_p, POINTER(c_void_p), c_void_p]

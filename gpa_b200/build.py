@@ -15,7 +15,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ("api.cu", "gdn.cu", "gdn_tc.cu", "level.cu", "level_tc.cu")
+SOURCES = ("api.cu", "decode.cu", "gdn.cu", "gdn_tc.cu", "level.cu", "level_tc.cu")
 OUTPUT = os.path.join(HERE, "libgpa_b200.so")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../../include/gpa_b200.h"
+#include "decode.cuh"
 #include "gdn.cuh"
 #include "level.cuh"
 
@@ -870,6 +871,57 @@ int gpa_b200_forward(const GpaDims* dims, const GpaParams* params, const void* q
   if (!q || !k || !v || !out) return fail(GPA_B200_BAD_ARGUMENT, "q/k/v/out must not be NULL");
   return forward_impl(g, params, q, k, v, state_in, state_out, out, saved, saved_bytes,
                       static_cast<cudaStream_t>(stream));
+}
+
+int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, const void* k,
+                  const void* v, const GpaStateRef* state, int32_t* offset, void* out,
+                  void* stream) {
+  g_last_error.clear();
+  Geo g;
+  std::string why;
+  int rc = make_geo(dims, &g, &why);
+  if (rc) return fail(rc, why);
+  if (g.T != 1) return fail(GPA_B200_BAD_ARGUMENT, "gpa_b200_step takes one token (length 1)");
+  if (g.C < 2)
+    return fail(GPA_B200_UNSUPPORTED, "gpa_b200_step needs lag blocks (chunk_size >= 2)");
+  if (g.D % 4 || g.Dv % 4)
+    return fail(GPA_B200_UNSUPPORTED, "gpa_b200_step needs key/value widths that are multiples of 4");
+  for (int j = 0; j < g.L; ++j)
+    if (g.M[j] % 4) return fail(GPA_B200_UNSUPPORTED, "gpa_b200_step needs slot counts that are multiples of 4");
+  if ((rc = check_params(g, params))) return rc;
+  if ((rc = check_state(g, state, true, "state"))) return rc;
+  if (!q || !k || !v || !out || !offset)
+    return fail(GPA_B200_BAD_ARGUMENT, "q/k/v/out/offset must not be NULL");
+  StepArgs a;
+  a.U = g.U;
+  a.H = g.H;
+  a.D = g.D;
+  a.Dv = g.Dv;
+  a.L = g.L;
+  a.E = g.E;
+  a.C = g.C;
+  for (int j = 0; j < kMaxLevels; ++j) a.M[j] = j < g.L ? g.M[j] : 0;
+  for (int e = 0; e < kMaxEdges; ++e) {
+    a.es[e] = e < g.E ? g.es[e] : 0;
+    a.ed[e] = e < g.E ? g.ed[e] : 0;
+  }
+  a.dt = g.dt;
+  a.pos_none = g.pos_none;
+  a.query_scale = g.qs;
+  a.beta_max = g.bm;
+  a.read_scale = g.rs;
+  a.p = *params;
+  a.s = *state;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.offset = offset;
+  if (decode_step_smem(a) > 227 * 1024)
+    return fail(GPA_B200_UNSUPPORTED, "gpa_b200_step: widths too large for one CTA");
+  const cudaError_t e = launch_decode_step(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(GPA_B200_LAUNCH_FAILURE, std::string("decode step: ") + cudaGetErrorString(e));
+  return GPA_B200_OK;
 }
 
 int gpa_b200_backward(const GpaDims* dims, const GpaParams* params, const GpaStateRef* state_in,

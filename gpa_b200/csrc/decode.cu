@@ -1,0 +1,403 @@
+// One-token decode step for lag-block caches (chunk_size >= 2), fused into a single kernel
+// per call: one CTA per (batch, head) unit walks the whole layer for its token and updates
+// the cache in place.  The chunk offset lives in device memory and is advanced by a second
+// one-thread kernel, so a sequence of steps can be captured once in a CUDA graph and replayed.
+//
+// Per unit and level j (src/gpa/attention.py:299-345 with a one-token block):
+//   slot = C_j k, gates from u(k); A <- GDN(A, u(k), slot) and raw = u(q)^T A;
+//   write = softmax(u(k)^T A_f) with A_f the frozen snapshot (the pre-update A when the
+//   token opens a block); counts += write; logits = raw + softplus(c_j) log1p(n);
+//   k <- k - eta_k A_f write, v <- v - eta_v write^T B_f.
+// then the relation GDN steps of every edge, the dense reader per level
+// (src/gpa/attention.py:225-262), the outer GDN steps B <- GDN(B, u(slot), v_j) read with
+// u(qo_j), and the softmax(output_logits) mix.  All arithmetic is fp32.
+//
+// Each state matrix is read from HBM once into shared memory, updated there and written
+// back once (the outer states, and the frozen snapshots when the token opens a block, are
+// read a second time): the step is HBM-bound on the cache, 2 x 4 x 155,968 bytes per unit at
+// the config-2 widths.
+#include "decode.cuh"
+
+namespace gpa {
+namespace {
+
+constexpr int kStepThreads = 256;
+
+// ---------------------------------------------------------------- block helpers
+
+GPA_DEV float block_sum_all(float x, float* red) {
+  x = warp_sum(x);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+  return s;
+}
+
+GPA_DEV float block_max_all(float x, float* red) {
+  x = warp_max(x);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float s = -INFINITY;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s = fmaxf(s, red[w]);
+  return s;
+}
+
+// dst = src / max(|src|, eps) (dst may alias src); ends synchronized
+GPA_DEV void unit_vec(float* dst, const float* src, int n, float* red) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += src[i] * src[i];
+  const float inv = 1.f / fmaxf(sqrtf(block_sum_all(ss, red)), kUnitEps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i] * inv;
+  __syncthreads();
+}
+
+// dst = softmax(src) (dst may alias src); ends synchronized
+GPA_DEV void softmax_vec(float* dst, const float* src, int n, float* red) {
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, src[i]);
+  mx = block_max_all(mx, red);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += __expf(src[i] - mx);
+  const float inv = 1.f / block_sum_all(s, red);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __expf(src[i] - mx) * inv;
+  __syncthreads();
+}
+
+// y[c] = sum_r x[r] S[r][c] for S [R x Cn] row-major (shared or global); Cn <= blockDim.
+// part: blockDim floats.  Ends synchronized.
+GPA_DEV void colsum(const float* S, int R, int Cn, const float* x, float* y, float* part) {
+  const int P = blockDim.x / Cn, c = threadIdx.x % Cn, pr = threadIdx.x / Cn;
+  float acc = 0.f;
+  if (pr < P)
+    for (int r = pr; r < R; r += P) acc += x[r] * S[(int64_t)r * Cn + c];
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x < Cn) {
+    float s = 0.f;
+    for (int i = 0; i < P; ++i) s += part[i * Cn + threadIdx.x];
+    y[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
+// y[r] = sum_c S[r][c] x[c] for S [R x Cn] row-major: a warp per row.  Ends synchronized.
+GPA_DEV void rowdot(const float* S, int R, int Cn, const float* x, float* y) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = w; r < R; r += nw) {
+    float acc = 0.f;
+    for (int c = lane; c < Cn; c += 32) acc += S[(int64_t)r * Cn + c] * x[c];
+    acc = warp_sum(acc);
+    if (lane == 0) y[r] = acc;
+  }
+  __syncthreads();
+}
+
+// shared <- global (n floats, multiple of 4, 16-byte aligned); optional copy to `also`
+GPA_DEV void load_mat(float* Ss, const float* g, int n, float* also) {
+  for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {
+    const float4 x = *reinterpret_cast<const float4*>(g + i);
+    *reinterpret_cast<float4*>(Ss + i) = x;
+    if (also) *reinterpret_cast<float4*>(also + i) = x;
+  }
+  __syncthreads();
+}
+
+// GDN update of the state already in shared memory (pre = kv^T S_old given):
+// S <- e^g S + beta kv (val - e^g pre)^T, written back to global; y = qv^T S_new.
+GPA_DEV void gdn_update(float* Ss, float* Sg, int K, int V, const float* kv, const float* val,
+                        const float* pre, float g, float beta, const float* qv, float* y,
+                        float* part) {
+  const float eg = __expf(g);
+  const int v4 = V >> 2;
+  for (int i = threadIdx.x; i < K * v4; i += blockDim.x) {
+    const int k = i / v4, c = (i - k * v4) << 2;
+    float4 x = *reinterpret_cast<const float4*>(Ss + k * V + c);
+    const float bk = beta * kv[k];
+    x.x = eg * x.x + bk * (val[c] - eg * pre[c]);
+    x.y = eg * x.y + bk * (val[c + 1] - eg * pre[c + 1]);
+    x.z = eg * x.z + bk * (val[c + 2] - eg * pre[c + 2]);
+    x.w = eg * x.w + bk * (val[c + 3] - eg * pre[c + 3]);
+    *reinterpret_cast<float4*>(Ss + k * V + c) = x;
+    *reinterpret_cast<float4*>(Sg + k * V + c) = x;
+  }
+  __syncthreads();
+  colsum(Ss, K, V, qv, y, part);
+}
+
+struct StepSmem {
+  size_t Ss, q, qn, key, kn, val, tmp, tmp2, pre, yb, part, red, slot, write, logits, valin, qo,
+      gates, total;
+  int msg_off[kMaxEdges];
+  __host__ __device__ StepSmem(const StepArgs& a) {
+    size_t off = 0;
+    auto take = [&](size_t nfloat) {
+      off = (off + 3) & ~size_t(3);
+      const size_t r = off;
+      off += nfloat;
+      return r;
+    };
+    int mx = 0, big = 0;
+    for (int j = 0; j < a.L; ++j) {
+      mx = a.M[j] > mx ? a.M[j] : mx;
+      const int s1 = a.D * a.M[j], s2 = a.M[j] * a.Dv;
+      big = s1 > big ? s1 : big;
+      big = s2 > big ? s2 : big;
+    }
+    for (int e = 0; e < a.E; ++e) {
+      const int s3 = a.M[a.es[e]] * a.M[a.ed[e]];
+      big = s3 > big ? s3 : big;
+    }
+    const int w = a.D > a.Dv ? a.D : a.Dv;
+    const int wide = (w > 2 * mx ? w : 2 * mx);
+    Ss = take(big);
+    q = take(a.D);
+    qn = take(a.D);
+    key = take(a.D);
+    kn = take(a.D);
+    val = take(a.Dv);
+    tmp = take(wide);
+    tmp2 = take(wide);
+    pre = take(w > mx ? w : mx);
+    yb = take(a.Dv);
+    part = take(kStepThreads);
+    red = take(32);
+    slot = take(a.L * mx);
+    write = take(a.L * mx);
+    logits = take(a.L * mx);
+    valin = take(a.L * a.Dv);
+    qo = take(a.L * mx);
+    gates = take(a.L * 4);
+    for (int e = 0; e < a.E; ++e) msg_off[e] = (int)take(a.M[a.ed[e]]);
+    total = off * sizeof(float);
+  }
+};
+
+__global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const StepSmem Lm(a);
+  const int u = blockIdx.x, h = u % a.H, D = a.D, Dv = a.Dv, L = a.L;
+  const int o = *a.offset;
+  int mx = 0;
+  for (int j = 0; j < L; ++j) mx = a.M[j] > mx ? a.M[j] : mx;
+  float* Ss = sm + Lm.Ss;
+  float* q = sm + Lm.q;
+  float* qn = sm + Lm.qn;
+  float* key = sm + Lm.key;
+  float* kn = sm + Lm.kn;
+  float* val = sm + Lm.val;
+  float* tmp = sm + Lm.tmp;
+  float* tmp2 = sm + Lm.tmp2;
+  float* part = sm + Lm.part;
+  float* red = sm + Lm.red;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    q[i] = load_in(a.q, (int64_t)u * D + i, a.dt);
+    key[i] = load_in(a.k, (int64_t)u * D + i, a.dt);
+  }
+  for (int i = threadIdx.x; i < Dv; i += blockDim.x) val[i] = load_in(a.v, (int64_t)u * Dv + i, a.dt);
+  __syncthreads();
+  unit_vec(qn, q, D, red);
+
+  // ------------------------------------------------ level chain
+  for (int j = 0; j < L; ++j) {
+    const int M = a.M[j];
+    float* slot = sm + Lm.slot + j * mx;
+    float* write = sm + Lm.write + j * mx;
+    float* logits = sm + Lm.logits + j * mx;
+    float* gates = sm + Lm.gates + 4 * j;
+    unit_vec(kn, key, D, red);
+    rowdot(a.p.center[j] + (int64_t)h * M * D, M, D, key, slot);  // slot = C k
+    {  // gates from u(k)
+      const float* wg = a.p.gate_weight[j] + (int64_t)h * D * 4;
+      float r[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float4 w4 = *reinterpret_cast<const float4*>(wg + 4 * d);
+        r[0] += kn[d] * w4.x;
+        r[1] += kn[d] * w4.y;
+        r[2] += kn[d] * w4.z;
+        r[3] += kn[d] * w4.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) r[c] = block_sum_all(r[c], red) + a.p.gate_bias[j][h * 4 + c];
+      if (threadIdx.x == 0) {
+        gates[0] = a.pos_none ? 0.f : -fminf(softplus(r[0]), 10.f);
+        gates[1] = a.beta_max * sigmoid(r[1]);
+        gates[2] = a.pos_none ? 0.f : -fminf(softplus(r[2]), 10.f);
+        gates[3] = a.beta_max * sigmoid(r[3]);
+      }
+      __syncthreads();
+    }
+    const int64_t szA = (int64_t)D * M, szB = (int64_t)M * Dv;
+    float* Ag = a.s.inner[j] + u * szA;
+    float* Bg = a.s.outer[j] + u * szB;
+    float* rk = tmp;  // [D]
+    if (o != 0) {     // write and rk from the frozen inner snapshot
+      load_mat(Ss, a.s.frozen_inner[j] + u * szA, (int)szA, nullptr);
+      colsum(Ss, D, M, kn, write, part);
+      softmax_vec(write, write, M, red);
+      rowdot(Ss, D, M, write, rk);
+    }
+    // inner GDN step; the pre-update A is the frozen snapshot when the token opens a block
+    load_mat(Ss, Ag, (int)szA, o == 0 ? a.s.frozen_inner[j] + u * szA : nullptr);
+    float* pre = sm + Lm.pre;  // u(k)^T A_old [M]
+    colsum(Ss, D, M, kn, pre, part);
+    if (o == 0) {
+      softmax_vec(write, pre, M, red);
+      rowdot(Ss, D, M, write, rk);
+    }
+    gdn_update(Ss, Ag, D, M, kn, slot, pre, gates[0], gates[1], qn, logits, part);  // logits <- raw
+    {  // counts and base logits
+      const float cg = softplus(a.p.count_gain_raw[j * a.H + h]);
+      float* n = a.s.count[j] + (int64_t)u * M;
+      for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        const float nn = n[m] + write[m];
+        n[m] = nn;
+        logits[m] = a.read_scale * logits[m] + cg * log1pf(nn);
+      }
+    }
+    // rv = write^T B_f
+    float* rv = tmp2;
+    load_mat(Ss, o == 0 ? Bg : a.s.frozen_outer[j] + u * szB, (int)szB,
+             o == 0 ? a.s.frozen_outer[j] + u * szB : nullptr);
+    colsum(Ss, M, Dv, write, rv, part);
+    float* vin = sm + Lm.valin + j * Dv;
+    const float ek = 1.f + .25f * tanhf(a.p.residual_raw[(j * a.H + h) * 2 + 0]);
+    const float ev = 1.f + .25f * tanhf(a.p.residual_raw[(j * a.H + h) * 2 + 1]);
+    for (int i = threadIdx.x; i < Dv; i += blockDim.x) {
+      vin[i] = val[i];
+      val[i] -= ev * rv[i];
+    }
+    for (int i = threadIdx.x; i < D; i += blockDim.x) key[i] -= ek * rk[i];
+    __syncthreads();
+  }
+
+  // ------------------------------------------------ relations
+  for (int e = 0; e < a.E; ++e) {
+    const int i = a.es[e], j = a.ed[e], Mi = a.M[i], Mj = a.M[j];
+    float* kv = tmp;   // u(write_i)
+    float* lq = tmp2;  // u(softmax(logits_i))
+    unit_vec(kv, sm + Lm.write + i * mx, Mi, red);
+    softmax_vec(lq, sm + Lm.logits + i * mx, Mi, red);
+    unit_vec(lq, lq, Mi, red);
+    const int64_t sz = (int64_t)Mi * Mj;
+    float* Rg = a.s.relation[e] + u * sz;
+    load_mat(Ss, Rg, (int)sz, nullptr);
+    float* prebuf = sm + Lm.pre;
+    colsum(Ss, Mi, Mj, kv, prebuf, part);
+    const float g = a.pos_none ? 0.f : -softplus(a.p.relation_decay_raw[e * a.H + h]);
+    const float b = sigmoid(a.p.relation_beta_raw[e * a.H + h]);
+    gdn_update(Ss, Rg, Mi, Mj, kv, sm + Lm.write + j * mx, prebuf, g, b, lq,
+               sm + Lm.msg_off[e], part);
+  }
+
+  // ------------------------------------------------ dense reader and outer steps
+  for (int j = 0; j < L; ++j) {
+    const int M = a.M[j];
+    float* base = tmp;  // [M]
+    float* logits = sm + Lm.logits + j * mx;
+    float* inc = tmp2;  // [M]
+    int nin = 0;
+    float wmax = -INFINITY;
+    for (int e = 0; e < a.E; ++e)
+      if (a.ed[e] == j) {
+        ++nin;
+        wmax = fmaxf(wmax, a.p.edge_logits[e * a.H + h]);
+      }
+    for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] = logits[m];
+    if (nin > 0) {
+      float ws = 0.f;
+      for (int e = 0; e < a.E; ++e)
+        if (a.ed[e] == j) ws += __expf(a.p.edge_logits[e * a.H + h] - wmax);
+      for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        float x = 0.f;
+        for (int e = 0; e < a.E; ++e)
+          if (a.ed[e] == j) x += (__expf(a.p.edge_logits[e * a.H + h] - wmax) / ws) * sm[Lm.msg_off[e] + m];
+        inc[m] = x;
+      }
+      __syncthreads();
+      float s = 0.f;
+      for (int m = threadIdx.x; m < M; m += blockDim.x) s += inc[m];
+      const float mean = block_sum_all(s, red) / M;
+      float vs = 0.f;
+      for (int m = threadIdx.x; m < M; m += blockDim.x) vs += (inc[m] - mean) * (inc[m] - mean);
+      const float sd = rsqrtf(block_sum_all(vs, red) / M + kCenterEps);
+      const float rg = a.p.relation_gain[j * a.H + h];
+      for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] += rg * tanhf((inc[m] - mean) * sd);
+      __syncthreads();
+    }
+    softmax_vec(base, base, M, red);  // route
+    float* hid = tmp2;                // [2M]
+    colsum(a.p.route_up[j] + (int64_t)h * M * 2 * M, M, 2 * M, base, hid, part);
+    for (int r = threadIdx.x; r < 2 * M; r += blockDim.x) hid[r] = gelu(hid[r]);
+    __syncthreads();
+    float* mlp = sm + Lm.qo + j * mx;  // scratch until qo is formed
+    colsum(a.p.route_down[j] + (int64_t)h * 2 * M * M, 2 * M, M, hid, mlp, part);
+    const float mg = a.p.route_mlp_gain[j * a.H + h];
+    for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] += mg * mlp[m];
+    __syncthreads();
+    float* qo = sm + Lm.qo + j * mx;
+    colsum(a.p.route_weight[j] + (int64_t)h * M * M, M, M, base, qo, part);
+    colsum(a.p.query_weight[j] + (int64_t)h * D * M, D, M, q, hid, part);
+    for (int m = threadIdx.x; m < M; m += blockDim.x) qo[m] += a.query_scale * hid[m];
+    __syncthreads();
+  }
+  float ow[kMaxLevels];
+  {
+    float mxl = -INFINITY, s = 0.f;
+    for (int j = 0; j < L; ++j) mxl = fmaxf(mxl, a.p.output_logits[j * a.H + h]);
+    for (int j = 0; j < L; ++j) {
+      ow[j] = __expf(a.p.output_logits[j * a.H + h] - mxl);
+      s += ow[j];
+    }
+    for (int j = 0; j < L; ++j) ow[j] /= s;
+  }
+  float outacc[4] = {0.f, 0.f, 0.f, 0.f};  // Dv <= 4 * blockDim
+  for (int j = 0; j < L; ++j) {
+    const int M = a.M[j];
+    float* kv = tmp;   // u(slot_j)
+    float* qv = tmp2;  // u(qo_j)
+    unit_vec(kv, sm + Lm.slot + j * mx, M, red);
+    unit_vec(qv, sm + Lm.qo + j * mx, M, red);
+    const int64_t szB = (int64_t)M * Dv;
+    float* Bg = a.s.outer[j] + u * szB;
+    load_mat(Ss, Bg, (int)szB, nullptr);
+    float* pre = sm + Lm.pre;
+    colsum(Ss, M, Dv, kv, pre, part);
+    const float* gt = sm + Lm.gates + 4 * j;
+    float* yv = sm + Lm.yb;
+    gdn_update(Ss, Bg, M, Dv, kv, sm + Lm.valin + j * Dv, pre, gt[2], gt[3], qv, yv, part);
+    for (int i = threadIdx.x, c = 0; i < Dv; i += blockDim.x, ++c) outacc[c] += ow[j] * yv[i];
+  }
+  for (int i = threadIdx.x, c = 0; i < Dv; i += blockDim.x, ++c)
+    store_out(a.out, (int64_t)u * Dv + i, outacc[c], a.dt);
+}
+
+__global__ void k_advance_offset(int* offset, int C) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *offset = (*offset + 1) % C;
+}
+
+}  // namespace
+
+size_t decode_step_smem(const StepArgs& a) { return StepSmem(a).total; }
+
+cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st) {
+  const size_t smem = decode_step_smem(a);
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  cudaError_t e = cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  {
+    Launch scope("decode_step", st);
+    k_decode_step<<<a.U, kStepThreads, smem, st>>>(a);
+  }
+  {
+    Launch scope("advance_offset", st);
+    k_advance_offset<<<1, 32, 0, st>>>(a.offset, a.C);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace gpa

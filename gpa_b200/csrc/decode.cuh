@@ -1,0 +1,29 @@
+// One-token decode step (decode.cu): host interface used by the C ABI (api.cu).
+#pragma once
+#include "../../include/gpa_b200.h"
+#include "common.cuh"
+#include "level.cuh"
+
+namespace gpa {
+
+struct StepArgs {
+  int U, H, D, Dv, L, E;
+  int C;  // lag-block length (>= 2)
+  int M[kMaxLevels];
+  int es[kMaxEdges], ed[kMaxEdges];
+  int dt, pos_none;
+  float query_scale, beta_max, read_scale;
+  GpaParams p;
+  GpaStateRef s;  // updated in place; frozen_* required
+  const void *q, *k, *v;
+  void* out;
+  int* offset;  // device int: the cache's chunk offset, advanced by the step
+};
+
+// Shared memory the step kernel needs for these widths (bytes).
+size_t decode_step_smem(const StepArgs& a);
+// Stream-ordered: the step kernel, then the one-thread offset advance.  No allocation, no
+// host synchronization (capturable in a CUDA graph).
+cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st);
+
+}  // namespace gpa

@@ -137,6 +137,20 @@ int gpa_b200_forward_noalloc(const GpaDims* dims, const GpaParams* params, const
                              GpaStateRef* state_out, void* out, void* stream);
 size_t gpa_b200_noalloc_capacity(void);
 
+/* One-token decode step of a lag-block cache (chunk_size >= 2; dims->length == 1),
+ * replacing a one-token DenseGPA.forward call (src/gpa/attention.py:347-414 with
+ * T = 1, which runs _block_segment :299-345 on a one-token block).  The cache is
+ * updated IN PLACE (state->frozen_* required: the snapshots of the current lag
+ * block, written by this call when the token opens a block), and *offset (device
+ * int32, the cache's chunk_offset) is advanced to (offset + 1) % chunk_size on the
+ * device; dims->chunk_offset is ignored.  out: [B,1,H,Dv] in the input dtype.
+ * Stream-ordered, allocates nothing and never synchronizes with the host, so a
+ * sequence of steps can be captured in a CUDA graph.  Widths must be multiples
+ * of 4. */
+int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, const void* k,
+                  const void* v, const GpaStateRef* state, int32_t* offset, void* out,
+                  void* stream);
+
 /* Diagnostics: copy the per-level post-MLP routes of a forward call out of its
  * saved buffer into routes[j] ([B,T,H,M_j], input dtype).  Replaces the
  * return_diagnostics routes of DenseGPA.forward (src/gpa/attention.py:407-413). */
