@@ -334,6 +334,113 @@ def run_b200(args, rank, world, local):
     return result
 
 
+# --------------------------------------------------------------- decode (config 4)
+
+DECODE_BATCHES = (1, 64, 256)
+DECODE_PREFILL = 4096
+
+
+def decode_bytes_per_unit(cfg):
+    """Algorithmic HBM bytes of one decode step per (batch, head) unit: the cache read and
+    written once (2 x 4 x S), one read of the frozen snapshots, q/k/v/out in bf16."""
+    D, Dv, M = cfg["key_dim"], cfg["value_dim"], cfg["slots"]
+    S = sum(D * m + m * Dv + m for m in M) + sum(M[i] * M[j] for i in range(len(M))
+                                                  for j in range(len(M)) if i != j)
+    frozen = sum(D * m + m * Dv for m in M)
+    return 2 * 4 * S + 4 * frozen + 2 * (3 * D + Dv)
+
+
+def decode_param_bytes(cfg):
+    """Per-head parameters read once per step (every unit of a head shares them in L2)."""
+    D, M = cfg["key_dim"], cfg["slots"]
+    return cfg["heads"] * 4 * sum(2 * D * m + 5 * m * m + 4 * D for m in M)
+
+
+def run_decode(args):
+    """Config 4: config 2's layer, prefill 4096 tokens, one-token steps under a CUDA graph."""
+    from gpa_b200 import _lib
+    from gpa_b200.decode import DecodeSession
+    dev = torch.device("cuda", 0)
+    model = make_model(dev)
+    H, D, Dv = CFG["heads"], CFG["key_dim"], CFG["value_dim"]
+    per_unit, pbytes = decode_bytes_per_unit(CFG), decode_param_bytes(CFG)
+    pk = peaks()
+    rows = {}
+    for B in DECODE_BATCHES:
+        g = torch.Generator(device=dev).manual_seed(1000 + B)
+        seg = 512 if B <= 64 else 64  # prefill in segments: the forward's workspace scales with B*T
+        with torch.no_grad():
+            state = model.initial_state(B, device=dev, dtype=torch.bfloat16)
+            for _ in range(DECODE_PREFILL // seg):
+                xs = [torch.randn(B, seg, H, w, device=dev, generator=g) for w in (D, D, Dv)]
+                xs[0] = xs[0] / xs[0].norm(dim=-1, keepdim=True)
+                xs[1] = xs[1] / xs[1].norm(dim=-1, keepdim=True)
+                _, state = model(*(x.bfloat16() for x in xs), state)
+            sess = DecodeSession(model, state, torch.bfloat16)
+            del state
+            torch.cuda.empty_cache()
+            steps = max(args.steps, 64)
+            host = [[x.cpu().pin_memory() for x in make_inputs(B, 1, 7 + i)] for i in range(8)]
+            static = [x.to(dev) for x in host[0]]
+            out = sess.capture(*static)
+            for i in range(max(args.warmup, 3)):
+                sess.replay()
+            torch.cuda.synchronize()
+            launches0 = _lib.launch_count()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(0) as clocks:
+                e0.record()
+                for _ in range(steps):
+                    sess.replay()
+                e1.record()
+                torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            # end to end: pinned host inputs in, output back, every step
+            hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+            t0 = time.perf_counter()
+            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e2.record()
+            for i in range(steps):
+                for s_, h_ in zip(static, host[i % len(host)]):
+                    s_.copy_(h_, non_blocking=True)
+                sess.replay()
+                hout.copy_(out, non_blocking=True)
+            e3.record()
+            torch.cuda.synchronize()
+            e2e_ms = max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3) / steps
+            U = B * H
+            byts = U * per_unit + pbytes
+            rows[B] = {"us_per_step": round(ms * 1e3, 2), "tokens_per_s": round(B / ms * 1e3, 1),
+                       "e2e_tokens_per_s": round(B / e2e_ms * 1e3, 1),
+                       "achieved_gbs": round(byts / (ms / 1e3) / 1e9, 1),
+                       "frac": round(byts / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                       "bytes_per_step": byts, "clocks": clocks.summary()}
+            del sess, out, static
+            torch.cuda.empty_cache()
+    top = rows[DECODE_BATCHES[-1]]
+    Bt = DECODE_BATCHES[-1]
+    h2d = 2 * Bt * H * (2 * D + Dv)
+    result = {
+        "metric": "DenseGPA decode tokens/s (config 4: config-2 layer, prefill 4096, CUDA graph)",
+        "value": top["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": max(args.steps, 64),
+        "warmup": max(args.warmup, 3), "ms_per_step": round(top["us_per_step"] / 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, random-init weights)",
+        "config": {"workload": f"config 4 decode, B={Bt}", "model": "DenseGPA", "global_batch": Bt,
+                   "seq_len": 1, "prefill": DECODE_PREFILL, "state_dtype": "fp32",
+                   "l2": f"cache {Bt * H * per_unit / 1e9:.2f} GB per step > 126 MB L2; no flush"},
+        "e2e": {"value": top["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": Bt * H * Dv * 2},
+        "gpu_launches": 2,
+        "roofline": {"bound": "hbm", "achieved": top["achieved_gbs"], "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": top["frac"], "traffic": None, "kernel": "decode_step",
+                     "bytes_per_step": top["bytes_per_step"], "peak_source": pk["source"]},
+        "by_batch": rows,
+        "clocks": top["clocks"],
+    }
+    return result
+
+
 # --------------------------------------------------------------- CPU (oracle) arm
 
 def cpu_sample_step(threads):
@@ -403,6 +510,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["train", "decode"], default="train",
+                    help="train: config-2 fwd+bwd (the headline); decode: config-4 one-token steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="per-rank batch (default: config 2); smaller values are for profiling")
@@ -413,6 +522,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "decode" and args.impl == "b200":
+        if rank == 0:
+            print(json.dumps(run_decode(args)), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank)
         if res is not None:
