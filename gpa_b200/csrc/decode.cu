@@ -67,29 +67,55 @@ GPA_DEV void softmax_vec(float* dst, const float* src, int n, float* red) {
   __syncthreads();
 }
 
-// y[c] = sum_r x[r] S[r][c] for S [R x Cn] row-major (shared or global); Cn <= blockDim.
-// part: blockDim floats.  Ends synchronized.
+GPA_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+GPA_DEV void fma4(float4& a, float x, float4 b) {
+  a.x += x * b.x;
+  a.y += x * b.y;
+  a.z += x * b.z;
+  a.w += x * b.w;
+}
+
+// y[c] = sum_r x[r] S[r][c] for S [R x Cn] row-major (shared or global), Cn a multiple of 4
+// and Cn / 4 <= blockDim: a thread owns 4 columns of a slice of the rows, four rows in
+// flight; part: 4 * blockDim floats.  Ends synchronized.
 GPA_DEV void colsum(const float* S, int R, int Cn, const float* x, float* y, float* part) {
-  const int P = blockDim.x / Cn, c = threadIdx.x % Cn, pr = threadIdx.x / Cn;
-  float acc = 0.f;
-  if (pr < P)
-    for (int r = pr; r < R; r += P) acc += x[r] * S[(int64_t)r * Cn + c];
-  part[threadIdx.x] = acc;
+  const int c4n = Cn >> 2, P = blockDim.x / c4n;
+  const int c4 = threadIdx.x % c4n, pr = threadIdx.x / c4n;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (pr < P) {
+    const float* col = S + 4 * c4;
+    int r = pr;
+    for (; r + 3 * P < R; r += 4 * P) {
+      const float4 a0 = ld4(col + (int64_t)r * Cn), a1 = ld4(col + (int64_t)(r + P) * Cn);
+      const float4 a2 = ld4(col + (int64_t)(r + 2 * P) * Cn), a3 = ld4(col + (int64_t)(r + 3 * P) * Cn);
+      fma4(acc, x[r], a0);
+      fma4(acc, x[r + P], a1);
+      fma4(acc, x[r + 2 * P], a2);
+      fma4(acc, x[r + 3 * P], a3);
+    }
+    for (; r < R; r += P) fma4(acc, x[r], ld4(col + (int64_t)r * Cn));
+    *reinterpret_cast<float4*>(part + pr * Cn + 4 * c4) = acc;
+  }
   __syncthreads();
-  if (threadIdx.x < Cn) {
+  for (int c = threadIdx.x; c < Cn; c += blockDim.x) {
     float s = 0.f;
-    for (int i = 0; i < P; ++i) s += part[i * Cn + threadIdx.x];
-    y[threadIdx.x] = s;
+    for (int i = 0; i < P; ++i) s += part[i * Cn + c];
+    y[c] = s;
   }
   __syncthreads();
 }
 
-// y[r] = sum_c S[r][c] x[c] for S [R x Cn] row-major: a warp per row.  Ends synchronized.
+// y[r] = sum_c S[r][c] x[c] for S [R x Cn] row-major, Cn a multiple of 4: a warp per row,
+// float4 columns.  Ends synchronized.
 GPA_DEV void rowdot(const float* S, int R, int Cn, const float* x, float* y) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int r = w; r < R; r += nw) {
     float acc = 0.f;
-    for (int c = lane; c < Cn; c += 32) acc += S[(int64_t)r * Cn + c] * x[c];
+    for (int c = 4 * lane; c < Cn; c += 128) {
+      const float4 a = ld4(S + (int64_t)r * Cn + c);
+      acc += a.x * x[c] + a.y * x[c + 1] + a.z * x[c + 2] + a.w * x[c + 3];
+    }
     acc = warp_sum(acc);
     if (lane == 0) y[r] = acc;
   }
@@ -163,7 +189,7 @@ struct StepSmem {
     tmp2 = take(wide);
     pre = take(w > mx ? w : mx);
     yb = take(a.Dv);
-    part = take(kStepThreads);
+    part = take(4 * kStepThreads);
     red = take(32);
     slot = take(a.L * mx);
     write = take(a.L * mx);
