@@ -110,24 +110,40 @@ GPA_DEV void colsum(const float* S, int R, int Cn, const float* x, float* y, flo
 // float4 columns.  Ends synchronized.
 GPA_DEV void rowdot(const float* S, int R, int Cn, const float* x, float* y) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int r = w; r < R; r += nw) {
-    float acc = 0.f;
+  for (int r0 = w; r0 < R; r0 += 4 * nw) {  // four rows of a warp in flight
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = 4 * lane; c < Cn; c += 128) {
-      const float4 a = ld4(S + (int64_t)r * Cn + c);
-      acc += a.x * x[c] + a.y * x[c + 1] + a.z * x[c + 2] + a.w * x[c + 3];
+      const float4 xv = ld4(x + c);
+      float4 a[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        a[i] = r0 + i * nw < R ? ld4(S + (int64_t)(r0 + i * nw) * Cn + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += a[i].x * xv.x + a[i].y * xv.y + a[i].z * xv.z + a[i].w * xv.w;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) y[r] = acc;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float s = warp_sum(acc[i]);
+      if (lane == 0 && r0 + i * nw < R) y[r0 + i * nw] = s;
+    }
   }
   __syncthreads();
 }
 
 // shared <- global (n floats, multiple of 4, 16-byte aligned); optional copy to `also`
 GPA_DEV void load_mat(float* Ss, const float* g, int n, float* also) {
-  for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {
-    const float4 x = *reinterpret_cast<const float4*>(g + i);
-    *reinterpret_cast<float4*>(Ss + i) = x;
-    if (also) *reinterpret_cast<float4*>(also + i) = x;
+  const int step = 4 * blockDim.x;
+  for (int i0 = 4 * threadIdx.x; i0 < n; i0 += 4 * step) {  // four float4 in flight
+    float4 x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (i0 + j * step < n) x[j] = ld4(g + i0 + j * step);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (i0 + j * step < n) {
+        *reinterpret_cast<float4*>(Ss + i0 + j * step) = x[j];
+        if (also) *reinterpret_cast<float4*>(also + i0 + j * step) = x[j];
+      }
   }
   __syncthreads();
 }
@@ -247,8 +263,17 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
         r[3] += kn[d] * w4.w;
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) r[c] = block_sum_all(r[c], red) + a.p.gate_bias[j][h * 4 + c];
+      for (int c = 0; c < 4; ++c) r[c] = warp_sum(r[c]);
+      __syncthreads();
+      if ((threadIdx.x & 31) == 0)
+        for (int c = 0; c < 4; ++c) part[4 * (threadIdx.x >> 5) + c] = r[c];
+      __syncthreads();
       if (threadIdx.x == 0) {
+        for (int c = 0; c < 4; ++c) {
+          float t = a.p.gate_bias[j][h * 4 + c];
+          for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[4 * w + c];
+          r[c] = t;
+        }
         gates[0] = a.pos_none ? 0.f : -fminf(softplus(r[0]), 10.f);
         gates[1] = a.beta_max * sigmoid(r[1]);
         gates[2] = a.pos_none ? 0.f : -fminf(softplus(r[2]), 10.f);
