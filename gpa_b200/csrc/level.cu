@@ -159,6 +159,45 @@ __global__ void __launch_bounds__(256) k_level_post(
 }
 
 // CTA per (u, lag block): counts = n0 + cumsum(write); logits; u(local); u(write).
+// dst[i] = src[i], i < n: float4 when `vec` (n, and both pointers' offsets, multiples of 4
+// floats; the caller checks M % 4 == 0), else scalar
+GPA_DEV void copy_rows(float* dst, const float* src, int n, bool vec) {
+  if (vec) {
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x)
+      *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(src + i);
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// Sum over the earlier lag blocks (before < 0: the later ones) of per-block vectors
+// [U, NB, M], all threads: partial sums in `part` (blockDim floats), result in pre[M].
+GPA_DEV void block_prefix(const float* bsum, int u, int nb, int first, int last, int M,
+                          float* pre, float* part) {
+  const int G = blockDim.x / M;  // thread groups per slot (M <= blockDim)
+  const int m = threadIdx.x % M, g = threadIdx.x / M;
+  float acc = 0.f;
+  if (g < G) {
+    const float* base = bsum + (int64_t)u * nb * M + m;
+    int p = first + g;
+    for (; p + 3 * G < last; p += 4 * G)
+      acc += (base[(int64_t)p * M] + base[(int64_t)(p + G) * M]) +
+             (base[(int64_t)(p + 2 * G) * M] + base[(int64_t)(p + 3 * G) * M]);
+    for (; p < last; p += G) acc += base[(int64_t)p * M];
+  }
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  for (int mm = threadIdx.x; mm < M; mm += blockDim.x) {
+    float s = 0.f;
+    for (int i = 0; i < G; ++i) s += part[i * M + mm];
+    pre[mm] = s;
+  }
+  __syncthreads();
+}
+
+// CTA per (u, lag block), level j: running counts from the incoming cache and the earlier
+// blocks, base logits, the normalised local distribution and write (relation queries / keys).
+// The block's write tile is staged in shared memory (rows t < c contiguous from t0).
 __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, float read_scale,
                                                 const float* count_gain_raw, int j,
                                                 const float* n0, const float* bsum,
@@ -168,22 +207,32 @@ __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, 
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
   const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  extern __shared__ __align__(16) float smc[];
+  float* Wt = smc;                     // [64 x M] write rows of the block
+  float* Ct = Wt + kRowsPerTile * M;   // [64 x M] counts
+  float* pre = Ct + kRowsPerTile * M;  // [M]
+  float* part = pre + M;               // [blockDim]
+  const int64_t r0 = row(u, T, t0) * M;
+  const bool vec = M % 4 == 0;
+  copy_rows(Wt, write + r0, c * M, vec);
+  block_prefix(bsum, u, bl.nb, 0, n, M, pre, part);
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    float acc = n0[(int64_t)u * M + m];
-    for (int p = 0; p < n; ++p) acc += bsum[((int64_t)u * bl.nb + p) * M + m];
+    float acc = n0[(int64_t)u * M + m] + pre[m];
     for (int t = 0; t < c; ++t) {
-      acc += write[row(u, T, t0 + t) * M + m];
-      counts[row(u, T, t0 + t) * M + m] = acc;
+      acc += Wt[t * M + m];
+      Ct[t * M + m] = acc;
     }
     if (n == bl.nb - 1) n_final[(int64_t)u * M + m] = acc;
   }
   __syncthreads();
+  copy_rows(counts + r0, Ct, c * M, vec);
   const float gain = softplus(count_gain_raw[j * H + h]);
   for (int t = warp; t < c; t += nw) {
     const int64_t o = row(u, T, t0 + t);
     float x[kMaxPerLane], w[kMaxPerLane], cn[kMaxPerLane];
     load_vec(x, raw + o * M, M);
-    load_vec(cn, counts + o * M, M);
+    load_vec(cn, Ct + t * M, M);
+    load_vec(w, Wt + t * M, M);
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) x[i] = read_scale * x[i] + gain * log1pf(cn[i]);
     store_vec(logits + o * M, x, M);
@@ -193,7 +242,6 @@ __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, 
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
     store_vec(lh + o * M, x, M);
-    load_vec(w, write + o * M, M);
     const float b = warp_norm(w, M);
     const float ib = 1.f / fmaxf(b, kUnitEps);
 #pragma unroll
@@ -549,69 +597,156 @@ __global__ void __launch_bounds__(256) k_bridge_bwd(
 }
 
 // one warp per (u, t), level j: logits / local-softmax / count-log backward.
-__global__ void k_logits_bwd(int U, Blocks bl, int H, int M, int L, int j, float read_scale,
-                             const float* count_gain_raw, const float* logits,
-                             const float* counts, const float* lh, const float* ln,
-                             const float* wh, const float* wn, const float* dlh, const float* dwh,
-                             const float* dlogits, float* dwrite, float* draw, float* dn,
-                             float* dnsum, double* scal) {
-  const int T = bl.T;
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (w >= U * T) return;
-  const int u = w / T, t = w - u * T, h = u % H;
-  const int64_t o = (int64_t)w * M;
-  const float cgr = count_gain_raw[j * H + h];
-  const float gain = softplus(cgr);
-  float x[kMaxPerLane], y[kMaxPerLane], dy[kMaxPerLane], d1[kMaxPerLane], d2[kMaxPerLane];
-  load_vec(x, logits + o, M);
-  warp_softmax(x, M);  // local
-  load_vec(y, lh + o, M);
-  load_vec(dy, dlh + o, M);
-  unit_bwd(d1, y, dy, ln[w], M);  // dlocal
-  softmax_bwd(d2, x, d1, M);
-  load_vec(d1, dlogits + o, M);
-  float cn[kMaxPerLane];
-  load_vec(cn, counts + o, M);
-  float cg = 0.f;
+// Row vectors of NPL values per lane (M <= 32 * NPL), sized to the level's width so that
+// every row read can be in flight at once without spending occupancy.
+template <int NPL>
+struct RowV {
+  float v[NPL];
+  GPA_DEV void load(const float* p, int n) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    const float dl = d1[i] + d2[i];
-    d1[i] = read_scale * dl;
-    if (lane + 32 * i < M) cg += dl * log1pf(cn[i]);
-    d2[i] = gain * dl / (1.f + cn[i]);
+    for (int i = 0; i < NPL; ++i) v[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
   }
-  store_vec(draw + o, d1, M);
-  store_vec(dn + o, d2, M);
-  const int n = bl.block_of(t);
+  GPA_DEV void store(float* p, int n) const {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < M) atomicAdd(&dnsum[((int64_t)u * bl.nb + n) * M + lane + 32 * i], d2[i]);
-  cg = warp_sum(cg);
-  if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], (double)cg);
-  load_vec(y, wh + o, M);
-  load_vec(dy, dwh + o, M);
-  unit_bwd(d1, y, dy, wn[w], M);
-  load_vec(d2, dwrite + o, M);
+    for (int i = 0; i < NPL; ++i)
+      if (lane + 32 * i < n) p[lane + 32 * i] = v[i];
+  }
+  GPA_DEV float dot(const RowV& o, int n) const {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) d2[i] += d1[i];
-  store_vec(dwrite + o, d2, M);
+    for (int i = 0; i < NPL; ++i)
+      if (lane + 32 * i < n) s += v[i] * o.v[i];
+    return warp_sum(s);
+  }
+};
+
+// Warp per token row, 8 rows per CTA: every global read of a row is issued before its
+// stores (which may alias), and the per-block count gradients of the CTA's rows are summed
+// in shared memory before one atomic per slot and block.
+template <int NPL>
+__global__ void __launch_bounds__(256) k_logits_bwd(
+    int U, Blocks bl, int H, int M, int L, int j, float read_scale, const float* count_gain_raw,
+    const float* logits, const float* counts, const float* lh, const float* ln, const float* wh,
+    const float* wn, const float* dlh, const float* dwh, const float* dlogits, float* dwrite,
+    float* draw, float* dn, float* dnsum, double* scal) {
+  __shared__ float red_dn[8][32 * NPL];
+  __shared__ int blk[8];
+  const int T = bl.T;
+  const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x >> 5) + wi;
+  const bool live = w < U * T;
+  const int u = live ? w / T : 0, t = live ? w - u * T : 0, h = u % H;
+  const int64_t o = (int64_t)w * M;
+  if (live) {
+    RowV<NPL> x, y, dy, dlg, cn, y2, dy2, dw;
+    x.load(logits + o, M);
+    y.load(lh + o, M);
+    dy.load(dlh + o, M);
+    dlg.load(dlogits + o, M);
+    cn.load(counts + o, M);
+    y2.load(wh + o, M);
+    dy2.load(dwh + o, M);
+    dw.load(dwrite + o, M);
+    const float lno = ln[w], wno = wn[w];
+    const float gain = softplus(count_gain_raw[j * H + h]);
+    // local = softmax(logits)
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i)
+      if (lane + 32 * i < M) mx = fmaxf(mx, x.v[i]);
+    mx = warp_max(mx);
+    float se = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      x.v[i] = lane + 32 * i < M ? __expf(x.v[i] - mx) : 0.f;
+      se += x.v[i];
+    }
+    const float inv = 1.f / warp_sum(se);
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) x.v[i] *= inv;
+    // dlocal = unit backward of lh
+    RowV<NPL> d1;
+    if (lno > kUnitEps) {
+      const float yd = y.dot(dy, M), il = 1.f / lno;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) d1.v[i] = (dy.v[i] - y.v[i] * yd) * il;
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) d1.v[i] = dy.v[i] / kUnitEps;
+    }
+    const float xd = x.dot(d1, M);
+    RowV<NPL> dr, dnv;
+    float cg = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      const float dl = dlg.v[i] + x.v[i] * (d1.v[i] - xd);
+      dr.v[i] = read_scale * dl;
+      if (lane + 32 * i < M) cg += dl * log1pf(cn.v[i]);
+      dnv.v[i] = gain * dl / (1.f + cn.v[i]);
+    }
+    dr.store(draw + o, M);
+    dnv.store(dn + o, M);
+    cg = warp_sum(cg);
+    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], (double)cg);
+    if (wno > kUnitEps) {
+      const float yd = y2.dot(dy2, M), iw = 1.f / wno;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) dw.v[i] += (dy2.v[i] - y2.v[i] * yd) * iw;
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) dw.v[i] += dy2.v[i] / kUnitEps;
+    }
+    dw.store(dwrite + o, M);
+    dnv.store(&red_dn[wi][0], M);
+    if (lane == 0) blk[wi] = u * bl.nb + bl.block_of(t);
+  } else if (lane == 0) {
+    blk[wi] = -1;
+  }
+  __syncthreads();
+  // rows of the CTA that share (unit, block) are consecutive: one atomic per run and slot
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    int r = 0;
+    while (r < 8) {
+      const int b = blk[r];
+      float s = 0.f;
+      int e = r;
+      for (; e < 8 && blk[e] == b; ++e) s += red_dn[e][m];
+      if (b >= 0) atomicAdd(&dnsum[(int64_t)b * M + m], s);
+      r = e;
+    }
+  }
 }
 
-// CTA per (u, lag block): dwrite += suffix sums of dn; dn0.
-__global__ void k_counts_bwd(int U, Blocks bl, int M, const float* dn, const float* dnsum,
-                             const float* dn_final, float* dwrite, float* dn0) {
+// CTA per (u, lag block): dwrite += suffix sums of dn; dn0.  The block's dn and dwrite
+// rows are staged in shared memory (rows t < c contiguous from t0).
+__global__ void __launch_bounds__(256) k_counts_bwd(int U, Blocks bl, int M, const float* dn,
+                                                    const float* dnsum, const float* dn_final,
+                                                    float* dwrite, float* dn0) {
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0;
+  extern __shared__ __align__(16) float smc[];
+  float* Dn = smc;                     // [64 x M]
+  float* Dw = Dn + kRowsPerTile * M;   // [64 x M]
+  float* suf = Dw + kRowsPerTile * M;  // [M]
+  float* part = suf + M;               // [blockDim]
+  const int64_t r0 = row(u, T, t0) * M;
+  const bool vec = M % 4 == 0;
+  copy_rows(Dn, dn + r0, c * M, vec);
+  copy_rows(Dw, dwrite + r0, c * M, vec);
+  block_prefix(dnsum, u, bl.nb, n + 1, bl.nb, M, suf, part);
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    float acc = dn_final ? dn_final[(int64_t)u * M + m] : 0.f;
-    for (int p = n + 1; p < bl.nb; ++p) acc += dnsum[((int64_t)u * bl.nb + p) * M + m];
+    float acc = (dn_final ? dn_final[(int64_t)u * M + m] : 0.f) + suf[m];
     for (int t = c - 1; t >= 0; --t) {
-      const int64_t o = row(u, T, t0 + t) * M + m;
-      acc += dn[o];
-      dwrite[o] += acc;
+      acc += Dn[t * M + m];
+      Dw[t * M + m] += acc;
     }
     if (n == 0) dn0[(int64_t)u * M + m] = acc;
   }
+  __syncthreads();
+  copy_rows(dwrite + r0, Dw, c * M, vec);
 }
 
 // CTA per (u, lag block), level j: residual + write backward; frozen-snapshot gradients.
@@ -966,7 +1101,13 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
                           cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
   Launch scope_("counts", st);
-  k_counts<<<U * bl.nb, 256, 0, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write,
+  const size_t smem = (2 * kRowsPerTile * M + M + 256) * sizeof(float);
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_counts, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  k_counts<<<U * bl.nb, 256, smem, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write,
                                       raw, counts, logits, lh, ln, wh, wn, n_final);
   return cudaGetLastError();
 }
@@ -1089,7 +1230,18 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
   const int rows = U * bl.T;
   if (!rows) return cudaSuccess;
   Launch scope_("logits_bwd", st);
-  k_logits_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
+  if (M <= 64)
+    k_logits_bwd<2><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
+                                                     count_gain_raw, logits, counts, lh, ln, wh,
+                                                     wn, dlh, dwh, dlogits, dwrite, draw, dn,
+                                                     dnsum, scal);
+  else if (M <= 128)
+    k_logits_bwd<4><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
+                                                     count_gain_raw, logits, counts, lh, ln, wh,
+                                                     wn, dlh, dwh, dlogits, dwrite, draw, dn,
+                                                     dnsum, scal);
+  else
+    k_logits_bwd<8><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
                                                      dnsum, scal);
@@ -1100,7 +1252,13 @@ cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, c
                               const float* dn_final, float* dwrite, float* dn0, cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
   Launch scope_("counts_bwd", st);
-  k_counts_bwd<<<U * bl.nb, 256, 0, st>>>(U, bl, M, dn, dnsum, dn_final, dwrite, dn0);
+  const size_t smem = (2 * kRowsPerTile * M + M + 256) * sizeof(float);
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_counts_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  k_counts_bwd<<<U * bl.nb, 256, smem, st>>>(U, bl, M, dn, dnsum, dn_final, dwrite, dn0);
   return cudaGetLastError();
 }
 

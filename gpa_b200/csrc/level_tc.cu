@@ -55,7 +55,7 @@ struct LPrep {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_level_prep(int U, int T, int H, int D, int M,
+__global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D, int M,
                                                      const float* key, const float* C,
                                                      const float* Wg, const float* gbias,
                                                      float beta_max, int pos_none, float* nk,
@@ -152,7 +152,7 @@ struct LPost {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_level_post(
+__global__ void __launch_bounds__(512) tk_level_post(
     int U, Blocks bl, int post, int H, int D, int Dv, int M, int with_residual, const float* nk,
     const float* key, const float* val, const float* Abnd, const float* Bbnd, const float* fzA,
     const float* fzB, const float* residual_raw, int j, float* write, float* bsum,
@@ -358,7 +358,7 @@ struct LBridge {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_bridge(
+__global__ void __launch_bounds__(512) tk_bridge(
     int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
     const float* relation_gain, const float* route_up, const float* route_down,
     const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
@@ -476,7 +476,7 @@ struct LBridgeBwd {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_bridge_bwd(
+__global__ void __launch_bounds__(512) tk_bridge_bwd(
     int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
     const float* relation_gain, const float* route_up, const float* route_down,
     const float* route_mlp_gain, const float* Wrs, const float* Wqs, float qs,
@@ -658,7 +658,7 @@ struct LPostBwd {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_post_bwd(
+__global__ void __launch_bounds__(512) tk_post_bwd(
     int U, Blocks bl, int post, int offset, int H, int D, int Dv, int M, int L, int j,
     int with_residual, const float* nk, const float* write, const float* Abnd, const float* Bbnd,
     const float* fzA, const float* fzB, const float* residual_raw, const float* dkey,
@@ -805,7 +805,7 @@ struct LPrepBwd {
   }
 };
 
-__global__ void __launch_bounds__(256) tk_prep_bwd(int U, int T, int H, int D, int M,
+__global__ void __launch_bounds__(512) tk_prep_bwd(int U, int T, int H, int D, int M,
                                                    const float* C, const float* Wg,
                                                    float beta_max, int pos_none, const float* raw4,
                                                    const float* nk, const float* kn,
@@ -990,8 +990,12 @@ cudaError_t tk_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStre
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  // a CTA that needs more than half of an SM's shared memory runs alone on its SM: give it
+  // 16 warps (the per-row loops and tiles adapt to blockDim); head_outer's tiling is fixed
+  // at 8 warps and its shared memory is small
+  const int threads = smem > 113 * 1024 ? 512 : 256;
   Launch scope(name, st);
-  k<<<grid, 256, smem, st>>>(args...);
+  k<<<grid, threads, smem, st>>>(args...);
   return cudaGetLastError();
 }
 
