@@ -144,10 +144,10 @@ GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
 // A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
 GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
                         const float* bt, float* A, float* Atil) {
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> acc;
     acc.zero();
-    tc::mma_acc3<1, 2, false, true>(acc, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
+    tc::mma_acc3<1, 1, false, true>(acc, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
     acc.each(m0, n0, [&](int t, int s, float& v) {
       const float at = s < t ? __expf(G[t] - G[s]) * v : 0.f;
       A[t * kAStride + s] = bt[t] * at;
@@ -407,10 +407,10 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, nullptr);
   }
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> acc;
     acc.zero();
-    mma_acc<1, 2, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
+    mma_acc<1, 1, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
     acc.each(m0, n0, [&](int t, int s, float& v) {
       tc::split_bf16(s <= t ? __expf(G[t] - G[s]) * v : 0.f, Ph + t * LDT + s, Pl + t * LDT + s);
     });
@@ -491,20 +491,20 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
   }
   // P = (Q K^T) o Gamma and dP = dO W^T on the same tile: rowsum / colsum of P o dP and
   // dX = dP o Gamma straight from the accumulators
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> pa, da;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> pa, da;
     pa.zero();
-    mma_acc<1, 2, false, true>(pa, Qs, ldk, Ks, ldk, m0, n0, K);
+    mma_acc<1, 1, false, true>(pa, Qs, ldk, Ks, ldk, m0, n0, K);
     pa.each(m0, n0, [&](int t, int s, float& v) {
       v = s <= t ? __expf(G[t] - G[s]) * v : 0.f;
       tc::split_bf16(v, Ph + t * LDT + s, Pl + t * LDT + s);
     });
     da.zero();
-    tc::mma_acc3<1, 2, false, true>(da, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
+    tc::mma_acc3<1, 1, false, true>(da, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    float rsum[2] = {0.f, 0.f}, csum[4][2] = {};
+    float rsum[2] = {0.f, 0.f}, csum[2][2] = {};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int t = m0 + g + 8 * (r >> 1), s = n0 + 8 * j + 2 * q + (r & 1);
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
       atomicAdd(&rs[m0 + g + 8], r1s);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float x = csum[j][h];
@@ -918,10 +918,10 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       atomicAdd(&db[m0 + g + 8], p1);
     }
   });
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> acc;
     acc.zero();
-    tc::mma_acc3<1, 2, false, true>(acc, dWh, dWl, ldv, Uh, Ul, ldv, m0, n0, V);
+    tc::mma_acc3<1, 1, false, true>(acc, dWh, dWl, ldv, Uh, Ul, ldv, m0, n0, V);
     acc.each(m0, n0, [&](int t, int s, float& v) { dAf[t * kAStride + s] = v; });
   });
   __syncthreads();
@@ -958,10 +958,10 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       atomicAdd(&rw[m0 + g + 8], p1);
     }
   });
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> acc;
     acc.each(m0, n0, [&](int t, int s, float& v) { v = dAf[t * kAStride + s]; });
-    tc::mma_acc3<1, 2, false, true>(acc, dWkh, dWkl, ldk, Wkh, Wkl, ldk, m0, n0, K);
+    tc::mma_acc3<1, 1, false, true>(acc, dWkh, dWkl, ldk, Wkh, Wkl, ldk, m0, n0, K);
     acc.each(m0, n0, [&](int t, int s, float& v) {
       tc::split_bf16(v, Mh + t * LDT + s, Ml + t * LDT + s);
     });
@@ -973,10 +973,10 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     dG[t] += bt[t] * e * rw[t];
   }
   // dA = -T^T M, strictly lower
-  for_tiles<1, 2>(C, C, [&](int m0, int n0) {
-    Acc<1, 2> acc;
+  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+    Acc<1, 1> acc;
     acc.zero();
-    tc::mma_acc3<1, 2, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
+    tc::mma_acc3<1, 1, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
     acc.each(m0, n0, [&](int t, int s, float& v) {
       dAf[t * kAStride + s] = (s < t && t < c) ? -v : 0.f;
     });

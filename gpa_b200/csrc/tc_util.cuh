@@ -161,9 +161,12 @@ GPA_DEV void copy_f4(float* dst, const float* src, int n) {
 
 template <int MI, int NI, class Body>
 GPA_DEV void tiles_n(int M, int N, Body body) {
-  // NI chosen at run time: 32-wide tiles when N allows, else 16-wide
-  if (N % 32 == 0) for_tiles<MI, 2>(M, N, [&](int m0, int n0) { body.template operator()<2>(m0, n0); });
-  else for_tiles<MI, 1>(M, N, [&](int m0, int n0) { body.template operator()<1>(m0, n0); });
+  // NI chosen at run time: 32-wide tiles when N allows and they still give every warp a
+  // tile, else 16-wide
+  if (N % 32 == 0 && (M / (16 * MI)) * (N / 32) >= (int)(blockDim.x >> 5))
+    for_tiles<MI, 2>(M, N, [&](int m0, int n0) { body.template operator()<2>(m0, n0); });
+  else
+    for_tiles<MI, 1>(M, N, [&](int m0, int n0) { body.template operator()<1>(m0, n0); });
 }
 
 }  // namespace tc
