@@ -366,12 +366,14 @@ def run_decode(args):
     per_unit, pbytes = decode_bytes_per_unit(CFG), decode_param_bytes(CFG)
     pk = peaks()
     rows = {}
-    for B in DECODE_BATCHES:
+    batches = tuple(int(b) for b in args.decode_batches.split(","))
+    for B in batches:
         g = torch.Generator(device=dev).manual_seed(1000 + B)
         seg = 512 if B <= 64 else 64  # prefill in segments: the forward's workspace scales with B*T
+        seg = min(seg, args.prefill)
         with torch.no_grad():
             state = model.initial_state(B, device=dev, dtype=torch.bfloat16)
-            for _ in range(DECODE_PREFILL // seg):
+            for _ in range(args.prefill // seg):
                 xs = [torch.randn(B, seg, H, w, device=dev, generator=g) for w in (D, D, Dv)]
                 xs[0] = xs[0] / xs[0].norm(dim=-1, keepdim=True)
                 xs[1] = xs[1] / xs[1].norm(dim=-1, keepdim=True)
@@ -417,8 +419,8 @@ def run_decode(args):
                        "bytes_per_step": byts, "clocks": clocks.summary()}
             del sess, out, static
             torch.cuda.empty_cache()
-    top = rows[DECODE_BATCHES[-1]]
-    Bt = DECODE_BATCHES[-1]
+    top = rows[batches[-1]]
+    Bt = batches[-1]
     h2d = 2 * Bt * H * (2 * D + Dv)
     result = {
         "metric": "DenseGPA decode tokens/s (config 4: config-2 layer, prefill 4096, CUDA graph)",
@@ -427,7 +429,7 @@ def run_decode(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, random-init weights)",
         "config": {"workload": f"config 4 decode, B={Bt}", "model": "DenseGPA", "global_batch": Bt,
-                   "seq_len": 1, "prefill": DECODE_PREFILL, "state_dtype": "fp32",
+                   "seq_len": 1, "prefill": args.prefill, "state_dtype": "fp32",
                    "l2": f"cache {Bt * H * per_unit / 1e9:.2f} GB per step > 126 MB L2; no flush"},
         "e2e": {"value": top["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": Bt * H * Dv * 2},
@@ -512,6 +514,10 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["train", "decode"], default="train",
                     help="train: config-2 fwd+bwd (the headline); decode: config-4 one-token steps")
+    ap.add_argument("--decode-batches", default=",".join(str(b) for b in DECODE_BATCHES),
+                    help="decode: batch sizes (the last one is the headline line)")
+    ap.add_argument("--prefill", type=int, default=DECODE_PREFILL,
+                    help="decode: prefill length before the steps (config 4: 4096)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="per-rank batch (default: config 2); smaller values are for profiling")
