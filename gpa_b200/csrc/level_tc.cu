@@ -943,31 +943,49 @@ __global__ void __launch_bounds__(256) tk_head_outer(int B, int T, int H, const 
     act[i] = tm[i] < pw && tn[i] < qw;
     acc[i].zero();
   }
-  for (int64_t rr = r0; rr < r1; rr += kORows) {
+  // Each thread moves 4 float4 of X and 4 of Y per 64-row step; the next step's values are
+  // loaded into registers while the current step's MMAs run.
+  constexpr int kPer = kORows * (kOTile / 4) / 256;
+  float4 xn[kPer], yn[kPer];
+  auto fetch = [&](int64_t rr) {
     const int rows = (int)min((int64_t)kORows, r1 - rr);
-    __syncthreads();
-    for (int i = threadIdx.x; i < kORows * (kOTile / 4); i += blockDim.x) {
+    const int b0 = (int)(rr / T), t0 = (int)(rr - (int64_t)b0 * T);  // one division per step
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * 256;
       const int rw = i / (kOTile / 4), cc = (i % (kOTile / 4)) * 4;
-      float4 xv = make_float4(0.f, 0.f, 0.f, 0.f), yv = xv;
+      xn[j] = yn[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (rw < rows) {
-        const int64_t g = rr + rw;
-        const int b = (int)(g / T), t = (int)(g - (int64_t)b * T);
-        const int64_t o = row(b * H + h, T, t);
-        if (cc < pw) {
-          xv = *reinterpret_cast<const float4*>(X + o * P + p0 + cc);
-          if (xmode == 1) {
-            xv.x = gelu(xv.x);
-            xv.y = gelu(xv.y);
-            xv.z = gelu(xv.z);
-            xv.w = gelu(xv.w);
-          }
+        int b = b0, t = t0 + rw;
+        while (t >= T) {  // rows of a step cross at most a few sequence ends
+          t -= T;
+          ++b;
         }
-        if (cc < qw) yv = *reinterpret_cast<const float4*>(Y + o * Q + q0 + cc);
+        const int64_t o = row(b * H + h, T, t);
+        if (cc < pw) xn[j] = *reinterpret_cast<const float4*>(X + o * P + p0 + cc);
+        if (cc < qw) yn[j] = *reinterpret_cast<const float4*>(Y + o * Q + q0 + cc);
+      }
+    }
+  };
+  if (r0 < r1) fetch(r0);
+  for (int64_t rr = r0; rr < r1; rr += kORows) {
+    __syncthreads();  // the previous step's MMAs are done with the tiles
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * 256;
+      const int rw = i / (kOTile / 4), cc = (i % (kOTile / 4)) * 4;
+      float4 xv = xn[j];
+      if (xmode == 1) {
+        xv.x = gelu(xv.x);
+        xv.y = gelu(xv.y);
+        xv.z = gelu(xv.z);
+        xv.w = gelu(xv.w);
       }
       tc::put4(Xh, Xl, rw * lo + cc, xv);
-      tc::put4(Yh, Yl, rw * lo + cc, yv);
+      tc::put4(Yh, Yl, rw * lo + cc, yn[j]);
     }
     __syncthreads();
+    if (rr + kORows < r1) fetch(rr + kORows);
 #pragma unroll
     for (int i = 0; i < 2; ++i)
       if (act[i])
