@@ -41,6 +41,11 @@ METRIC = "DenseGPA fwd+bwd tokens/s at 1/2/4/8 B200 (T=8192) + % of roofline"
 CFG = dict(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
 BATCH, LENGTH = 8, 8192
 CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
+# DRAM bytes per 64-token block of one scan, measured with ncu on a small case of the same
+# kernel (profiles/tc_bwd_chunk_small.md: 189.4 MB over 512 blocks of a K=128, V=64 scan);
+# scaled to a full launch by the blocks it processes.  Other scan shapes move a similar
+# amount (their K x V states and token tiles are at most this size), so this is an estimate.
+TRAFFIC_PER_BLOCK = {"tc_bwd_chunk": 189.4e6 / 512}
 
 
 def peaks():
@@ -300,9 +305,16 @@ def run_b200(args, rank, world, local):
     per_step_ms = {n: round(t / args.steps, 3) for n, (c, t) in prof.items()}
     if top in kf:
         achieved = kf[top] / (tot_ms / args.steps / 1e3) / 1e12
+        traffic = None
+        if top in TRAFFIC_PER_BLOCK:  # scans x units x blocks of the step, per launch
+            nb = -(-LENGTH // CFG["chunk_size"])
+            scans = sum(len(x) for x in gdn_scans(CFG))
+            blocks = scans * units * nb / (n_launch / args.steps)
+            traffic = round(TRAFFIC_PER_BLOCK[top] * blocks)
         roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 5),
-                "traffic": None, "kernel": top, "launches_per_step": n_launch // args.steps,
+                "traffic": traffic, "traffic_source": "ncu small case scaled by blocks",
+                "kernel": top, "launches_per_step": n_launch // args.steps,
                 "avg_launch_ms": round(tot_ms / n_launch, 4),
                 "flops_per_step": kf[top], "peak_source": pk["source"]}
     else:
