@@ -29,7 +29,8 @@ def _inputs(gen, B, T, H, D, Dv, dtype):
     return [x.to(dtype) for x in (q, k, v)]
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2),
+                                       (torch.float16, 2e-2)])
 @pytest.mark.parametrize("prefill", [6, 8])
 def test_decode_steps_match_oracle(dtype, tol, prefill, cpu_threads):
     model = make_model(CFG, seed=3, prefix_std=0.02, perturb=0.1).cuda()

@@ -89,12 +89,15 @@ BF16_CASES = {
 }
 
 
-@pytest.mark.parametrize("name", list(BF16_CASES))
-def test_bf16_forward_backward_matches_reference_semantics(name, cpu_threads):
+@pytest.mark.parametrize("name,dtype", [(n, torch.bfloat16) for n in BF16_CASES] +
+                         [("chunk64_T130", torch.float16)])
+def test_bf16_forward_backward_matches_reference_semantics(name, dtype, cpu_threads):
+    """bf16 activations; fp16 activations run the same bf16-operand tensor-core kernels and
+    are held to the bf16 bar (the alternative criterion uses the bf16 reference's error)."""
     cfg, B, T = BF16_CASES[name]
     model = make_model(cfg, seed=4, prefix_std=.02, perturb=.3)
-    q, k, v = _inputs(cfg, B, T, torch.bfloat16, 4)
-    vs_bf16 = run_pair(model, q, k, v, oracle_dtype=torch.bfloat16)
+    q, k, v = _inputs(cfg, B, T, dtype, 4)
+    vs_bf16 = run_pair(model, q, k, v, oracle_dtype=dtype)
     vs_f64 = run_pair(model, q, k, v, oracle_dtype=torch.float64)
     ref_f64 = _oracle_vs_f64(model, q, k, v, torch.bfloat16)
     bad = {}
