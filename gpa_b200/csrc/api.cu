@@ -309,8 +309,10 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
   const int slots = g.L - 1 > 2 ? g.L - 1 : 2;
   for (int i = 0; i < slots; ++i) {
     s->dWk[i] = b.take(UT * K);
-    s->db[i] = b.take(UT);
-    s->dA[i] = b.take((size_t)g.U * nb * kMaxChunk * kMaxChunk);
+    // per-block dA and db round trips exist only on the SIMT path (the tensor-core backward
+    // chunk kernel keeps them in shared memory)
+    s->db[i] = g.fast ? nullptr : b.take(UT);
+    s->dA[i] = g.fast ? nullptr : b.take((size_t)g.U * nb * kMaxChunk * kMaxChunk);
     s->Dend[i] = b.take((size_t)g.U * nb * K * V);
     s->dK[i] = b.take(UT * K);
     s->dW[i] = b.take(UT * V);

@@ -22,7 +22,6 @@ namespace {
 using tc::Acc;
 using tc::bf16;
 using tc::Carve;
-using tc::copy_f4;
 using tc::for_tiles;
 using tc::ld2;
 using tc::st2;
@@ -38,19 +37,9 @@ using tc::TileJob;
 constexpr int C = kMaxChunk;  // 64 rows per block tile (zero padded)
 constexpr int kThreads = 512;  // 16 warps: global-load latency of the tile loads is the limiter
 
-// block gates with padding: rows >= c keep G = G[c-1] and beta = 0
-GPA_DEV void load_gates_pad(const ScanDesc& d, int u, int t0, int c, float* G, float* bt) {
-  load_gates(d, u, t0, c, G, bt);
-  __syncthreads();
-  for (int t = c + threadIdx.x; t < C; t += blockDim.x) {
-    G[t] = G[c - 1];
-    if (bt) bt[t] = 0.f;
-  }
-}
-
 // Gates of one block in registers of warp 0 (t = lane, lane + 32), fetched before the tile
 // loads so that their latency overlaps them; gate_finish writes the inclusive cumsum G and
-// beta with the padding of load_gates_pad.
+// beta, padded: rows >= c keep G = G[c-1] and beta = 0.
 struct GateRegs {
   float g0, g1, b0, b1;
 };

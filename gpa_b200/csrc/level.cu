@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(256) k_head_outer(int B, int T, int H, const f
                                                     const float* scale, int64_t scale_stride,
                                                     float cscale, float* out) {
   const int h = blockIdx.x;
-  const int tp = (P + kHoTile - 1) / kHoTile, tq = (Q + kHoTile - 1) / kHoTile;
+  const int tq = (Q + kHoTile - 1) / kHoTile;
   const int p0 = (blockIdx.y / tq) * kHoTile, q0 = (blockIdx.y % tq) * kHoTile;
   const int pw = min(kHoTile, P - p0), qw = min(kHoTile, Q - q0);
   const int64_t total = (int64_t)B * T;

@@ -111,104 +111,5 @@ GPA_DEV void edge_weights(const BridgeIn& in, const float* edge_logits, int H, i
   for (int a = 0; a < in.n; ++a) w[a] /= s;
 }
 
-// Dense reader forward of one token row (one warp): base <- softmax(logits + rg *
-// tanh(c / sqrt(mean(c^2) + eps))), c = incoming - mean(incoming),
-// incoming = sum_e w_e msg_e  (src/gpa/attention.py:227-242).
-GPA_DEV void reader_row_fwd(float (&base)[kMaxPerLane], int64_t o, int M, const BridgeIn& in,
-                            const float* w, float rg, const float* logits) {
-  load_vec(base, logits + o * M, M);
-  if (in.n > 0) {
-    const int lane = threadIdx.x & 31;
-    float inc[kMaxPerLane];
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
-    for (int a = 0; a < in.n; ++a) {
-      float x[kMaxPerLane];
-      load_vec(x, in.msg[a] + o * M, M);
-#pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
-    }
-    float mean = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (lane + 32 * i < M) mean += inc[i];
-    mean = warp_sum(mean) / M;
-    float var = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (lane + 32 * i < M) {
-        inc[i] -= mean;
-        var += inc[i] * inc[i];
-      }
-    var = warp_sum(var) / M;
-    const float sd = rsqrtf(var + kCenterEps);
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) base[i] += rg * tanhf(inc[i] * sd);
-  }
-  warp_softmax(base, M);
-}
-
-// Backward of reader_row_fwd: db = d(logits) of the row; writes dmsg rows;
-// accumulates the relation-gain and edge-weight partial sums (lane-uniform).
-GPA_DEV void reader_row_bwd(float (&db)[kMaxPerLane], const float (&r)[kMaxPerLane],
-                            const float (&dr)[kMaxPerLane], int64_t o, int M,
-                            const BridgeIn& in, const float* w, float rg, float& rg_acc,
-                            float (&ew_acc)[kMaxIn]) {
-  const int lane = threadIdx.x & 31;
-  softmax_bwd(db, r, dr, M);
-  if (in.n == 0) return;
-  float inc[kMaxPerLane];
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
-  for (int a = 0; a < in.n; ++a) {
-    float x[kMaxPerLane];
-    load_vec(x, in.msg[a] + o * M, M);
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) inc[i] += w[a] * x[i];
-  }
-  float mean = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < M) mean += inc[i];
-  mean = warp_sum(mean) / M;
-  float var = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if (lane + 32 * i < M) {
-      inc[i] -= mean;
-      var += inc[i] * inc[i];
-    }
-  var = warp_sum(var) / M;
-  const float sd = rsqrtf(var + kCenterEps);
-  float dz[kMaxPerLane], rgp = 0.f, dsum = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    const float tz = tanhf(inc[i] * sd);
-    if (lane + 32 * i < M) rgp += db[i] * tz;
-    dz[i] = rg * db[i] * (1.f - tz * tz);
-    if (lane + 32 * i < M) dsum += dz[i] * inc[i];
-  }
-  rg_acc += warp_sum(rgp);
-  dsum = warp_sum(dsum);
-  const float dvar = dsum * -0.5f * sd * sd * sd;
-  float dmean = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    dz[i] = dz[i] * sd + dvar * 2.f * inc[i] / M;
-    if (lane + 32 * i < M) dmean += dz[i];
-  }
-  dmean = warp_sum(dmean) / M;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) dz[i] -= dmean;
-  for (int a = 0; a < in.n; ++a) {
-    float x[kMaxPerLane], dm[kMaxPerLane];
-    load_vec(x, in.msg[a] + o * M, M);
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) dm[i] = w[a] * dz[i];
-    store_vec(in.dmsg[a] + o * M, dm, M);
-    ew_acc[a] += warp_dot(dz, x, M);
-  }
-}
-
 }  // namespace
 }  // namespace gpa

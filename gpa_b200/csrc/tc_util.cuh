@@ -153,12 +153,6 @@ GPA_DEV void load_tiles(const TileJob (&jobs)[N]) {
   }
 }
 
-// dst[i] = src[i] for n floats (n multiple of 4, 16-byte aligned), float4 copies
-GPA_DEV void copy_f4(float* dst, const float* src, int n) {
-  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
-    *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(src + i);
-}
-
 template <int MI, int NI, class Body>
 GPA_DEV void tiles_n(int M, int N, Body body) {
   // NI chosen at run time: 32-wide tiles when N allows and they still give every warp a
