@@ -422,14 +422,13 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
 GPA_DEV float dscale(const ScanDesc& d, int u) { return d.dO_scale ? d.dO_scale[u] : 1.f; }
 
 struct LBwdLocal {
-  size_t Qs, Ks, Ss, Wh, Wl, dOs, Ph, Pl, dXh, dXl, G, racc, rs, cs, total;
+  size_t Qs, Ks, Ss, Wh, dOs, Ph, Pl, dXh, dXl, G, racc, rs, cs, total;
   __host__ __device__ LBwdLocal(int K, int V) {
     Carve c;
     Qs = c.take(2 * C * ld16(K));
     Ks = c.take(2 * C * ld16(K));
     Ss = c.take(2 * K * ld16(V));
     Wh = c.take(2 * C * ld16(V));
-    Wl = c.take(2 * C * ld16(V));
     dOs = c.take(2 * C * ld16(V));
     Ph = c.take(2 * C * LDT);
     Pl = c.take(2 * C * LDT);
@@ -444,7 +443,7 @@ struct LBwdLocal {
 };
 
 // grid (U*NB, nscan): read-path gradients of O = e^G Q S_n + P W.
-__global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blocks bl) {
+__global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
@@ -456,7 +455,6 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
   bf16* Ks = (bf16*)(smem + L.Ks);
   bf16* Ss = (bf16*)(smem + L.Ss);
   bf16* Wh = (bf16*)(smem + L.Wh);
-  bf16* Wl = (bf16*)(smem + L.Wl);
   bf16* dOs = (bf16*)(smem + L.dOs);
   bf16* Ph = (bf16*)(smem + L.Ph);
   bf16* Pl = (bf16*)(smem + L.Pl);
@@ -473,7 +471,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
         tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
-        tc::job(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C),
+        tc::job(Wh, nullptr, ldv, d.W + row(u, T, t0) * V, V, c, V, C),
         tc::job(dOs, nullptr, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, dscale(d, u))};
     tc::load_tiles(jobs);
     gate_finish(gr, c, G, nullptr);
@@ -489,7 +487,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_local(ScanBatch b, int U, Blo
       tc::split_bf16(v, Ph + t * LDT + s, Pl + t * LDT + s);
     });
     da.zero();
-    tc::mma_acc3<1, 1, false, true>(da, dOs, nullptr, ldv, Wh, Wl, ldv, m0, n0, V);
+    mma_acc<1, 1, false, true>(da, dOs, ldv, Wh, ldv, m0, n0, V);  // dO is bf16 already
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     float rsum[2] = {0.f, 0.f}, csum[2][2] = {};
 #pragma unroll
