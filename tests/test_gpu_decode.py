@@ -29,13 +29,17 @@ def _inputs(gen, B, T, H, D, Dv, dtype):
     return [x.to(dtype) for x in (q, k, v)]
 
 
+# a second shape: three levels with equal outer states and narrower values
+CFG_SPLIT = dict(heads=2, key_dim=32, value_dim=16, slots=(16, 8, 16), chunk_size=4)
+
+
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2),
                                        (torch.float16, 2e-2)])
-@pytest.mark.parametrize("prefill", [6, 8])
-def test_decode_steps_match_oracle(dtype, tol, prefill, cpu_threads):
-    model = make_model(CFG, seed=3, prefix_std=0.02, perturb=0.1).cuda()
+@pytest.mark.parametrize("prefill,cfg", [(6, CFG), (8, CFG), (6, CFG_SPLIT)])
+def test_decode_steps_match_oracle(dtype, tol, prefill, cfg, cpu_threads):
+    model = make_model(cfg, seed=3, prefix_std=0.02, perturb=0.1).cuda()
     gen = torch.Generator().manual_seed(7)
-    B, H, D, Dv = 2, CFG["heads"], CFG["key_dim"], CFG["value_dim"]
+    B, H, D, Dv = 2, cfg["heads"], cfg["key_dim"], cfg["value_dim"]
     pre = _inputs(gen, B, prefill, H, D, Dv, dtype)
     steps = [_inputs(gen, B, 1, H, D, Dv, dtype) for _ in range(9)]
     p = {n: t.detach().cpu().double() for n, t in model.state_dict().items()}
