@@ -353,14 +353,13 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
 }
 
 struct LFwdOut {
-  size_t Qs, Ks, Ss, Wh, Wl, Ph, Pl, G, total;
+  size_t Qs, Ks, Ss, Wh, Ph, Pl, G, total;
   __host__ __device__ LFwdOut(int K, int V) {
     Carve c;
     Qs = c.take(2 * C * ld16(K));
     Ks = c.take(2 * C * ld16(K));
     Ss = c.take(2 * K * ld16(V));
     Wh = c.take(2 * C * ld16(V));
-    Wl = c.take(2 * C * ld16(V));
     Ph = c.take(2 * C * LDT);
     Pl = c.take(2 * C * LDT);
     G = c.take(4 * C);
@@ -382,7 +381,6 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
   bf16* Ks = (bf16*)(smem + L.Ks);
   bf16* Ss = (bf16*)(smem + L.Ss);
   bf16* Wh = (bf16*)(smem + L.Wh);
-  bf16* Wl = (bf16*)(smem + L.Wl);
   bf16* Ph = (bf16*)(smem + L.Ph);
   bf16* Pl = (bf16*)(smem + L.Pl);
   float* G = (float*)(smem + L.G);
@@ -392,7 +390,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
         tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
-        tc::job(Wh, Wl, ldv, d.W + row(u, T, t0) * V, V, c, V, C)};
+        tc::job(Wh, nullptr, ldv, d.W + row(u, T, t0) * V, V, c, V, C)};
     tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, nullptr);
   }
@@ -410,7 +408,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
     acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
-    tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, Wl, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, nullptr, ldv, m0, n0, C);
     acc.each(m0, n0, [&](int t, int col, float& v) {
       if (t < c) d.O[row(u, T, t0 + t) * V + col] = v;
     });
