@@ -641,18 +641,20 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
 // ------------------------------------------------------------- post backward
 
 struct LPostBwd {
-  size_t Af, Bf, Wb, Wf, dWf, dKb, dVb, Nk, dLb, red, total;
+  // Bf is dead once dW is formed: dLb takes its place; Wf and dWf are dead after the
+  // softmax backward rows: Nk is loaded there (the M = 64 layout then fits two CTAs per SM)
+  size_t Af, Bf, dLb, Wb, Wf, dWf, Nk, dKb, dVb, red, total;
   __host__ __device__ LPostBwd(int D, int Dv, int M) {
     Carve c;
     Af = c.take(2 * D * ld16(M));
-    Bf = c.take(2 * M * ld16(Dv));
+    const size_t sb = 2 * M * ld16(Dv), sl = 2 * R * ld16(M);
+    Bf = dLb = c.take(sb > sl ? sb : sl);
     Wb = c.take(2 * R * ld16(M));
-    Wf = c.take(4 * R * M);
-    dWf = c.take(4 * R * M);
+    const size_t sw = 2 * 4 * R * M, sn = 2 * R * ld16(D);
+    Wf = Nk = c.take(sw > sn ? sw : sn);
+    dWf = Wf + 4 * R * M;
     dKb = c.take(2 * R * ld16(D));
     dVb = c.take(2 * R * ld16(Dv));
-    Nk = c.take(2 * R * ld16(D));
-    dLb = c.take(2 * R * ld16(M));
     red = c.take(4 * 34);
     total = c.off;
   }
@@ -686,7 +688,6 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
   tile_to_bf16(Af, lm, frozen_at(Abnd, fz0 ? fzA : nullptr, u, n, bl.nb, post, (int64_t)D * M), M,
                D, M, D);
   tile_to_bf16(Wb, lm, write + row(u, T, t0) * M, M, c, M, R);
-  tile_to_bf16(Nk, ld, nk + row(u, T, t0) * D, D, c, D, R);
   for (int i = 4 * threadIdx.x; i < R * M; i += 4 * blockDim.x) {
     const bool in = i < c * M;  // rows t < c are contiguous from t0
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -749,7 +750,8 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
     softmax_bwd(dx, y, dy, M);
     store_bf16_row(dLb + t * lm, dx, M);
   }
-  __syncthreads();
+  __syncthreads();  // Wf / dWf are dead: the Nk tile goes there
+  tile_to_bf16(Nk, ld, nk + row(u, T, t0) * D, D, c, D, R);
   // dnk = dlw A_f^T
   tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
@@ -759,6 +761,7 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
       if (t < c) dnk[row(u, T, t0 + t) * D + d] = v;
     });
   });
+  __syncthreads();  // Nk
   float* ta = fz0 ? dfzA + (int64_t)u * D * M
                   : extA + ((int64_t)u * (bl.nb + 1) + n + post) * D * M;
   float* tb = fz0 ? dfzB + (int64_t)u * M * Dv
