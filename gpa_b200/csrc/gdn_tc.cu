@@ -703,22 +703,18 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
 }
 
 struct LBwdChunk {
-  // fixed buffers, then Y (dW hi/lo) and a pool X whose contents change by stage:
-  //   state terms: Sb, Db, Wb | U path: Uh, Ul | Wk path: Wkh, Wkl, dWkh, dWkl | final: Mmb
-  size_t Ks, Kl, Th, Tl, A, dAf, Mh, Ml, G, bt, dG, db, dlam, rw, red, dWh, dWl, X, total;
-  size_t Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mmb;
+  // T (hi/lo) and the per-token vectors are fixed; a pool X holds, stage by stage,
+  //   1 state terms: dWh, dWl, Sb, Db, Wb   2 U path: dWh, dWl, Uh, Ul
+  //   3 Wk path: Wkh, Wkl, dWkh, dWkl       4 dA: Mh, Ml, dAf, A, Ks, Kl (then Mmb over Mh)
+  // so that every shape with K, V <= 128 but (128, 128) fits two CTAs per SM.
+  size_t Th, Tl, G, bt, dG, db, dlam, rw, red, X, total;
+  size_t dWh, dWl, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mh, Ml, dAf, A, Ks, Kl, Mmb;
   __host__ __device__ LBwdChunk(int K, int V) {
     Carve c;
     const size_t sK = 2 * C * ld16(K), sV = 2 * C * ld16(V), sS = 2 * K * ld16(V);
     const size_t sA = 4 * C * kAStride, sT = 2 * C * LDT;
-    Ks = c.take(sK);
-    Kl = c.take(sK);
     Th = c.take(sT);
     Tl = c.take(sT);
-    A = c.take(sA);
-    dAf = c.take(sA);
-    Mh = c.take(sT);
-    Ml = c.take(sT);
     G = c.take(4 * C);
     bt = c.take(4 * C);
     dG = c.take(4 * C);
@@ -726,29 +722,43 @@ struct LBwdChunk {
     dlam = c.take(4 * C);
     rw = c.take(4 * C);
     red = c.take(4 * 32);
-    dWh = c.take(sV);
-    dWl = c.take(sV);
-    size_t pool = 2 * sS + sV;
-    pool = pool > 2 * sV ? pool : 2 * sV;
-    pool = pool > 4 * sK ? pool : 4 * sK;
+    Carve s1, s2, s3, s4;
+    dWh = s1.take(sV);
+    dWl = s1.take(sV);
+    Sb = s1.take(sS);
+    Db = s1.take(sS);
+    Wb = s1.take(sV);
+    s2.take(2 * sV);  // dW stays
+    Uh = s2.take(sV);
+    Ul = s2.take(sV);
+    Wkh = s3.take(sK);
+    Wkl = s3.take(sK);
+    dWkh = s3.take(sK);
+    dWkl = s3.take(sK);
+    Mh = s4.take(sT);
+    Ml = s4.take(sT);
+    dAf = s4.take(sA);
+    A = s4.take(sA);
+    Ks = s4.take(sK);
+    Kl = s4.take(sK);
+    size_t pool = s1.off;
+    pool = pool > s2.off ? pool : s2.off;
+    pool = pool > s3.off ? pool : s3.off;
+    pool = pool > s4.off ? pool : s4.off;
     X = c.take(pool);
-    Sb = X;
-    Db = X + sS;
-    Wb = X + 2 * sS;
-    Uh = X;
-    Ul = X + sV;
-    Wkh = X;
-    Wkl = X + sK;
-    dWkh = X + 2 * sK;
-    dWkl = X + 3 * sK;
-    Mmb = X;
+    size_t* const in_pool[] = {&dWh, &dWl, &Sb, &Db, &Wb, &Uh, &Ul, &Wkh, &Wkl,
+                               &dWkh, &dWkl, &Mh, &Ml, &dAf, &A, &Ks, &Kl};
+    for (size_t* q : in_pool) *q += X;
+    Mmb = Mh;
     total = c.off;
   }
 };
 
 // grid (U*NB, nscan): the whole block backward after the state sweep (dW and D known):
 // state-update terms, U path, Wk path, dA consequences, final dK / dg / dbeta.
-// The dA of both paths is formed as -T^T (dW U^T + dWk Wk^T) (strictly lower part).
+// The dA of both paths is formed as -T^T (dW U^T + dWk Wk^T) (strictly lower part); that
+// C x C sum stays in each warp's accumulator tiles across the U and Wk stages.  Launched
+// with 256 threads (two CTAs per SM) or 512.
 __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blocks bl) {
   const ScanDesc& d = b.s[blockIdx.y];
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
@@ -789,44 +799,37 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   const float* dg = d.Dend + ((int64_t)u * bl.nb + n) * KV;
   const int64_t r0 = row(u, T, t0);
 
-  // ---- T = (I + A)^-1 of the block
+  // M = dW U^T + dWk Wk^T: 16 accumulator tiles of 16 x 16, tile w + i nw of each warp
+  constexpr int kMT = 2;  // 8 or 16 warps
+  Acc<1, 1> macc[kMT];
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     dG[t] = t < c ? d.sc_dG[r0 + t] : 0.f;
     db[t] = dlam[t] = rw[t] = 0.f;
   }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
-  {  // K, gates, and A, T of the block as the forward formed them
+  {  // gates, T of the block as the forward formed it, and the state-term operands
     const GateRegs gr = gate_fetch(d, u, t0, c, true);
-    const float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
-    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C),
-                            tc::job(Th, Tl, LDT, d.Tsv + ((int64_t)u * bl.nb + n) * C * C, C, C, C, C)};
+    const TileJob jobs[] = {tc::job(Th, Tl, LDT, d.Tsv + ((int64_t)u * bl.nb + n) * C * C, C, C, C, C),
+                            tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C),
+                            tc::job(Sb, nullptr, ldv, sg, V, K, V, K),
+                            tc::job(Db, nullptr, ldv, dg, V, K, V, K),
+                            tc::job(Wb, nullptr, ldv, d.W + r0 * V, V, c, V, C)};
     tc::load_tiles(jobs);
-    for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
-      const float4 a = *reinterpret_cast<const float4*>(As + 4 * i);
-      float* dst = A + (4 * i / C) * kAStride + (4 * i) % C;
-      dst[0] = a.x;
-      dst[1] = a.y;
-      dst[2] = a.z;
-      dst[3] = a.w;
-    }
     gate_finish(gr, c, G, bt);
   }
+  __syncthreads();
 
   // ---- state-update terms: WD = W D^T, <D, S>, dWk = -dW S^T
-  {
-    const TileJob jobs[] = {tc::job(Sb, nullptr, ldv, sg, V, K, V, K),
-                            tc::job(Db, nullptr, ldv, dg, V, K, V, K),
-                            tc::job(Wb, nullptr, ldv, d.W + r0 * V, V, c, V, C),
-                            tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C)};
-    tc::load_tiles(jobs);
-  }
-  __syncthreads();
   // sc_dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
-    float2 dk[Acc<1, NI>::kPairs];
+    float2 dk[Acc<1, NI>::kPairs], kk[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-      if (t < c) dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
+      kk[p] = make_float2(0.f, 0.f);
+      if (t < c) {
+        dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
+        kk[p] = ld2(d.k + (r0 + t) * K + col);
+      }
     });
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Wb, ldv, Db, ldv, m0, n0, V);
@@ -836,8 +839,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
         const float lm = __expf(G[c - 1] - G[t]);
         st2(d.sc_dK + (r0 + t) * K + col, dk[p].x + lm * v0, dk[p].y + lm * v1);
       }
-      part[(t - m0) >> 3 & 1] += v0 * __bfloat162float(Ks[t * ldk + col]) +
-                                 v1 * __bfloat162float(Ks[t * ldk + col + 1]);
+      part[(t - m0) >> 3 & 1] += v0 * kk[p].x + v1 * kk[p].y;
     });
     const int g = lane >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
@@ -903,12 +905,14 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       atomicAdd(&db[m0 + g + 8], p1);
     }
   });
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
-    Acc<1, 1> acc;
-    acc.zero();
-    tc::mma_acc3<1, 1, false, true>(acc, dWh, dWl, ldv, Uh, Ul, ldv, m0, n0, V);
-    acc.each(m0, n0, [&](int t, int s, float& v) { dAf[t * kAStride + s] = v; });
-  });
+#pragma unroll
+  for (int i = 0; i < kMT; ++i) {
+    const int tl = w + i * nw;
+    macc[i].zero();
+    if (tl < 16)
+      tc::mma_acc3<1, 1, false, true>(macc[i], dWh, dWl, ldv, Uh, Ul, ldv, 16 * (tl >> 2),
+                                      16 * (tl & 3), V);
+  }
   __syncthreads();
 
   // ---- Wk path: dRw = T^T dWk ; sc_dK += b e^G dRw ; rw = rowsum(dRw o K) ; M += dWk Wk^T
@@ -920,9 +924,13 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   __syncthreads();
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
-    float2 dk[Acc<1, NI>::kPairs];
+    float2 dk[Acc<1, NI>::kPairs], kk[Acc<1, NI>::kPairs];
     acc.each2(m0, n0, [&](int p, int t, int col, float&, float&) {
-      if (t < c) dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
+      kk[p] = make_float2(0.f, 0.f);
+      if (t < c) {
+        dk[p] = ld2(d.sc_dK + (r0 + t) * K + col);
+        kk[p] = ld2(d.k + (r0 + t) * K + col);
+      }
     });
     acc.zero();
     tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWkh, dWkl, ldk, m0, n0, C);
@@ -932,9 +940,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
         const float be = bt[t] * __expf(G[t]);
         st2(d.sc_dK + (r0 + t) * K + col, dk[p].x + be * v0, dk[p].y + be * v1);
       }
-      const int o = t * ldk + col;
-      part[(t - m0) >> 3 & 1] += v0 * (__bfloat162float(Ks[o]) + __bfloat162float(Kl[o])) +
-                                 v1 * (__bfloat162float(Ks[o + 1]) + __bfloat162float(Kl[o + 1]));
+      part[(t - m0) >> 3 & 1] += v0 * kk[p].x + v1 * kk[p].y;
     });
     const int g = lane >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
@@ -943,20 +949,41 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       atomicAdd(&rw[m0 + g + 8], p1);
     }
   });
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
-    Acc<1, 1> acc;
-    acc.each(m0, n0, [&](int t, int s, float& v) { v = dAf[t * kAStride + s]; });
-    tc::mma_acc3<1, 1, false, true>(acc, dWkh, dWkl, ldk, Wkh, Wkl, ldk, m0, n0, K);
-    acc.each(m0, n0, [&](int t, int s, float& v) {
-      tc::split_bf16(v, Mh + t * LDT + s, Ml + t * LDT + s);
-    });
-  });
-  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kMT; ++i) {
+    const int tl = w + i * nw;
+    if (tl < 16)
+      tc::mma_acc3<1, 1, false, true>(macc[i], dWkh, dWkl, ldk, Wkh, Wkl, ldk, 16 * (tl >> 2),
+                                      16 * (tl & 3), K);
+  }
+  __syncthreads();  // Wk, dWk are dead: M, A and K of the block go into the pool
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     const float e = __expf(G[t]);
     db[t] += e * rw[t];
     dG[t] += bt[t] * e * rw[t];
   }
+  {
+    const float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
+    const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C)};
+    tc::load_tiles(jobs);
+    for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
+      const float4 a = *reinterpret_cast<const float4*>(As + 4 * i);
+      float* dst = A + (4 * i / C) * kAStride + (4 * i) % C;
+      dst[0] = a.x;
+      dst[1] = a.y;
+      dst[2] = a.z;
+      dst[3] = a.w;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kMT; ++i) {
+    const int tl = w + i * nw;
+    if (tl < 16)
+      macc[i].each(16 * (tl >> 2), 16 * (tl & 3), [&](int t, int s, float& v) {
+        tc::split_bf16(v, Mh + t * LDT + s, Ml + t * LDT + s);
+      });
+  }
+  __syncthreads();
   // dA = -T^T M, strictly lower
   for_tiles<1, 1>(C, C, [&](int m0, int n0) {
     Acc<1, 1> acc;
@@ -1056,9 +1083,11 @@ cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStre
 // Launch one kernel per group of scans with the same (K, V): each group gets the shared
 // memory its own shape needs, so narrow scans fit more CTAs per SM.
 // gx: CTAs per scan along x; with `sliced`, times the state slices of the group's shape.
+// With `halve`, a group whose layout fits two CTAs per SM (113 KB) runs 256 threads per CTA.
 template <class Lay, class Kern>
 cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& b, int U,
-                             const Blocks& bl, cudaStream_t st, bool sliced = false) {
+                             const Blocks& bl, cudaStream_t st, bool sliced = false,
+                             bool halve = false) {
   bool done[kMaxScans] = {};
   for (int i = 0; i < b.n; ++i) {
     if (done[i]) continue;
@@ -1072,8 +1101,10 @@ cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& 
       }
     const int K = b.s[i].K, V = b.s[i].V;
     const int x = sliced ? gx * state_slices(K, V) : gx;
-    const cudaError_t e = tc_launch(name, k, dim3(x, sub.n), Lay(K, V).total, st, sub, U, bl,
-                                    sliced ? kStateThreads : kThreads);
+    const size_t smem = Lay(K, V).total;
+    const int threads =
+        sliced ? kStateThreads : (halve && smem <= 113 * 1024 ? kThreads / 2 : kThreads);
+    const cudaError_t e = tc_launch(name, k, dim3(x, sub.n), smem, st, sub, U, bl, threads);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -1106,7 +1137,8 @@ cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaS
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
   cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess) return e;
-  return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st);
+  return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st,
+                                     false, true);
 }
 
 }  // namespace gpa
