@@ -41,11 +41,11 @@ METRIC = "DenseGPA fwd+bwd tokens/s at 1/2/4/8 B200 (T=8192) + % of roofline"
 CFG = dict(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
 BATCH, LENGTH = 8, 8192
 CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
-# DRAM bytes per 64-token block of one scan, measured with ncu on a small case of the same
-# kernel (profiles/tc_bwd_chunk_small.md: 189.4 MB over 512 blocks of a K=128, V=64 scan);
-# scaled to a full launch by the blocks it processes.  Other scan shapes move a similar
-# amount (their K x V states and token tiles are at most this size), so this is an estimate.
-TRAFFIC_PER_BLOCK = {"tc_bwd_chunk": 189.4e6 / 512}
+# DRAM bytes moved per algorithmic byte, measured with ncu on a small case of the same kernel
+# (profiles/tc_bwd_chunk_small.md: 254.9 MB over 1024 blocks of (K, V) = (64, 64) scans and
+# 189.9 MB over 512 blocks of (128, 64), against 247.0 and 361.7 KB of algorithmic bytes per
+# block); the traffic of a full launch is its algorithmic bytes times this ratio.
+TRAFFIC_RATIO = {"tc_bwd_chunk": 1.02}
 
 
 def peaks():
@@ -129,6 +129,22 @@ def kernel_flops(cfg, units, length):
     out["tc_fwd_chunk"] = out["gdn_fwd_chunk"] // 2
     out["tc_bwd_chunk"] = out["gdn_bwd_chunk_v"] + out["gdn_bwd_chunk_k"]
     return out
+
+
+def kernel_bytes(cfg, units, length):
+    """Algorithmic HBM bytes per training step of the kernels whose bound is memory.
+
+    tc_bwd_chunk, per block of c tokens of a (K, V) scan, fp32: reads k, Wk, the dk partial
+    and the accumulated dk (c K each), W, dW, U, v and the accumulated dv (c V each), the
+    state snapshot S and its gradient D (K V each), A and T (c^2 each), and the gates and
+    the dG partial (3 c); writes dk (c K), dv (c V), dg and dbeta (2 c).
+    """
+    c = cfg["chunk_size"]
+    nb = -(-length // c)
+    inner, outer, rel = gdn_scans(cfg)
+    per = sum(4 * (2 * K * V + 2 * c * c + 5 * c * K + 6 * c * V + 5 * c)
+              for K, V in inner + outer + rel)
+    return {"tc_bwd_chunk": units * nb * per}
 
 
 # ------------------------------------------------------------------ clocks
@@ -316,24 +332,35 @@ def run_b200(args, rank, world, local):
     pk = peaks()
     units = BATCH * CFG["heads"]
     kf = kernel_flops(CFG, units, LENGTH)
+    kb = kernel_bytes(CFG, units, LENGTH)
     # dominant kernel by device time
     top = max(prof, key=lambda n: prof[n][1])
     n_launch, tot_ms = prof[top]
     per_step_ms = {n: round(t / args.steps, 3) for n, (c, t) in prof.items()}
     if top in kf:
-        achieved = kf[top] / (tot_ms / args.steps / 1e3) / 1e12
+        # the bound is whichever of the algorithmic FLOPs and bytes needs more time at peak
+        step_s = tot_ms / args.steps / 1e3
+        lps = n_launch / args.steps
+        t_flop = kf[top] / (pk["bf16_tflops"] * 1e12)
+        t_byte = kb.get(top, 0) / (pk["hbm_gbs"] * 1e9)
         traffic = None
-        if top in TRAFFIC_PER_BLOCK:  # scans x units x blocks of the step, per launch
-            nb = -(-LENGTH // CFG["chunk_size"])
-            scans = sum(len(x) for x in gdn_scans(CFG))
-            blocks = scans * units * nb / (n_launch / args.steps)
-            traffic = round(TRAFFIC_PER_BLOCK[top] * blocks)
-        roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": pk["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 5),
-                "traffic": traffic, "traffic_source": "ncu small case scaled by blocks",
-                "kernel": top, "launches_per_step": n_launch // args.steps,
-                "avg_launch_ms": round(tot_ms / n_launch, 4),
-                "flops_per_step": kf[top], "peak_source": pk["source"]}
+        if top in TRAFFIC_RATIO:
+            traffic = round(kb[top] / lps * TRAFFIC_RATIO[top])
+        if t_byte >= t_flop:
+            achieved = kb[top] / step_s / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4)}
+        else:
+            achieved = kf[top] / step_s / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": pk["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 5)}
+        roof.update({"traffic": traffic,
+                     "traffic_source": "algorithmic bytes x DRAM/algorithmic ratio of an ncu small case",
+                     "kernel": top, "launches_per_step": round(lps),
+                     "avg_launch_ms": round(tot_ms / n_launch, 4),
+                     "bytes_per_step": kb.get(top), "flops_per_step": kf[top],
+                     "tensor_frac": round(kf[top] / step_s / 1e12 / pk["bf16_tflops"], 5),
+                     "peak_source": pk["source"]})
     else:
         roof = {"bound": "tensor", "achieved": None, "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": None, "traffic": None, "kernel": top,
