@@ -257,7 +257,8 @@ struct LFwdState {
   __host__ __device__ LFwdState(int K, int V) {
     const int VS = state_slice(K, V);
     Carve c;
-    Sf = c.take(4 * K * VS);
+    Sf = c.take(4 * K * (VS + 8));  // padded rows: the accumulator-layout float2 accesses
+                                    // of a half-warp hit 16 distinct bank pairs
     Sb = c.take(2 * K * ld16(VS));
     Wkh = c.take(2 * C * ld16(K));
     Wkl = c.take(2 * C * ld16(K));
@@ -282,6 +283,7 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
   extern __shared__ __align__(16) unsigned char smem[];
   const LFwdState L(K, V);
   float* Sf = (float*)(smem + L.Sf);
+  const int lsf = VS + 8;
   bf16* Sb = (bf16*)(smem + L.Sb);
   bf16* Wkh = (bf16*)(smem + L.Wkh);
   bf16* Wkl = (bf16*)(smem + L.Wkl);
@@ -297,13 +299,13 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
     for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
       const int k = i / q4, j = (i - k * q4) << 2;
       *reinterpret_cast<float4*>(dst + (int64_t)k * V + v0 + j) =
-          *reinterpret_cast<const float4*>(Sf + k * VS + j);
+          *reinterpret_cast<const float4*>(Sf + k * lsf + j);
     }
   };
   for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
     const int k = i / q4, j = (i - k * q4) << 2;
     const float4 x = *reinterpret_cast<const float4*>(d.S0 + u * KV + (int64_t)k * V + v0 + j);
-    *reinterpret_cast<float4*>(Sf + k * VS + j) = x;
+    *reinterpret_cast<float4*>(Sf + k * lsf + j) = x;
     tc::put4(Sb, nullptr, k * lds + j, x);
   }
   __syncthreads();
@@ -330,8 +332,7 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
       acc.each2(m0, n0, [&](int p, int t, int col, float& x0, float& x1) {
         const float w0 = t < c ? ub[p].x - x0 : 0.f, w1 = t < c ? ub[p].y - x1 : 0.f;
         if (t < c) st2(d.W + row(u, T, t0 + t) * V + v0 + col, w0, w1);
-        tc::split_bf16(w0 * lam[t], Wch + t * lds + col, Wcl + t * lds + col);
-        tc::split_bf16(w1 * lam[t], Wch + t * lds + col + 1, Wcl + t * lds + col + 1);
+        tc::split2(w0 * lam[t], w1 * lam[t], Wch + t * lds + col, Wcl + t * lds + col);
       });
     });
     __syncthreads();
@@ -339,11 +340,15 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
     // S = e^{G_c} S + K^T diag(lambda) W
     tiles_spread(K, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
-      acc.each(m0, n0, [&](int k, int col, float& x) { x = gc * Sf[k * VS + col]; });
+      acc.each2(m0, n0, [&](int, int k, int col, float& x0, float& x1) {
+        const float2 sv = *reinterpret_cast<const float2*>(Sf + k * lsf + col);
+        x0 = gc * sv.x;
+        x1 = gc * sv.y;
+      });
       tc::mma_acc3<1, NI, true, false>(acc, Ks, Kl, ldk, Wch, Wcl, lds, m0, n0, C);
-      acc.each(m0, n0, [&](int k, int col, float& x) {
-        Sf[k * VS + col] = x;
-        Sb[k * lds + col] = __float2bfloat16(x);
+      acc.each2(m0, n0, [&](int, int k, int col, float& x0, float& x1) {
+        *reinterpret_cast<float2*>(Sf + k * lsf + col) = make_float2(x0, x1);
+        *reinterpret_cast<__nv_bfloat162*>(Sb + k * lds + col) = __floats2bfloat162_rn(x0, x1);
       });
     });
     __syncthreads();
@@ -674,8 +679,7 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
         const float w0 = t < c ? dw[p].x + lam[t] * x0 : 0.f;
         const float w1 = t < c ? dw[p].y + lam[t] * x1 : 0.f;
         if (t < c) st2(d.sc_dW + row(u, T, t0 + t) * V + v0 + col, w0, w1);
-        tc::split_bf16(w0, dWh + t * lds + col, dWl + t * lds + col);
-        tc::split_bf16(w1, dWh + t * lds + col + 1, dWl + t * lds + col + 1);
+        tc::split2(w0, w1, dWh + t * lds + col, dWl + t * lds + col);
       });
     });
     __syncthreads();
@@ -684,17 +688,19 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
     // D <- e^{G_c} D + (e^G Q)^T dO - Wk^T dW + ext_n
     tiles_spread(K, VS, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
-      acc.each(m0, n0, [&](int k, int col, float& x) {
+      acc.each2(m0, n0, [&](int, int k, int col, float& x0, float& x1) {
         const int o = k * lds + col;
-        x = gc * (__bfloat162float(Dh[o]) + __bfloat162float(Dl[o])) +
-            (ext ? ext[(int64_t)k * V + col] : 0.f);
+        const float2 h = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Dh + o));
+        const float2 l = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Dl + o));
+        const float2 e = ext ? ld2(ext + (int64_t)k * V + col) : make_float2(0.f, 0.f);
+        x0 = gc * (h.x + l.x) + e.x;
+        x1 = gc * (h.y + l.y) + e.y;
       });
       mma_acc<1, NI, true, false>(acc, Qg, ldk, dOs, lds, m0, n0, C);
       tc::mma_acc3<1, NI, true, false>(acc, Wknh, Wknl, ldk, dWh, dWl, lds, m0, n0, C);
       __syncwarp();
-      acc.each(m0, n0, [&](int k, int col, float& x) {
-        const int o = k * lds + col;
-        tc::split_bf16(x, Dh + o, Dl + o);
+      acc.each2(m0, n0, [&](int, int k, int col, float& x0, float& x1) {
+        tc::split2(x0, x1, Dh + k * lds + col, Dl + k * lds + col);
       });
     });
     __syncthreads();

@@ -179,6 +179,14 @@ GPA_DEV void split_bf16(float x, bf16* hi, bf16* lo) {
   *lo = __float2bfloat16(x - __bfloat162float(h));
 }
 
+// hi / lo bf16 pairs of two adjacent fp32 values (hi, lo 4-byte aligned)
+GPA_DEV void split2(float a, float b, bf16* hi, bf16* lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 f = __bfloat1622float2(h);
+  *reinterpret_cast<__nv_bfloat162*>(hi) = h;
+  *reinterpret_cast<__nv_bfloat162*>(lo) = __floats2bfloat162_rn(a - f.x, b - f.y);
+}
+
 // Round-robin the (16MI x 16NI) tiles of an M x N output over the block's warps.
 template <int MI, int NI, class Body>
 GPA_DEV void for_tiles(int M, int N, Body body) {
