@@ -198,9 +198,10 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
   float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) Ts[i] = Tm[(i / C) * kAStride + (i % C)];
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    tc::split_bf16(Tm[t * kAStride + s] * bt[s], Fh + t * LDT + s, Fl + t * LDT + s);
+  for (int i = threadIdx.x; i < C * C / 2; i += blockDim.x) {
+    const int t = 2 * i / C, s = 2 * i - t * C;
+    tc::split2(Tm[t * kAStride + s] * bt[s], Tm[t * kAStride + s + 1] * bt[s + 1],
+               Fh + t * LDT + s, Fl + t * LDT + s);
   }
   __syncthreads();
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
@@ -212,10 +213,11 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
     });
   });
   __syncthreads();
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    tc::split_bf16(Tm[t * kAStride + s] * bt[s] * __expf(G[s]), Fh + t * LDT + s,
-                   Fl + t * LDT + s);
+  for (int i = threadIdx.x; i < C * C / 2; i += blockDim.x) {
+    const int t = 2 * i / C, s = 2 * i - t * C;
+    tc::split2(Tm[t * kAStride + s] * bt[s] * __expf(G[s]),
+               Tm[t * kAStride + s + 1] * bt[s + 1] * __expf(G[s + 1]), Fh + t * LDT + s,
+               Fl + t * LDT + s);
   }
   __syncthreads();
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
@@ -403,8 +405,10 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     Acc<1, 1> acc;
     acc.zero();
     mma_acc<1, 1, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
-    acc.each(m0, n0, [&](int t, int s, float& v) {
-      tc::split_bf16(s <= t ? __expf(G[t] - G[s]) * v : 0.f, Ph + t * LDT + s, Pl + t * LDT + s);
+    acc.each2(m0, n0, [&](int, int t, int s, float& v0, float& v1) {
+      tc::split2(s <= t ? __expf(G[t] - G[s]) * v0 : 0.f,
+                 s + 1 <= t ? __expf(G[t] - G[s + 1]) * v1 : 0.f, Ph + t * LDT + s,
+                 Pl + t * LDT + s);
     });
   });
   __syncthreads();
@@ -485,9 +489,10 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
     Acc<1, 1> pa, da;
     pa.zero();
     mma_acc<1, 1, false, true>(pa, Qs, ldk, Ks, ldk, m0, n0, K);
-    pa.each(m0, n0, [&](int t, int s, float& v) {
-      v = s <= t ? __expf(G[t] - G[s]) * v : 0.f;
-      tc::split_bf16(v, Ph + t * LDT + s, Pl + t * LDT + s);
+    pa.each2(m0, n0, [&](int, int t, int s, float& v0, float& v1) {
+      v0 = s <= t ? __expf(G[t] - G[s]) * v0 : 0.f;
+      v1 = s + 1 <= t ? __expf(G[t] - G[s + 1]) * v1 : 0.f;
+      tc::split2(v0, v1, Ph + t * LDT + s, Pl + t * LDT + s);
     });
     da.zero();
     mma_acc<1, 1, false, true>(da, dOs, ldv, Wh, ldv, m0, n0, V);  // dO is bf16 already
@@ -496,13 +501,18 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int t = m0 + g + 8 * (r >> 1), s = n0 + 8 * j + 2 * q + (r & 1);
-        const float dp = s <= t ? da.v[0][j][r] : 0.f;
-        const float pr = pa.v[0][j][r] * dp;
-        rsum[r >> 1] += pr;
-        csum[j][r & 1] += pr;
-        tc::split_bf16(s <= t ? dp * __expf(G[t] - G[s]) : 0.f, dXh + t * LDT + s, dXl + t * LDT + s);
+      for (int h = 0; h < 2; ++h) {
+        const int t = m0 + g + 8 * h, s = n0 + 8 * j + 2 * q;
+        float x[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float dp = s + e <= t ? da.v[0][j][2 * h + e] : 0.f;
+          const float pr = pa.v[0][j][2 * h + e] * dp;
+          rsum[h] += pr;
+          csum[j][e] += pr;
+          x[e] = s + e <= t ? dp * __expf(G[t] - G[s + e]) : 0.f;
+        }
+        tc::split2(x[0], x[1], dXh + t * LDT + s, dXl + t * LDT + s);
       }
     const float r0s = quad_sum(rsum[0]), r1s = quad_sum(rsum[1]);
     if (q == 0) {
@@ -985,8 +995,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   for (int i = 0; i < kMT; ++i) {
     const int tl = w + i * nw;
     if (tl < 16)
-      macc[i].each(16 * (tl >> 2), 16 * (tl & 3), [&](int t, int s, float& v) {
-        tc::split_bf16(v, Mh + t * LDT + s, Ml + t * LDT + s);
+      macc[i].each2(16 * (tl >> 2), 16 * (tl & 3), [&](int, int t, int s, float& v0, float& v1) {
+        tc::split2(v0, v1, Mh + t * LDT + s, Ml + t * LDT + s);
       });
   }
   __syncthreads();

@@ -577,8 +577,7 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
         x1 = mg * v1 * gelu_grad(hv[p].y);
         tc::st2(dhp_out + row(u, T, t0 + t) * 2 * M + rr, x0, x1);
       }
-      tc::split_bf16(x0, Hb + t * lh + rr, Hl + t * lh + rr);
-      tc::split_bf16(x1, Hb + t * lh + rr + 1, Hl + t * lh + rr + 1);
+      tc::split2(x0, x1, Hb + t * lh + rr, Hl + t * lh + rr);
     });
   });
   __syncthreads();

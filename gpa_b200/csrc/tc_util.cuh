@@ -25,14 +25,21 @@ struct Carve {
 // per thread.  With `lo`, the tile is stored as a hi/lo pair.
 constexpr int kLoadIlp = 4;
 
+// four values -> one 8-byte store per tile (o a multiple of 4: tiles are 8-byte aligned)
 GPA_DEV void put4(bf16* hi, bf16* lo, int o, float4 v) {
-  __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
-  *reinterpret_cast<__nv_bfloat162*>(hi + o) = h01;
-  *reinterpret_cast<__nv_bfloat162*>(hi + o + 2) = h23;
+  union Pack {
+    __nv_bfloat162 h[2];
+    uint2 u;
+  };
+  Pack ph, pl;
+  ph.h[0] = __floats2bfloat162_rn(v.x, v.y);
+  ph.h[1] = __floats2bfloat162_rn(v.z, v.w);
+  *reinterpret_cast<uint2*>(hi + o) = ph.u;
   if (lo) {
-    const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
-    *reinterpret_cast<__nv_bfloat162*>(lo + o) = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
-    *reinterpret_cast<__nv_bfloat162*>(lo + o + 2) = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+    const float2 f01 = __bfloat1622float2(ph.h[0]), f23 = __bfloat1622float2(ph.h[1]);
+    pl.h[0] = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+    pl.h[1] = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+    *reinterpret_cast<uint2*>(lo + o) = pl.u;
   }
 }
 
