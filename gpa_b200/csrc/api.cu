@@ -198,9 +198,10 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
     s->raw4[j] = b.take(UT * 4);
     s->gates[j] = b.take(UT * 4);
     s->Abnd[j] = b.take((size_t)g.U * nb1 * g.D * M);
-    s->WA[j] = b.take(UT * M);
+    const size_t wsz = g.fast ? (UT + 1) / 2 : UT;  // W is bf16 on the tensor-core path
+    s->WA[j] = b.take(wsz * M);
     s->Bbnd[j] = b.take((size_t)g.U * nb1 * M * g.Dv);
-    s->WB[j] = b.take(UT * g.Dv);
+    s->WB[j] = b.take(wsz * g.Dv);
     s->raw[j] = b.take(UT * M);
     s->write[j] = b.take(UT * M);
     s->counts[j] = b.take(UT * M);
@@ -221,7 +222,7 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
   for (int e = 0; e < g.E; ++e) {
     const size_t Mi = g.M[g.es[e]], Mj = g.M[g.ed[e]];
     s->Rbnd[e] = b.take((size_t)g.U * nb1 * Mi * Mj);
-    s->WR[e] = b.take(UT * Mj);
+    s->WR[e] = b.take((g.fast ? (UT + 1) / 2 : UT) * Mj);
     s->msg[e] = b.take(UT * Mj);
   }
   s->ge = b.take((size_t)g.E * g.U);
@@ -795,10 +796,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
                        x.dslot, x.d4, x.dkey, st));
     CK(head_outer(g, g.B, T, H, x.dslot, M, 0, s.key[j], D, nullptr, 0, 1.f, gp->center[j],
                          st));
-    CK(head_outer(g, g.B, T, H, s.nk[j], D, 0, x.d4, 4, nullptr, 0, 1.f, gp->gate_weight[j],
-                         st));
-    CK(head_outer(g, g.B, T, H, nullptr, 1, 2, x.d4, 4, nullptr, 0, 1.f, gp->gate_bias[j],
-                         st));
+    CK(launch_gate_grad(g.B, T, H, s.nk[j], D, x.d4, gp->gate_weight[j], gp->gate_bias[j], st));
   }
   CK(launch_input_bwd(g.B, T, H, D, Dv, g.dt, s.qh, s.qn, x.dqh, x.dq_direct, x.dkey, x.dval, dq,
                       dk, dv, st));

@@ -42,7 +42,8 @@ struct ScanDesc {
   int64_t g_su, g_st;
   const float* S0;    // [U,K,V] initial state
   float* Sb;          // [U,NB+1,K,V] block-boundary states
-  float* W;           // [U,T,V] pseudo-values
+  float* W;           // [U,T,V] pseudo-values: fp32 (SIMT path) or bf16 (tensor-core path,
+                      // whose every consumer reads W as single bf16 operands)
   float* Ub;          // [U,T,V] T diag(b) V (may alias W in the forward)
   float* Wk;          // [U,T,K] T diag(b e^G) K
   float* O;           // [U,T,V] output (null: none)

@@ -333,7 +333,9 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_fwd_state(ScanBatch b, in
       tc::mma_acc3<1, NI, false, false>(acc, Wkh, Wkl, ldk, Sb, nullptr, lds, m0, n0, K);
       acc.each2(m0, n0, [&](int p, int t, int col, float& x0, float& x1) {
         const float w0 = t < c ? ub[p].x - x0 : 0.f, w1 = t < c ? ub[p].y - x1 : 0.f;
-        if (t < c) st2(d.W + row(u, T, t0 + t) * V + v0 + col, w0, w1);
+        if (t < c)
+          *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<bf16*>(d.W) + row(u, T, t0 + t) * V +
+                                             v0 + col) = __floats2bfloat162_rn(w0, w1);
         tc::split2(w0 * lam[t], w1 * lam[t], Wch + t * lds + col, Wcl + t * lds + col);
       });
     });
@@ -396,8 +398,8 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     const TileJob jobs[] = {
         tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
-        tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
-        tc::job(Wh, nullptr, ldv, d.W + row(u, T, t0) * V, V, c, V, C)};
+        tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K)};
+    tc::copy_bf16_tile(Wh, ldv, reinterpret_cast<const bf16*>(d.W) + row(u, T, t0) * V, V, c, V, C);
     tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, nullptr);
   }
@@ -478,8 +480,8 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
         tc::job(Qs, nullptr, ldk, d.q + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ks, nullptr, ldk, d.k + row(u, T, t0) * K, K, c, K, C),
         tc::job(Ss, nullptr, ldv, d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV, V, K, V, K),
-        tc::job(Wh, nullptr, ldv, d.W + row(u, T, t0) * V, V, c, V, C),
         tc::job(dOs, nullptr, ldv, d.dO + row(u, T, t0) * V, V, c, V, C, dscale(d, u))};
+    tc::copy_bf16_tile(Wh, ldv, reinterpret_cast<const bf16*>(d.W) + row(u, T, t0) * V, V, c, V, C);
     tc::load_tiles(jobs);
     gate_finish(gr, c, G, nullptr);
   }
@@ -721,7 +723,7 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
 struct LBwdChunk {
   // T (hi/lo) and the per-token vectors are fixed; a pool X holds, stage by stage,
   //   1 state terms: dWh, dWl, Sb, Db, Wb   2 U path: dWh, dWl, Uh, Ul
-  //   3 Wk path: Wkh, Wkl, dWkh, dWkl       4 dA: Mh, Ml, dAf, A, Ks, Kl (then Mmb over Mh)
+  //   3 Wk path: Wkh, Wkl, dWkh, dWkl       4 dA: Mh, Ml, Mmb, A, Ks, Kl
   // so that every shape with K, V <= 128 but (128, 128) fits two CTAs per SM.
   size_t Th, Tl, G, bt, dG, db, dlam, rw, red, X, total;
   size_t dWh, dWl, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mh, Ml, dAf, A, Ks, Kl, Mmb;
@@ -765,7 +767,7 @@ struct LBwdChunk {
     size_t* const in_pool[] = {&dWh, &dWl, &Sb, &Db, &Wb, &Uh, &Ul, &Wkh, &Wkl,
                                &dWkh, &dWkl, &Mh, &Ml, &dAf, &A, &Ks, &Kl};
     for (size_t* q : in_pool) *q += X;
-    Mmb = Mh;
+    Mmb = dAf;  // the dA epilogue writes Mm while other warps still read Mh, Ml
     total = c.off;
   }
 };
@@ -789,7 +791,6 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   bf16* Th = (bf16*)(smem + L.Th);
   bf16* Tl = (bf16*)(smem + L.Tl);
   float* A = (float*)(smem + L.A);
-  float* dAf = (float*)(smem + L.dAf);
   bf16* Mh = (bf16*)(smem + L.Mh);
   bf16* Ml = (bf16*)(smem + L.Ml);
   float* G = (float*)(smem + L.G);
@@ -828,8 +829,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     const TileJob jobs[] = {tc::job(Th, Tl, LDT, d.Tsv + ((int64_t)u * bl.nb + n) * C * C, C, C, C, C),
                             tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C),
                             tc::job(Sb, nullptr, ldv, sg, V, K, V, K),
-                            tc::job(Db, nullptr, ldv, dg, V, K, V, K),
-                            tc::job(Wb, nullptr, ldv, d.W + r0 * V, V, c, V, C)};
+                            tc::job(Db, nullptr, ldv, dg, V, K, V, K)};
+    tc::copy_bf16_tile(Wb, ldv, reinterpret_cast<const bf16*>(d.W) + r0 * V, V, c, V, C);
     tc::load_tiles(jobs);
     gate_finish(gr, c, G, bt);
   }
@@ -977,6 +978,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     const float e = __expf(G[t]);
     db[t] += e * rw[t];
     dG[t] += bt[t] * e * rw[t];
+    rw[t] = dlam[t] = 0.f;  // reused below for the row / column sums of dA o A
   }
   {
     const float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
@@ -1000,36 +1002,48 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       });
   }
   __syncthreads();
-  // dA = -T^T M, strictly lower
+  // dA = -T^T M (strictly lower, real rows), straight from the accumulators: the row and
+  // column sums of dA o A (into rw, dlam) and Mm = dA o b_t e^{G_t - G_s} (bf16, into Mmb)
+  float* rsum = rw;
+  float* csum = dlam;
   for_tiles<1, 1>(C, C, [&](int m0, int n0) {
     Acc<1, 1> acc;
     acc.zero();
     tc::mma_acc3<1, 1, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
-    acc.each(m0, n0, [&](int t, int s, float& v) {
-      dAf[t * kAStride + s] = (s < t && t < c) ? -v : 0.f;
+    float rp[2] = {0.f, 0.f}, cp[2][2] = {};
+    acc.each2(m0, n0, [&](int p, int t, int s, float& v0, float& v1) {
+      const float d0 = (s < t && t < c) ? -v0 : 0.f, d1 = (s + 1 < t && t < c) ? -v1 : 0.f;
+      const float p0 = d0 * A[t * kAStride + s], p1 = d1 * A[t * kAStride + s + 1];
+      rp[(t - m0) >> 3] += p0 + p1;
+      cp[(p >> 1) & 1][0] += p0;
+      cp[(p >> 1) & 1][1] += p1;
+      const float f = bt[t];
+      *reinterpret_cast<__nv_bfloat162*>(Mmb + t * LDT + s) =
+          __floats2bfloat162_rn(d0 * f * __expf(G[t] - G[s]), d1 * f * __expf(G[t] - G[s + 1]));
     });
+    const int g = lane >> 2, q = lane & 3;
+    const float r0s = quad_sum(rp[0]), r1s = quad_sum(rp[1]);
+    if (q == 0) {
+      atomicAdd(&rsum[m0 + g], r0s);
+      atomicAdd(&rsum[m0 + g + 8], r1s);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float x = cp[j][e];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        if (g == 0) atomicAdd(&csum[n0 + 8 * j + 2 * q + e], x);
+      }
   });
   __syncthreads();
   // A = b_t Atil: rowsum(dA o Atil) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
-  for (int t = w; t < C; t += nw) {
-    float r2 = 0.f, c2 = 0.f;
-    for (int s = lane; s < C; s += 32) {
-      r2 += dAf[t * kAStride + s] * A[t * kAStride + s];
-      c2 += dAf[s * kAStride + t] * A[s * kAStride + t];
-    }
-    r2 = warp_sum(r2);
-    c2 = warp_sum(c2);
-    if (lane == 0) {
-      if (t < c) db[t] += r2 / bt[t];
-      dG[t] += r2 - c2;
-    }
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    if (t < c) db[t] += rsum[t] / bt[t];
+    dG[t] += rsum[t] - csum[t];
   }
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i - t * C;
-    Mmb[t * LDT + s] =
-        __float2bfloat16(s < t ? dAf[t * kAStride + s] * bt[t] * __expf(G[t] - G[s]) : 0.f);
-  }
-  __syncthreads();
   // dK = sc_dK + Mm K + Mm^T K
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;

@@ -960,6 +960,59 @@ __global__ void __launch_bounds__(256) k_head_outer(int B, int T, int H, const f
   }
 }
 
+// Gate parameter gradients of one level, one CTA per (head, batch row, 1024-token chunk):
+// gw[h] (D x 4) += sum_t x_t^T y_t and gb[h] += sum_t y_t, x = u(k) rows [U,T,D], y = the four
+// gate-logit gradients [U,T,4] (the gate_weight / gate_bias products of the reference's
+// _gates, src/gpa/attention.py:161-174).  A warp takes every eighth row: lane l holds the
+// columns l, l + 32, ... of x (coalesced) and the row's y (one broadcast 16-byte load).
+constexpr int kGateCols = 4;     // D <= 128
+constexpr int kGateRows = 1024;  // tokens per CTA
+__global__ void __launch_bounds__(256) k_gate_grad(int T, int H, const float* X, int D,
+                                                   const float* Y, float* gw, float* gb) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int t0 = blockIdx.z * kGateRows, t1 = min(T, t0 + kGateRows);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t u = (int64_t)b * H + h;
+  float acc[kGateCols][4] = {}, bsum[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = t0 + w; t < t1; t += 8) {
+    const int64_t o = u * T + t;
+    const float4 y = *reinterpret_cast<const float4*>(Y + o * 4);
+    const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int i = 0; i < kGateCols; ++i) {
+      const int d = lane + 32 * i;
+      const float x = d < D ? X[o * D + d] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] += x * yv[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bsum[j] += yv[j];
+  }
+  __shared__ float red[8][32 * kGateCols][4];
+  __shared__ float rb[8][4];
+#pragma unroll
+  for (int i = 0; i < kGateCols; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[w][lane + 32 * i][j] = acc[i][j];
+  if (lane == 0)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) rb[w][j] = bsum[j];
+  __syncthreads();
+  for (int i = threadIdx.x; i < D * 4; i += blockDim.x) {
+    const int d = i >> 2, j = i & 3;
+    float s = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < 8; ++ww) s += red[ww][d][j];
+    atomicAdd(&gw[((int64_t)h * D + d) * 4 + j], s);
+  }
+  if (threadIdx.x < 4) {
+    float s = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < 8; ++ww) s += rb[ww][threadIdx.x];
+    atomicAdd(&gb[h * 4 + threadIdx.x], s);
+  }
+}
+
 // one warp per (u, t): final input gradients in the input layout / dtype.
 __global__ void k_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
                             const float* qn, const float* dqh, const float* dq_direct,
@@ -1284,6 +1337,16 @@ cudaError_t launch_prep_bwd(int U, int T, int H, int D, int M, const float* C, c
   const size_t smem = sizeof(float) * kRowsPerTile * M;
   return launch_smem("prep_bwd", k_prep_bwd, U * ntile, smem, st, U, T, H, D, M, C, Wg, beta_max, pos_none,
                      raw4, nk, kn, ns, sn, dgates, dnk, dns, dslot, d4, dkey);
+}
+
+cudaError_t launch_gate_grad(int B, int T, int H, const float* X, int D, const float* Y, float* gw,
+                             float* gb, cudaStream_t st) {
+  if (!B || !T) return cudaSuccess;
+  if (D > 32 * kGateCols) return cudaErrorInvalidValue;
+  dim3 grid(H, B, (unsigned)((T + kGateRows - 1) / kGateRows));
+  Launch scope_("gate_grad", st);
+  k_gate_grad<<<grid, 256, 0, st>>>(T, H, X, D, Y, gw, gb);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xmode,

@@ -97,6 +97,10 @@ cudaError_t launch_prep_bwd(int U, int T, int H, int D, int M, const float* C, c
                             float* dkey, cudaStream_t st);
 // out[h] (P x Q) += scale[h] * sum over units of head h and tokens of X^T Y.
 // xmode: 0 identity, 1 gelu(X), 2 X is all ones (P must be 1).
+// gate parameter gradients of one level: gw[h] (D x 4) += sum_{b,t} X^T Y and gb[h] (4) +=
+// sum_{b,t} Y over the rows of head h; X [U,T,D] (D <= 128), Y [U,T,4]
+cudaError_t launch_gate_grad(int B, int T, int H, const float* X, int D, const float* Y, float* gw,
+                             float* gb, cudaStream_t st);
 cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xmode,
                               const float* Y, int Q, const float* scale, int64_t scale_stride,
                               float cscale, float* out, cudaStream_t st);

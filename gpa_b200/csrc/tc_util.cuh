@@ -160,6 +160,28 @@ GPA_DEV void load_tiles(const TileJob (&jobs)[N]) {
   }
 }
 
+// bf16 rows [rows x cols] in global memory (row stride src_ld, cols % 8 == 0, 16-byte
+// aligned rows) -> bf16 tile [rows_pad x ld]; rows >= `rows` zero.  16-byte copies, two in
+// flight per thread.
+GPA_DEV void copy_bf16_tile(bf16* dst, int ld, const bf16* src, int src_ld, int rows, int cols,
+                            int rows_pad) {
+  const int c8 = cols >> 3, n = rows_pad * c8;
+  for (int base = threadIdx.x; base < n; base += 2 * blockDim.x) {
+    uint4 v[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = base + j * blockDim.x, r = i / c8, cc = (i - r * c8) << 3;
+      v[j] = (i < n && r < rows) ? *reinterpret_cast<const uint4*>(src + (int64_t)r * src_ld + cc)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = base + j * blockDim.x, r = i / c8, cc = (i - r * c8) << 3;
+      if (i < n) *reinterpret_cast<uint4*>(dst + r * ld + cc) = v[j];
+    }
+  }
+}
+
 template <int MI, int NI, class Body>
 GPA_DEV void tiles_n(int M, int N, Body body) {
   // NI chosen at run time: 32-wide tiles when N allows and they still give every warp a

@@ -86,6 +86,12 @@ BF16_CASES = {
                                 chunk_size=64), 1, 512),
     "chunk64_T130": (dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
                           chunk_size=64), 2, 130),
+    # widths that are multiples of 16 but not of 32 or 64 (16-wide warp tiles, odd tile
+    # counts).  The scalar parameter gradients (relation_gain, edge_logits, relation_beta_raw)
+    # are sums with heavy cancellation: against fp64, the bf16 reference itself is 1.5-9 % off
+    # on them across seeds at these sizes, hence the alternative criterion below.
+    "odd_widths_T200": (dict(heads=2, key_dim=48, value_dim=80, slots=(16, 48, 112),
+                             chunk_size=64), 2, 200),
 }
 
 
