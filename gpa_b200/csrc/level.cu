@@ -435,21 +435,39 @@ __global__ void k_scales(int U, int H, int L, const float* output_logits, float*
 // one warp per (u, t): fp32 unit-major dout; per-unit sum of dout . y_j
 __global__ void k_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, int dt, YPtrs yp,
                           float* dout_f, double* scal) {
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  // 256 threads: a warp per row; the CTA's rows (consecutive, mostly one unit) are summed in
+  // shared memory first, so each level takes one double atomic per unit run, not per row
+  __shared__ float red[8][kMaxLevels];
+  const int wi = threadIdx.x >> 5;
+  const int w = blockIdx.x * (blockDim.x >> 5) + wi, lane = threadIdx.x & 31;
   const int U = B * H;
-  if (w >= U * T) return;
-  const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
-  const int64_t src = (((int64_t)b * T + t) * H + h) * Dv;
-  float acc[kMaxLevels];
-  for (int j = 0; j < L; ++j) acc[j] = 0.f;
-  for (int v = lane; v < Dv; v += 32) {
-    const float g = load_in(dout, src + v, dt);
-    dout_f[(int64_t)w * Dv + v] = g;
-    for (int j = 0; j < L; ++j) acc[j] += g * yp.y[j][(int64_t)w * Dv + v];
+  if (w < U * T) {
+    const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
+    const int64_t src = (((int64_t)b * T + t) * H + h) * Dv;
+    float acc[kMaxLevels];
+    for (int j = 0; j < L; ++j) acc[j] = 0.f;
+    for (int v = lane; v < Dv; v += 32) {
+      const float g = load_in(dout, src + v, dt);
+      dout_f[(int64_t)w * Dv + v] = g;
+      for (int j = 0; j < L; ++j) acc[j] += g * yp.y[j][(int64_t)w * Dv + v];
+    }
+    for (int j = 0; j < L; ++j) {
+      const float s = warp_sum(acc[j]);
+      if (lane == 0) red[wi][j] = s;
+    }
   }
-  for (int j = 0; j < L; ++j) {
-    const float s = warp_sum(acc[j]);
-    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_OutW], (double)s);
+  __syncthreads();
+  if (threadIdx.x < L) {
+    const int j = threadIdx.x, w0 = blockIdx.x * (blockDim.x >> 5);
+    int r = 0;
+    while (r < 8 && w0 + r < U * T) {
+      const int ur = (w0 + r) / T;
+      double s = 0.0;
+      int e = r;
+      for (; e < 8 && w0 + e < U * T && (w0 + e) / T == ur; ++e) s += red[e][j];
+      atomicAdd(&scal[((int64_t)ur * L + j) * kNScal + kS_OutW], s);
+      r = e;
+    }
   }
 }
 
@@ -634,6 +652,7 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     float* draw, float* dn, float* dnsum, double* scal) {
   __shared__ float red_dn[8][32 * NPL];
   __shared__ int blk[8];
+  __shared__ float red_cg[8];  // count-gain partial of each warp's row (one atomic per unit run)
   const int T = bl.T;
   const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + wi;
@@ -690,7 +709,7 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     dr.store(draw + o, M);
     dnv.store(dn + o, M);
     cg = warp_sum(cg);
-    if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_CountGain], (double)cg);
+    if (lane == 0) red_cg[wi] = cg;
     if (wno > kUnitEps) {
       const float yd = y2.dot(dy2, M), iw = 1.f / wno;
 #pragma unroll
@@ -706,6 +725,18 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     blk[wi] = -1;
   }
   __syncthreads();
+  if (threadIdx.x == 0) {  // consecutive live rows of one unit: one double atomic per run
+    const int w0 = blockIdx.x * (blockDim.x >> 5);
+    int r = 0;
+    while (r < 8 && w0 + r < U * T) {
+      const int ur = (w0 + r) / T;
+      double s = 0.0;
+      int e = r;
+      for (; e < 8 && w0 + e < U * T && (w0 + e) / T == ur; ++e) s += red_cg[e];
+      atomicAdd(&scal[((int64_t)ur * L + j) * kNScal + kS_CountGain], s);
+      r = e;
+    }
+  }
   // rows of the CTA that share (unit, block) are consecutive: one atomic per run and slot
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     int r = 0;
@@ -1022,17 +1053,34 @@ __global__ void k_input_bwd(int B, int T, int H, int D, int Dv, int dt, const fl
   if (w >= U * T) return;
   const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
   const int64_t dst = ((int64_t)b * T + t) * H + h;
+  // every operand of the row is loaded before the reduction (D, Dv <= 128: 4 per lane)
+  float y[4], dy[4], dd[4], dkv[4], dvv[4];
   const float nrm = qn[w];
-  float yd = 0.f;
-  for (int d = lane; d < D; d += 32) yd += qh[(int64_t)w * D + d] * dqh[(int64_t)w * D + d];
-  yd = warp_sum(yd);
-  for (int d = lane; d < D; d += 32) {
-    const int64_t i = (int64_t)w * D + d;
-    const float g = nrm > kUnitEps ? (dqh[i] - qh[i] * yd) / nrm : dqh[i] / kUnitEps;
-    store_out(dq, dst * D + d, g + dq_direct[i], dt);
-    store_out(dk, dst * D + d, dkey[i], dt);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = lane + 32 * i;
+    const int64_t o = (int64_t)w * D + d;
+    const bool in = d < D;
+    y[i] = in ? qh[o] : 0.f;
+    dy[i] = in ? dqh[o] : 0.f;
+    dd[i] = in ? dq_direct[o] : 0.f;
+    dkv[i] = in ? dkey[o] : 0.f;
+    dvv[i] = d < Dv ? dval[(int64_t)w * Dv + d] : 0.f;
   }
-  for (int d = lane; d < Dv; d += 32) store_out(dv, dst * Dv + d, dval[(int64_t)w * Dv + d], dt);
+  float yd = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) yd += y[i] * dy[i];
+  yd = warp_sum(yd);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) {
+      const float g = nrm > kUnitEps ? (dy[i] - y[i] * yd) / nrm : dy[i] / kUnitEps;
+      store_out(dq, dst * D + d, g + dd[i], dt);
+      store_out(dk, dst * D + d, dkv[i], dt);
+    }
+    if (d < Dv) store_out(dv, dst * Dv + d, dvv[i], dt);
+  }
 }
 
 // per head: scalar parameter gradients from per-unit sums.
