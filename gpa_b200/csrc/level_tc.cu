@@ -24,17 +24,19 @@ using tc::tiles_n;
 
 constexpr int R = kRowsPerTile;  // 64 tokens per CTA
 
-GPA_DEV void store_bf16_row(bf16* dst, const float (&x)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV void store_bf16_row(bf16* dst, const float (&x)[N], int n) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) dst[lane + 32 * i] = __float2bfloat16(x[i]);
 }
 
-GPA_DEV void store_split_row(bf16* hi, bf16* lo, const float (&x)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV void store_split_row(bf16* hi, bf16* lo, const float (&x)[N], int n) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) tc::split_bf16(x[i], hi + lane + 32 * i, lo + lane + 32 * i);
 }
 
@@ -55,6 +57,7 @@ struct LPrep {
   }
 };
 
+template <int NPL>
 __global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D, int M,
                                                      const float* key, const float* C,
                                                      const float* Wg, const float* gbias,
@@ -77,13 +80,13 @@ __global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D,
     *reinterpret_cast<float4*>(Wg4 + 4 * i) = *reinterpret_cast<const float4*>(Wg + ((int64_t)h * D + i) * 4);
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
-    float kx[kMaxPerLane];
+    float kx[NPL];
     load_vec(kx, key + row(u, T, t0 + t) * D, D);
     const float nrm = warp_norm(kx, D);
     const float inv = 1.f / fmaxf(nrm, kUnitEps);
     float r[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       const int d = lane + 32 * i;
       if (d >= D) break;
       const float x = kx[i] * inv;
@@ -120,12 +123,12 @@ __global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D,
   });
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
-    float x[kMaxPerLane];
+    float x[NPL];
     load_vec(x, St + t * M, M);
     const float nrm = warp_norm(x, M);
     const float inv = 1.f / fmaxf(nrm, kUnitEps);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= inv;
+    for (int i = 0; i < NPL; ++i) x[i] *= inv;
     store_vec(ns + row(u, T, t0 + t) * M, x, M);
     if (lane == 0) sn[row(u, T, t0 + t)] = nrm;
   }
@@ -152,6 +155,7 @@ struct LPost {
   }
 };
 
+template <int NPL>
 __global__ void __launch_bounds__(512) tk_level_post(
     int U, Blocks bl, int post, int H, int D, int Dv, int M, int with_residual, const float* nk,
     const float* key, const float* val, const float* Abnd, const float* Bbnd, const float* fzA,
@@ -181,14 +185,14 @@ __global__ void __launch_bounds__(512) tk_level_post(
   });
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
-    float x[kMaxPerLane];
+    float x[NPL];
     if (t < c) {
       load_vec(x, Wf + t * M, M);
       warp_softmax(x, M);
       store_vec(write + row(u, T, t0 + t) * M, x, M);
     } else {
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) x[i] = 0.f;
+      for (int i = 0; i < NPL; ++i) x[i] = 0.f;
     }
     store_vec(Wf + t * M, x, M);
     store_bf16_row(Wb + t * lm, x, M);
@@ -265,21 +269,22 @@ GPA_DEV void stage_rows(float* dst, const float* src, int c, int M) {
 }
 
 // reader_row_fwd with the row's logits and weighted incoming message in shared memory
-GPA_DEV void reader_row_fwd_s(float (&base)[kMaxPerLane], const float* lg, const float* incr,
+template <int N>
+GPA_DEV void reader_row_fwd_s(float (&base)[N], const float* lg, const float* incr,
                               int M, bool has_in, float rg) {
   load_vec(base, lg, M);
   if (has_in) {
     const int lane = threadIdx.x & 31;
-    float inc[kMaxPerLane];
+    float inc[N];
     load_vec(inc, incr, M);
     float mean = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
+    for (int i = 0; i < N; ++i)
       if (lane + 32 * i < M) mean += inc[i];
     mean = warp_sum(mean) / M;
     float var = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
+    for (int i = 0; i < N; ++i)
       if (lane + 32 * i < M) {
         inc[i] -= mean;
         var += inc[i] * inc[i];
@@ -287,31 +292,32 @@ GPA_DEV void reader_row_fwd_s(float (&base)[kMaxPerLane], const float* lg, const
     var = warp_sum(var) / M;
     const float sd = rsqrtf(var + kCenterEps);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) base[i] += rg * tanhf(inc[i] * sd);
+    for (int i = 0; i < N; ++i) base[i] += rg * tanhf(inc[i] * sd);
   }
   warp_softmax(base, M);
 }
 
 // reader_row_bwd up to dz (the gradient of the weighted incoming message), which the caller
 // scatters to the messages and edge weights tile-wise.
-GPA_DEV void reader_row_bwd_s(float (&db)[kMaxPerLane], float (&dz)[kMaxPerLane],
-                              const float (&r)[kMaxPerLane], const float (&dr)[kMaxPerLane],
+template <int N>
+GPA_DEV void reader_row_bwd_s(float (&db)[N], float (&dz)[N], const float (&r)[N],
+                              const float (&dr)[N],
                               const float* incr, int M, bool has_in, float rg, float& rg_acc) {
   const int lane = threadIdx.x & 31;
   softmax_bwd(db, r, dr, M);
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) dz[i] = 0.f;
+  for (int i = 0; i < N; ++i) dz[i] = 0.f;
   if (!has_in) return;
-  float inc[kMaxPerLane];
+  float inc[N];
   load_vec(inc, incr, M);
   float mean = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < M) mean += inc[i];
   mean = warp_sum(mean) / M;
   float var = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < M) {
       inc[i] -= mean;
       var += inc[i] * inc[i];
@@ -320,7 +326,7 @@ GPA_DEV void reader_row_bwd_s(float (&db)[kMaxPerLane], float (&dz)[kMaxPerLane]
   const float sd = rsqrtf(var + kCenterEps);
   float rgp = 0.f, dsum = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < N; ++i) {
     const float tz = tanhf(inc[i] * sd);
     if (lane + 32 * i < M) rgp += db[i] * tz;
     dz[i] = rg * db[i] * (1.f - tz * tz);
@@ -331,13 +337,13 @@ GPA_DEV void reader_row_bwd_s(float (&db)[kMaxPerLane], float (&dz)[kMaxPerLane]
   const float dvar = dsum * -0.5f * sd * sd * sd;
   float dmean = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < N; ++i) {
     dz[i] = dz[i] * sd + dvar * 2.f * inc[i] / M;
     if (lane + 32 * i < M) dmean += dz[i];
   }
   dmean = warp_sum(dmean) / M;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) dz[i] -= dmean;
+  for (int i = 0; i < N; ++i) dz[i] -= dmean;
 }
 
 // ------------------------------------------------------------------ bridge
@@ -358,6 +364,7 @@ struct LBridge {
   }
 };
 
+template <int NPL>
 __global__ void __launch_bounds__(512) tk_bridge(
     int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
     const float* relation_gain, const float* route_up, const float* route_down,
@@ -386,14 +393,14 @@ __global__ void __launch_bounds__(512) tk_bridge(
   }
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
-    float x[kMaxPerLane];
+    float x[NPL];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
       reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * M, M, in.n > 0, rg);
       store_vec(r_out + o * M, x, M);
     } else {
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) x[i] = 0.f;
+      for (int i = 0; i < NPL; ++i) x[i] = 0.f;
     }
     store_vec(Rf + t * M, x, M);
     store_bf16_row(ARQ + t * la, x, M);
@@ -444,12 +451,12 @@ __global__ void __launch_bounds__(512) tk_bridge(
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
     const int64_t o = row(u, T, t0 + t);
-    float x[kMaxPerLane];
+    float x[NPL];
     load_vec(x, Of + t * M, M);
     const float a = warp_norm(x, M);
     const float ia = 1.f / fmaxf(a, kUnitEps);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
+    for (int i = 0; i < NPL; ++i) x[i] *= ia;
     store_vec(qoh + o * M, x, M);
     if ((threadIdx.x & 31) == 0) qon[o] = a;
   }
@@ -476,6 +483,7 @@ struct LBridgeBwd {
   }
 };
 
+template <int NPL>
 __global__ void __launch_bounds__(512) tk_bridge_bwd(
     int U, int T, int H, int D, int M, int L, int j, BridgeIn in, const float* edge_logits,
     const float* relation_gain, const float* route_up, const float* route_down,
@@ -505,17 +513,17 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
   for (int t = threadIdx.x; t < R; t += blockDim.x) qn[t] = t < c ? qon[row(u, T, t0 + t)] : 0.f;
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
-    float dx[kMaxPerLane];
+    float dx[NPL];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
-      float y[kMaxPerLane], dy[kMaxPerLane];
+      float y[NPL], dy[NPL];
       load_vec(y, Rf + t * M, M);
       load_vec(dy, (const float*)Hb + t * M, M);
       unit_bwd(dx, y, dy, qn[t], M);
       store_vec(dqo_out + o * M, dx, M);
     } else {
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) dx[i] = 0.f;
+      for (int i = 0; i < NPL; ++i) dx[i] = 0.f;
     }
     store_split_row(Qb + t * lm, Ql + t * lm, dx, M);
   }
@@ -603,16 +611,16 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
   __syncthreads();
   float rg_acc = 0.f;
   for (int t = warp; t < R; t += nw) {
-    float dz[kMaxPerLane];
+    float dz[NPL];
     if (t < c) {
-      float r[kMaxPerLane], dr[kMaxPerLane], db[kMaxPerLane];
+      float r[NPL], dr[NPL], db[NPL];
       load_vec(r, Rr + t * M, M);
       load_vec(dr, Rf + t * M, M);
       reader_row_bwd_s(db, dz, r, dr, Inc + t * M, M, in.n > 0, rg, rg_acc);
       store_vec(dlogits + row(u, T, t0 + t) * M, db, M);
     } else {
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) dz[i] = 0.f;
+      for (int i = 0; i < NPL; ++i) dz[i] = 0.f;
     }
     store_vec(DZ + t * M, dz, M);
   }
@@ -659,6 +667,7 @@ struct LPostBwd {
   }
 };
 
+template <int NPL>
 __global__ void __launch_bounds__(512) tk_post_bwd(
     int U, Blocks bl, int post, int offset, int H, int D, int Dv, int M, int L, int j,
     int with_residual, const float* nk, const float* write, const float* Abnd, const float* Bbnd,
@@ -743,7 +752,7 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
     atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_EtaV], -(double)red[33]);
   }
   for (int t = warp; t < R; t += nw) {
-    float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+    float y[NPL], dy[NPL], dx[NPL];
     load_vec(y, Wf + t * M, M);
     load_vec(dy, dWf + t * M, M);
     softmax_bwd(dx, y, dy, M);
@@ -807,7 +816,8 @@ struct LPrepBwd {
   }
 };
 
-__global__ void __launch_bounds__(512) tk_prep_bwd(int U, int T, int H, int D, int M,
+template <int NPL>
+__global__ void __launch_bounds__(512, 2) tk_prep_bwd(int U, int T, int H, int D, int M,
                                                    const float* C, const float* Wg,
                                                    float beta_max, int pos_none, const float* raw4,
                                                    const float* nk, const float* kn,
@@ -830,17 +840,17 @@ __global__ void __launch_bounds__(512) tk_prep_bwd(int U, int T, int H, int D, i
     *reinterpret_cast<float4*>(Wg4 + 4 * i) = *reinterpret_cast<const float4*>(Wg + ((int64_t)h * D + i) * 4);
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
-    float base[kMaxPerLane];
+    float base[NPL];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
       // every global read of the row first (the stores below may alias the inputs)
       const float4 r4 = *reinterpret_cast<const float4*>(raw4 + o * 4);
       const float4 g4 = *reinterpret_cast<const float4*>(dgates + o * 4);
-      float y[kMaxPerLane], dy[kMaxPerLane], dx[kMaxPerLane];
+      float y[NPL], dy[NPL], dx[NPL];
       load_vec(y, ns + o * M, M);
       load_vec(dy, dns + o * M, M);
       load_vec(base, dslot + o * M, M);
-      float a[kMaxPerLane], da[kMaxPerLane], dkx[kMaxPerLane], cur[kMaxPerLane];
+      float a[NPL], da[NPL], dkx[NPL], cur[NPL];
       load_vec(a, nk + o * D, D);
       load_vec(da, dnk + o * D, D);
       load_vec(cur, dkey + o * D, D);
@@ -858,10 +868,10 @@ __global__ void __launch_bounds__(512) tk_prep_bwd(int U, int T, int H, int D, i
       if (lane < 4) d4out[o * 4 + lane] = d4[lane];
       unit_bwd(dx, y, dy, sno, M);
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) base[i] += dx[i];
+      for (int i = 0; i < NPL; ++i) base[i] += dx[i];
       store_vec(dslot + o * M, base, M);
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) {
+      for (int i = 0; i < NPL; ++i) {
         const int d = lane + 32 * i;
         if (d < D) {
           const float4 w4 = *reinterpret_cast<const float4*>(Wg4 + d * 4);
@@ -870,11 +880,11 @@ __global__ void __launch_bounds__(512) tk_prep_bwd(int U, int T, int H, int D, i
       }
       unit_bwd(dkx, a, da, kno, D);
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) cur[i] += dkx[i];
+      for (int i = 0; i < NPL; ++i) cur[i] += dkx[i];
       store_vec(dkey + o * D, cur, D);
     } else {
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) base[i] = 0.f;
+      for (int i = 0; i < NPL; ++i) base[i] = 0.f;
     }
     store_bf16_row(Dsb + t * lm, base, M);
   }
@@ -1003,6 +1013,12 @@ __global__ void __launch_bounds__(256) tk_head_outer(int B, int T, int H, const 
       });
 }
 
+// per-lane registers of a warp-held row of n <= 256 values; the row kernels are compiled for
+// each count so that their per-row loops have no predicated-off iterations
+inline int npl_of(int n) { return n <= 32 ? 1 : n <= 64 ? 2 : n <= 128 ? 4 : 8; }
+#define TK_NPL(kern, n) \
+  (npl_of(n) == 1 ? kern<1> : npl_of(n) == 2 ? kern<2> : npl_of(n) == 4 ? kern<4> : kern<8>)
+
 template <class Kern, class... Args>
 cudaError_t tk_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStream_t st,
                       Args... args) {
@@ -1026,7 +1042,7 @@ cudaError_t tc_level_prep(int U, int T, int H, int D, int M, const float* key, c
                           float* nk, float* kn, float* slot, float* ns, float* sn, float* raw4,
                           float* gates, cudaStream_t st) {
   const int ntile = (T + R - 1) / R;
-  return tk_launch("tc_level_prep", tk_level_prep, dim3(U * ntile), smem_of<LPrep>(D, M, 0), st,
+  return tk_launch("tc_level_prep", TK_NPL(tk_level_prep, D > M ? D : M), dim3(U * ntile), smem_of<LPrep>(D, M, 0), st,
                    U, T, H, D, M, key, C, Wg, gbias, beta_max, pos_none, nk, kn, slot, ns, sn,
                    raw4, gates);
 }
@@ -1036,7 +1052,7 @@ cudaError_t tc_level_post(int U, const Blocks& bl, int post, int H, int D, int D
                           const float* Abnd, const float* Bbnd, const float* fzA, const float* fzB,
                           const float* residual_raw, int j, float* write, float* bsum,
                           float* key_next, float* val_next, cudaStream_t st) {
-  return tk_launch("tc_level_post", tk_level_post, dim3(U * bl.nb), smem_of<LPost>(D, Dv, M), st,
+  return tk_launch("tc_level_post", TK_NPL(tk_level_post, M), dim3(U * bl.nb), smem_of<LPost>(D, Dv, M), st,
                    U, bl, post, H, D, Dv, M, with_residual, nk, key, val, Abnd, Bbnd, fzA, fzB,
                    residual_raw, j, write, bsum, key_next, val_next);
 }
@@ -1048,7 +1064,7 @@ cudaError_t tc_bridge(int U, int T, int H, int D, int M, int L, int j, const Bri
                       float* hp, float* mlp, float* route, float* qoh, float* qon,
                       cudaStream_t st) {
   const int ntile = (T + R - 1) / R;
-  return tk_launch("tc_bridge", tk_bridge, dim3(U * ntile), smem_of<LBridge>(D, M, 0), st, U, T,
+  return tk_launch("tc_bridge", TK_NPL(tk_bridge, M), dim3(U * ntile), smem_of<LBridge>(D, M, 0), st, U, T,
                    H, D, M, L, j, in, edge_logits, relation_gain, route_up, route_down,
                    route_mlp_gain, Wrs, Wqs, qs, logits, qf, r, hp, mlp, route, qoh, qon);
 }
@@ -1062,7 +1078,7 @@ cudaError_t tc_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, const
                           float* dqo, float* droute, float* dhp, float* dlogits, float* dq_direct,
                           double* scal, double* scalE, int E, cudaStream_t st) {
   const int ntile = (T + R - 1) / R;
-  return tk_launch("tc_bridge_bwd", tk_bridge_bwd, dim3(U * ntile), smem_of<LBridgeBwd>(D, M, 0),
+  return tk_launch("tc_bridge_bwd", TK_NPL(tk_bridge_bwd, M), dim3(U * ntile), smem_of<LBridgeBwd>(D, M, 0),
                    st, U, T, H, D, M, L, j, in, edge_logits, relation_gain, route_up, route_down,
                    route_mlp_gain, Wrs, Wqs, qs, logits, r, hp, mlp, qoh, qon, dqoh, dqo, droute,
                    dhp, dlogits, dq_direct, scal, scalE, E);
@@ -1075,7 +1091,7 @@ cudaError_t tc_post_bwd(int U, const Blocks& bl, int post, int offset, int H, in
                         const float* dkey, const float* dval, float* dwrite, float* dnk,
                         float* extA, float* extB, float* dfzA, float* dfzB, double* scal,
                         cudaStream_t st) {
-  return tk_launch("tc_post_bwd", tk_post_bwd, dim3(U * bl.nb), smem_of<LPostBwd>(D, Dv, M), st,
+  return tk_launch("tc_post_bwd", TK_NPL(tk_post_bwd, M), dim3(U * bl.nb), smem_of<LPostBwd>(D, Dv, M), st,
                    U, bl, post, offset, H, D, Dv, M, L, j, with_residual, nk, write, Abnd, Bbnd,
                    fzA, fzB, residual_raw, dkey, dval, dwrite, dnk, extA, extB, dfzA, dfzB, scal);
 }
@@ -1086,7 +1102,7 @@ cudaError_t tc_prep_bwd(int U, int T, int H, int D, int M, const float* C, const
                         const float* dnk, const float* dns, float* dslot, float* d4, float* dkey,
                         cudaStream_t st) {
   const int ntile = (T + R - 1) / R;
-  return tk_launch("tc_prep_bwd", tk_prep_bwd, dim3(U * ntile), smem_of<LPrepBwd>(D, M, 0), st, U,
+  return tk_launch("tc_prep_bwd", TK_NPL(tk_prep_bwd, D > M ? D : M), dim3(U * ntile), smem_of<LPrepBwd>(D, M, 0), st, U,
                    T, H, D, M, C, Wg, beta_max, pos_none, raw4, nk, kn, ns, sn, dgates, dnk, dns,
                    dslot, d4, dkey);
 }

@@ -12,16 +12,17 @@ constexpr int kMaxPerLane = 8;  // vectors up to 256 long per warp row
 GPA_DEV int64_t row(int u, int T, int t) { return (int64_t)u * T + t; }
 
 // softmax over the lane-strided vector x[0..n) held in registers
-GPA_DEV void warp_softmax(float (&x)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV void warp_softmax(float (&x)[N], int n) {
   const int lane = threadIdx.x & 31;
   float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) mx = fmaxf(mx, x[i]);
   mx = warp_max(mx);
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) {
       x[i] = __expf(x[i] - mx);
       s += x[i];
@@ -29,60 +30,65 @@ GPA_DEV void warp_softmax(float (&x)[kMaxPerLane], int n) {
   s = warp_sum(s);
   const float inv = 1.f / s;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) x[i] *= inv;
 }
 
-GPA_DEV float warp_norm(const float (&x)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV float warp_norm(const float (&x)[N], int n) {
   const int lane = threadIdx.x & 31;
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) s += x[i] * x[i];
   return sqrtf(warp_sum(s));
 }
 
-GPA_DEV float warp_dot(const float (&x)[kMaxPerLane], const float (&y)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV float warp_dot(const float (&x)[N], const float (&y)[N], int n) {
   const int lane = threadIdx.x & 31;
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) s += x[i] * y[i];
   return warp_sum(s);
 }
 
-GPA_DEV void load_vec(float (&x)[kMaxPerLane], const float* p, int n) {
+template <int N>
+GPA_DEV void load_vec(float (&x)[N], const float* p, int n) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) x[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
+  for (int i = 0; i < N; ++i) x[i] = lane + 32 * i < n ? p[lane + 32 * i] : 0.f;
 }
 
-GPA_DEV void store_vec(float* p, const float (&x)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV void store_vec(float* p, const float (&x)[N], int n) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < N; ++i)
     if (lane + 32 * i < n) p[lane + 32 * i] = x[i];
 }
 
 // unit-normalisation backward: y = x / max(|x|, eps)
-GPA_DEV void unit_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
-                      const float (&dy)[kMaxPerLane], float nrm, int n) {
+template <int N>
+GPA_DEV void unit_bwd(float (&dx)[N], const float (&y)[N], const float (&dy)[N], float nrm,
+                      int n) {
   if (nrm > kUnitEps) {
     const float yd = warp_dot(y, dy, n);
     const float inv = 1.f / nrm;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = (dy[i] - y[i] * yd) * inv;
+    for (int i = 0; i < N; ++i) dx[i] = (dy[i] - y[i] * yd) * inv;
   } else {
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) dx[i] = dy[i] / kUnitEps;
+    for (int i = 0; i < N; ++i) dx[i] = dy[i] / kUnitEps;
   }
 }
 
-GPA_DEV void softmax_bwd(float (&dx)[kMaxPerLane], const float (&y)[kMaxPerLane],
-                         const float (&dy)[kMaxPerLane], int n) {
+template <int N>
+GPA_DEV void softmax_bwd(float (&dx)[N], const float (&y)[N], const float (&dy)[N], int n) {
   const float yd = warp_dot(y, dy, n);
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) dx[i] = y[i] * (dy[i] - yd);
+  for (int i = 0; i < N; ++i) dx[i] = y[i] * (dy[i] - yd);
 }
 
 GPA_DEV float block_sum(float x, float* red) {
