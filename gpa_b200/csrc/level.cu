@@ -198,6 +198,7 @@ GPA_DEV void block_prefix(const float* bsum, int u, int nb, int first, int last,
 // CTA per (u, lag block), level j: running counts from the incoming cache and the earlier
 // blocks, base logits, the normalised local distribution and write (relation queries / keys).
 // The block's write tile is staged in shared memory (rows t < c contiguous from t0).
+template <int NPL>  // registers per lane of an M-long row
 __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, float read_scale,
                                                 const float* count_gain_raw, int j,
                                                 const float* n0, const float* bsum,
@@ -229,23 +230,23 @@ __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, 
   const float gain = softplus(count_gain_raw[j * H + h]);
   for (int t = warp; t < c; t += nw) {
     const int64_t o = row(u, T, t0 + t);
-    float x[kMaxPerLane], w[kMaxPerLane], cn[kMaxPerLane];
+    float x[NPL], w[NPL], cn[NPL];
     load_vec(x, raw + o * M, M);
     load_vec(cn, Ct + t * M, M);
     load_vec(w, Wt + t * M, M);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) x[i] = read_scale * x[i] + gain * log1pf(cn[i]);
+    for (int i = 0; i < NPL; ++i) x[i] = read_scale * x[i] + gain * log1pf(cn[i]);
     store_vec(logits + o * M, x, M);
     warp_softmax(x, M);
     const float a = warp_norm(x, M);
     const float ia = 1.f / fmaxf(a, kUnitEps);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) x[i] *= ia;
+    for (int i = 0; i < NPL; ++i) x[i] *= ia;
     store_vec(lh + o * M, x, M);
     const float b = warp_norm(w, M);
     const float ib = 1.f / fmaxf(b, kUnitEps);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) w[i] *= ib;
+    for (int i = 0; i < NPL; ++i) w[i] *= ib;
     store_vec(wh + o * M, w, M);
     if ((threadIdx.x & 31) == 0) {
       ln[o] = a;
@@ -385,11 +386,18 @@ __global__ void k_mix(int B, int T, int H, int Dv, int L, const float* output_lo
     s += ow[j];
   }
   const int64_t dst = (((int64_t)b * T + t) * H + h) * Dv;
-  for (int v = lane; v < Dv; v += 32) {
-    float acc = 0.f;
-    for (int j = 0; j < L; ++j) acc += (ow[j] / s) * yp.y[j][(int64_t)w * Dv + v];
-    store_out(out, dst + v, acc, dt);
+  // Dv <= 128: every level's values of the row are loaded before the first store
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < L; ++j) {
+    const float wj = ow[j] / s;
+    const float* yj = yp.y[j] + (int64_t)w * Dv;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < Dv) acc[i] += wj * yj[lane + 32 * i];
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (lane + 32 * i < Dv) store_out(out, dst + lane + 32 * i, acc[i], dt);
 }
 
 __global__ void k_copy(float* dst, const float* src, int64_t n) {
@@ -446,11 +454,18 @@ __global__ void k_mix_bwd(int B, int T, int H, int Dv, int L, const void* dout, 
     const int64_t src = (((int64_t)b * T + t) * H + h) * Dv;
     float acc[kMaxLevels];
     for (int j = 0; j < L; ++j) acc[j] = 0.f;
-    for (int v = lane; v < Dv; v += 32) {
-      const float g = load_in(dout, src + v, dt);
-      dout_f[(int64_t)w * Dv + v] = g;
-      for (int j = 0; j < L; ++j) acc[j] += g * yp.y[j][(int64_t)w * Dv + v];
+    float g[4];  // Dv <= 128: the row's gradient is loaded before any store
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g[i] = lane + 32 * i < Dv ? load_in(dout, src + lane + 32 * i, dt) : 0.f;
+    for (int j = 0; j < L; ++j) {
+      const float* yj = yp.y[j] + (int64_t)w * Dv;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (lane + 32 * i < Dv) acc[j] += g[i] * yj[lane + 32 * i];
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < Dv) dout_f[(int64_t)w * Dv + lane + 32 * i] = g[i];
     for (int j = 0; j < L; ++j) {
       const float s = warp_sum(acc[j]);
       if (lane == 0) red[wi][j] = s;
@@ -1202,14 +1217,18 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
                           cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
   Launch scope_("counts", st);
+  const auto kern = M <= 32    ? k_counts<1>
+                    : M <= 64  ? k_counts<2>
+                    : M <= 128 ? k_counts<4>
+                               : k_counts<8>;
   const size_t smem = (2 * kRowsPerTile * M + M + 256) * sizeof(float);
   if (smem > 48 * 1024) {
     const cudaError_t e =
-        cudaFuncSetAttribute(k_counts, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  k_counts<<<U * bl.nb, 256, smem, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write,
-                                      raw, counts, logits, lh, ln, wh, wn, n_final);
+  kern<<<U * bl.nb, 256, smem, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write, raw,
+                                    counts, logits, lh, ln, wh, wn, n_final);
   return cudaGetLastError();
 }
 
