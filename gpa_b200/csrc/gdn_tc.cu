@@ -420,8 +420,8 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
     acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
     tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, nullptr, ldv, m0, n0, C);
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      if (t < c) d.O[row(u, T, t0 + t) * V + col] = v;
+    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+      if (t < c) st2(d.O + row(u, T, t0 + t) * V + col, v0, v1);
     });
   });
 }
@@ -538,8 +538,9 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
     float part[2] = {0.f, 0.f};
-    acc.each(m0, n0, [&](int t, int col, float& v) {
-      part[(t - m0) >> 3 & 1] += v * __bfloat162float(dOs[t * ldv + col]);
+    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+      const float2 o2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dOs + t * ldv + col));
+      part[(t - m0) >> 3 & 1] += v0 * o2.x + v1 * o2.y;
     });
     const int g = (threadIdx.x & 31) >> 2;
     const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
@@ -571,16 +572,16 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
     Acc<1, NI> acc;
     acc.zero();
     tc::mma_acc3<1, NI, true, false>(acc, dXh, dXl, LDT, Qs, nullptr, ldk, m0, n0, C);
-    acc.each(m0, n0, [&](int s, int col, float& v) {
-      if (s < c) d.sc_dK[row(u, T, t0 + s) * K + col] = v;
+    acc.each2(m0, n0, [&](int, int s, int col, float& v0, float& v1) {
+      if (s < c) st2(d.sc_dK + row(u, T, t0 + s) * K + col, v0, v1);
     });
   });
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
     tc::mma_acc3<1, NI, true, false>(acc, Ph, Pl, LDT, dOs, nullptr, ldv, m0, n0, C);
-    acc.each(m0, n0, [&](int s, int col, float& v) {
-      if (s < c) d.sc_dW[row(u, T, t0 + s) * V + col] = v;
+    acc.each2(m0, n0, [&](int, int s, int col, float& v0, float& v1) {
+      if (s < c) st2(d.sc_dW + row(u, T, t0 + s) * V + col, v0, v1);
     });
   });
 }

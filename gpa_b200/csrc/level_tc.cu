@@ -116,9 +116,9 @@ __global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D,
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Kb, ld16(D), Cb, ld16(D), m0, n0, D);
-    acc.each(m0, n0, [&](int t, int m, float& v) {
-      St[t * M + m] = v;
-      if (t < c) slot[row(u, T, t0 + t) * M + m] = v;
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      *reinterpret_cast<float2*>(St + t * M + m) = make_float2(v0, v1);
+      if (t < c) tc::st2(slot + row(u, T, t0 + t) * M + m, v0, v1);
     });
   });
   __syncthreads();
@@ -181,7 +181,9 @@ __global__ void __launch_bounds__(512) tk_level_post(
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Nk, ld, Af, lm, m0, n0, D);
-    acc.each(m0, n0, [&](int t, int m, float& v) { Wf[t * M + m] = v; });
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      *reinterpret_cast<float2*>(Wf + t * M + m) = make_float2(v0, v1);
+    });
   });
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
@@ -413,9 +415,9 @@ __global__ void __launch_bounds__(512) tk_bridge(
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, false>(acc, ARQ, la, Wbuf, lh, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int rr, float& v) {
-      if (t < c) hp_out[row(u, T, t0 + t) * 2 * M + rr] = v;
-      Hb[t * lh + rr] = __float2bfloat16(gelu(v));
+    acc.each2(m0, n0, [&](int, int t, int rr, float& v0, float& v1) {
+      if (t < c) tc::st2(hp_out + row(u, T, t0 + t) * 2 * M + rr, v0, v1);
+      *reinterpret_cast<__nv_bfloat162*>(Hb + t * lh + rr) = __floats2bfloat162_rn(gelu(v0), gelu(v1));
     });
   });
   __syncthreads();
@@ -427,14 +429,15 @@ __global__ void __launch_bounds__(512) tk_bridge(
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Hb, lh, Wbuf, lm, m0, n0, 2 * M);
-    acc.each(m0, n0, [&](int t, int m, float& v) {
-      const float route = Rf[t * M + m] + mg * v;
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      const float2 rf = *reinterpret_cast<const float2*>(Rf + t * M + m);
+      const float route0 = rf.x + mg * v0, route1 = rf.y + mg * v1;
       if (t < c) {
         const int64_t o = row(u, T, t0 + t) * M + m;
-        mlp_out[o] = v;
-        route_out[o] = route;
+        tc::st2(mlp_out + o, v0, v1);
+        tc::st2(route_out + o, route0, route1);
       }
-      ARQ[t * la + m] = __float2bfloat16(route);
+      *reinterpret_cast<__nv_bfloat162*>(ARQ + t * la + m) = __floats2bfloat162_rn(route0, route1);
     });
   });
   __syncthreads();
@@ -446,7 +449,9 @@ __global__ void __launch_bounds__(512) tk_bridge(
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, false>(acc, ARQ, la, Wbuf, lm, m0, n0, M + D);
-    acc.each(m0, n0, [&](int t, int m, float& v) { Of[t * M + m] = v; });
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      *reinterpret_cast<float2*>(Of + t * M + m) = make_float2(v0, v1);
+    });
   });
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
@@ -535,10 +540,10 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
     Acc<1, NI> acc;
     acc.zero();
     tc::mma_acc3<1, NI, false, true>(acc, Qb, Ql, lm, Wbuf, nullptr, lm, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int m, float& v) {
-      Rf[t * M + m] = v;
-      Rb[t * lm + m] = __float2bfloat16(v);
-      if (t < c) droute_out[row(u, T, t0 + t) * M + m] = v;
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      *reinterpret_cast<float2*>(Rf + t * M + m) = make_float2(v0, v1);
+      *reinterpret_cast<__nv_bfloat162*>(Rb + t * lm + m) = __floats2bfloat162_rn(v0, v1);
+      if (t < c) tc::st2(droute_out + row(u, T, t0 + t) * M + m, v0, v1);
     });
   });
   // dq_direct += qs dqo W_qs^T
@@ -596,7 +601,11 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
     Acc<1, NI> acc;
     acc.zero();
     tc::mma_acc3<1, NI, false, true>(acc, Hb, Hl, lh, Wbuf, nullptr, lh, m0, n0, 2 * M);
-    acc.each(m0, n0, [&](int t, int m, float& v) { Rf[t * M + m] += v; });
+    acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+      float2* p = reinterpret_cast<float2*>(Rf + t * M + m);
+      const float2 x = *p;
+      *p = make_float2(x.x + v0, x.y + v1);
+    });
   });
   __syncthreads();
   float w[kMaxIn];
@@ -765,8 +774,8 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
     Acc<1, NI> acc;
     acc.zero();
     mma_acc<1, NI, false, true>(acc, dLb, lm, Af, lm, m0, n0, M);
-    acc.each(m0, n0, [&](int t, int d, float& v) {
-      if (t < c) dnk[row(u, T, t0 + t) * D + d] = v;
+    acc.each2(m0, n0, [&](int, int t, int d, float& v0, float& v1) {
+      if (t < c) tc::st2(dnk + row(u, T, t0 + t) * D + d, v0, v1);
     });
   });
   __syncthreads();  // Nk
