@@ -51,7 +51,7 @@ struct LPrep {
     Carve c;
     Kb = c.take(2 * R * ld16(D));
     Cb = c.take(2 * M * ld16(D));
-    St = c.take(4 * R * M);
+    St = c.take(4 * R * (M + 8));  // row stride M + 8: conflict-free accumulator float2 stores
     Wg4 = c.take(4 * 4 * D);
     total = c.off;
   }
@@ -117,14 +117,14 @@ __global__ void __launch_bounds__(512) tk_level_prep(int U, int T, int H, int D,
     acc.zero();
     mma_acc<1, NI, false, true>(acc, Kb, ld16(D), Cb, ld16(D), m0, n0, D);
     acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
-      *reinterpret_cast<float2*>(St + t * M + m) = make_float2(v0, v1);
+      *reinterpret_cast<float2*>(St + t * (M + 8) + m) = make_float2(v0, v1);
       if (t < c) tc::st2(slot + row(u, T, t0 + t) * M + m, v0, v1);
     });
   });
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
     float x[NPL];
-    load_vec(x, St + t * M, M);
+    load_vec(x, St + t * (M + 8), M);
     const float nrm = warp_norm(x, M);
     const float inv = 1.f / fmaxf(nrm, kUnitEps);
 #pragma unroll
@@ -149,7 +149,7 @@ struct LPost {
     Af = c.take(2 * D * ld16(M));
     Bf = c.take(2 * M * ld16(Dv));
     Nk = c.take(2 * R * ld16(D));
-    Wf = c.take(4 * R * M);
+    Wf = c.take(4 * R * (M + 8));  // row stride M + 8
     Wb = c.take(2 * R * ld16(M));
     total = c.off;
   }
@@ -182,27 +182,27 @@ __global__ void __launch_bounds__(512) tk_level_post(
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Nk, ld, Af, lm, m0, n0, D);
     acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
-      *reinterpret_cast<float2*>(Wf + t * M + m) = make_float2(v0, v1);
+      *reinterpret_cast<float2*>(Wf + t * (M + 8) + m) = make_float2(v0, v1);
     });
   });
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
     float x[NPL];
     if (t < c) {
-      load_vec(x, Wf + t * M, M);
+      load_vec(x, Wf + t * (M + 8), M);
       warp_softmax(x, M);
       store_vec(write + row(u, T, t0 + t) * M, x, M);
     } else {
 #pragma unroll
       for (int i = 0; i < NPL; ++i) x[i] = 0.f;
     }
-    store_vec(Wf + t * M, x, M);
+    store_vec(Wf + t * (M + 8), x, M);
     store_bf16_row(Wb + t * lm, x, M);
   }
   __syncthreads();
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     float s = 0.f;
-    for (int t = 0; t < c; ++t) s += Wf[t * M + m];
+    for (int t = 0; t < c; ++t) s += Wf[t * (M + 8) + m];
     bsum[((int64_t)u * bl.nb + n) * M + m] = s;
   }
   if (!with_residual) return;
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(512) tk_level_post(
 // incoming message's loads in flight together): inc[t][m] = sum_a w_a msg_a[t][m] and, when
 // given, a second [rows x M] fp32 tile; rows t >= c are zero.
 GPA_DEV void stage_incoming(float* inc, const BridgeIn& in, const float* w, int64_t r0, int c,
-                            int M) {
+                            int M, int ld) {  // ld: row stride of inc
   const int m4 = M >> 2;
   for (int i = threadIdx.x; i < R * m4; i += blockDim.x) {
     const int t = i / m4;
@@ -259,7 +259,7 @@ GPA_DEV void stage_incoming(float* inc, const BridgeIn& in, const float* w, int6
           acc.w += w[a] * x[a].w;
         }
     }
-    *reinterpret_cast<float4*>(inc + 4 * i) = acc;
+    *reinterpret_cast<float4*>(inc + t * ld + 4 * i - t * M) = acc;
   }
 }
 
@@ -354,14 +354,14 @@ struct LBridge {
   size_t Rf, ARQ, Hb, Wbuf, Of, total;
   __host__ __device__ LBridge(int D, int M, int) {
     Carve c;
-    Rf = c.take(4 * R * M);
+    Rf = c.take(4 * R * (M + 8));  // fp32 tiles with row stride M + 8
     ARQ = c.take(2 * R * ld16(M + D));
     Hb = c.take(2 * R * ld16(2 * M));
     const size_t w1 = 2 * M * ld16(2 * M), w2 = 2 * (2 * M) * ld16(M), w3 = 2 * (M + D) * ld16(M);
     size_t w = w1 > w2 ? w1 : w2;
     w = w > w3 ? w : w3;
     Wbuf = c.take(w);
-    Of = c.take(4 * R * M);
+    Of = c.take(4 * R * (M + 8));
     total = c.off;
   }
 };
@@ -391,20 +391,20 @@ __global__ void __launch_bounds__(512) tk_bridge(
   {
     float* Lg = (float*)(smem + Lb.Hb);  // Hb and Of are free until their GEMMs
     stage_rows(Lg, logits + row(u, T, t0) * M, c, M);
-    if (in.n > 0) stage_incoming(Of, in, w, row(u, T, t0), c, M);
+    if (in.n > 0) stage_incoming(Of, in, w, row(u, T, t0), c, M, M + 8);
   }
   __syncthreads();
   for (int t = warp; t < R; t += nw) {
     float x[NPL];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
-      reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * M, M, in.n > 0, rg);
+      reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * (M + 8), M, in.n > 0, rg);
       store_vec(r_out + o * M, x, M);
     } else {
 #pragma unroll
       for (int i = 0; i < NPL; ++i) x[i] = 0.f;
     }
-    store_vec(Rf + t * M, x, M);
+    store_vec(Rf + t * (M + 8), x, M);
     store_bf16_row(ARQ + t * la, x, M);
   }
   tile_to_bf16(ARQ + M, la, qf + row(u, T, t0) * D, D, c, D, R);
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(512) tk_bridge(
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Hb, lh, Wbuf, lm, m0, n0, 2 * M);
     acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
-      const float2 rf = *reinterpret_cast<const float2*>(Rf + t * M + m);
+      const float2 rf = *reinterpret_cast<const float2*>(Rf + t * (M + 8) + m);
       const float route0 = rf.x + mg * v0, route1 = rf.y + mg * v1;
       if (t < c) {
         const int64_t o = row(u, T, t0 + t) * M + m;
@@ -450,14 +450,14 @@ __global__ void __launch_bounds__(512) tk_bridge(
     acc.zero();
     mma_acc<1, NI, false, false>(acc, ARQ, la, Wbuf, lm, m0, n0, M + D);
     acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
-      *reinterpret_cast<float2*>(Of + t * M + m) = make_float2(v0, v1);
+      *reinterpret_cast<float2*>(Of + t * (M + 8) + m) = make_float2(v0, v1);
     });
   });
   __syncthreads();
   for (int t = warp; t < c; t += nw) {
     const int64_t o = row(u, T, t0 + t);
     float x[NPL];
-    load_vec(x, Of + t * M, M);
+    load_vec(x, Of + t * (M + 8), M);
     const float a = warp_norm(x, M);
     const float ia = 1.f / fmaxf(a, kUnitEps);
 #pragma unroll
@@ -615,7 +615,7 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
   float* Inc = (float*)Hb;
   float* Rr = (float*)Hl;
   float* DZ = (float*)Wbuf;
-  if (in.n > 0) stage_incoming(Inc, in, w, row(u, T, t0), c, M);
+  if (in.n > 0) stage_incoming(Inc, in, w, row(u, T, t0), c, M, M);
   stage_rows(Rr, r_in + row(u, T, t0) * M, c, M);
   __syncthreads();
   float rg_acc = 0.f;
@@ -749,10 +749,16 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
     // dW += (-ek dk) A_f + (-ev dv) B_f^T
     tiles_n<1, 2>(R, M, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
-      acc.each(m0, n0, [&](int t, int m, float& v) { v = dWf[t * M + m]; });
+      acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+        const float2 x = *reinterpret_cast<const float2*>(dWf + t * M + m);
+        v0 = x.x;
+        v1 = x.y;
+      });
       mma_acc<1, NI, false, false>(acc, dKb, ld, Af, lm, m0, n0, D);
       mma_acc<1, NI, false, true>(acc, dVb, lv, Bf, lv, m0, n0, Dv);
-      acc.each(m0, n0, [&](int t, int m, float& v) { dWf[t * M + m] = v; });
+      acc.each2(m0, n0, [&](int, int t, int m, float& v0, float& v1) {
+        *reinterpret_cast<float2*>(dWf + t * M + m) = make_float2(v0, v1);
+      });
     });
   }
   __syncthreads();
