@@ -825,17 +825,23 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     db[t] = dlam[t] = rw[t] = 0.f;
   }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
+  float dsp = 0.f;  // this thread's part of <D, S>
   {  // gates, T of the block as the forward formed it, and the state-term operands
     const GateRegs gr = gate_fetch(d, u, t0, c, true);
     const TileJob jobs[] = {tc::job(Th, Tl, LDT, d.Tsv + ((int64_t)u * bl.nb + n) * C * C, C, C, C, C),
-                            tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C),
-                            tc::job(Sb, nullptr, ldv, sg, V, K, V, K),
-                            tc::job(Db, nullptr, ldv, dg, V, K, V, K)};
+                            tc::job(dWh, dWl, ldv, d.sc_dW + r0 * V, V, c, V, C)};
     tc::copy_bf16_tile(Wb, ldv, reinterpret_cast<const bf16*>(d.W) + r0 * V, V, c, V, C);
     tc::load_tiles(jobs);
+    const TileJob js = tc::job(Sb, nullptr, ldv, sg, V, K, V, K);
+    const TileJob jd = tc::job(Db, nullptr, ldv, dg, V, K, V, K);
+    tc::tile_pair(js, &jd, &dsp);  // S and D tiles; <D, S> from their fp32 values
     gate_finish(gr, c, G, bt);
   }
   __syncthreads();
+  {  // <D, S> in fp32 (red was zeroed before the barrier)
+    const float part = warp_sum(dsp);
+    if (lane == 0) atomicAdd(&red[0], part);
+  }
 
   // ---- state-update terms: WD = W D^T, <D, S>, dWk = -dW S^T
   // sc_dK += lambda WD ; dlambda_t = sum_k K_tk WD_tk
@@ -866,16 +872,6 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       atomicAdd(&dlam[m0 + g + 8], p1);
     }
   });
-  {  // <D, S> in fp32
-    float part = 0.f;
-    for (int i = 4 * threadIdx.x; i < K * V; i += 4 * blockDim.x) {
-      const float4 a = *reinterpret_cast<const float4*>(dg + i);
-      const float4 s4 = *reinterpret_cast<const float4*>(sg + i);
-      part += a.x * s4.x + a.y * s4.y + a.z * s4.z + a.w * s4.w;
-    }
-    part = warp_sum(part);
-    if (lane == 0) atomicAdd(&red[0], part);
-  }
   // dWk = -dW S^T, staged through global memory (L2) for the Wk path
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;

@@ -99,8 +99,9 @@ GPA_DEV TileJob job(bf16* hi, bf16* lo, int ld, const float* src, int src_ld, in
 }
 
 // Load the tiles two at a time: each thread keeps kLoadIlp float4 of each of the two tiles in
-// flight before converting any of them.
-GPA_DEV void tile_pair(const TileJob& A, const TileJob* B) {
+// flight before converting any of them.  With `dot` (A and B of the same geometry), the
+// thread's part of sum(A o B) over the fp32 values is added to *dot on the way.
+GPA_DEV void tile_pair(const TileJob& A, const TileJob* B, float* dot = nullptr) {
   const int ca = A.cols >> 2, na = A.rows_pad * ca;
   const int cb = B ? B->cols >> 2 : 1, nb = B ? B->rows_pad * cb : 0;
   const int n = na > nb ? na : nb;
@@ -119,6 +120,11 @@ GPA_DEV void tile_pair(const TileJob& A, const TileJob* B) {
                     ? *reinterpret_cast<const float4*>(B->src + (int64_t)rb * B->src_ld + xb)
                     : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    }
+    if (dot) {
+#pragma unroll
+      for (int q = 0; q < kLoadIlp; ++q)
+        *dot += va[q].x * vb[q].x + va[q].y * vb[q].y + va[q].z * vb[q].z + va[q].w * vb[q].w;
     }
 #pragma unroll
     for (int q = 0; q < kLoadIlp; ++q) {
