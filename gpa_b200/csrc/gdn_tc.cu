@@ -532,26 +532,30 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
         if (g == 0) atomicAdd(&cs[n0 + 8 * j + 2 * q + h], x);
       }
   });
-  // rowsum(dO o (Q S_n))
-  tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
-    Acc<1, NI> acc;
-    acc.zero();
-    mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
-    float part[2] = {0.f, 0.f};
-    acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
-      const float2 o2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dOs + t * ldv + col));
-      part[(t - m0) >> 3 & 1] += v0 * o2.x + v1 * o2.y;
-    });
+  // racc = rowsum(dO o (Q S_n)) = rowsum(Q o (dO S_n^T)): taken from dq's first product when
+  // dq is wanted, else from Q S_n
+  auto racc_add = [&](int m0, float part0, float part1) {
     const int g = (threadIdx.x & 31) >> 2;
-    const float p0 = quad_sum(part[0]), p1 = quad_sum(part[1]);
+    const float p0 = quad_sum(part0), p1 = quad_sum(part1);
     if ((threadIdx.x & 3) == 0) {
       atomicAdd(&racc[m0 + g], p0);
       atomicAdd(&racc[m0 + g + 8], p1);
     }
-  });
-  __syncthreads();
-  for (int t = threadIdx.x; t < c; t += blockDim.x)
-    d.sc_dG[row(u, T, t0 + t)] = __expf(G[t]) * racc[t] + rs[t] - cs[t];
+  };
+  if (!d.dq) {
+    tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
+      Acc<1, NI> acc;
+      acc.zero();
+      mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
+      float part[2] = {0.f, 0.f};
+      acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+        const float2 o2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dOs + t * ldv + col));
+        part[(t - m0) >> 3 & 1] += v0 * o2.x + v1 * o2.y;
+      });
+      racc_add(m0, part[0], part[1]);
+    });
+  }
+  __syncthreads();  // dX, P / dP sums
   if (d.dq) {
     tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
@@ -561,13 +565,24 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
       });
       acc.zero();
       mma_acc<1, NI, false, true>(acc, dOs, ldv, Ss, ldv, m0, n0, V);
-      acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
+      float part[2] = {0.f, 0.f};
+      acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
+        const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Qs + t * ldk + col));
+        part[(t - m0) >> 3 & 1] += v0 * q2.x + v1 * q2.y;
+        const float e = __expf(G[t]);
+        v0 *= e;
+        v1 *= e;
+      });
+      racc_add(m0, part[0], part[1]);
       tc::mma_acc3<1, NI, false, false>(acc, dXh, dXl, LDT, Ks, nullptr, ldk, m0, n0, C);
       acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
         if (t < c) st2(d.dq + row(u, T, t0 + t) * K + col, dq[p].x + v0, dq[p].y + v1);
       });
     });
+    __syncthreads();  // racc
   }
+  for (int t = threadIdx.x; t < c; t += blockDim.x)
+    d.sc_dG[row(u, T, t0 + t)] = __expf(G[t]) * racc[t] + rs[t] - cs[t];
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
