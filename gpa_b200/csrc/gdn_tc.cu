@@ -664,12 +664,13 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
   auto get_slice = [&](float* dst) {
     for (int i = threadIdx.x; i < K * q4; i += blockDim.x) {
       const int k = i / q4, j = (i - k * q4) << 2, o = k * lds + j;
-      float4 x;
-      x.x = __bfloat162float(Dh[o]) + __bfloat162float(Dl[o]);
-      x.y = __bfloat162float(Dh[o + 1]) + __bfloat162float(Dl[o + 1]);
-      x.z = __bfloat162float(Dh[o + 2]) + __bfloat162float(Dl[o + 2]);
-      x.w = __bfloat162float(Dh[o + 3]) + __bfloat162float(Dl[o + 3]);
-      *reinterpret_cast<float4*>(dst + (int64_t)k * V + v0 + j) = x;
+      const uint2 h = *reinterpret_cast<const uint2*>(Dh + o), l = *reinterpret_cast<const uint2*>(Dl + o);
+      const float2 h01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h.x));
+      const float2 h23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h.y));
+      const float2 l01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&l.x));
+      const float2 l23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&l.y));
+      *reinterpret_cast<float4*>(dst + (int64_t)k * V + v0 + j) =
+          make_float4(h01.x + l01.x, h01.y + l01.y, h23.x + l23.x, h23.y + l23.y);
     }
   };
   __syncthreads();
