@@ -42,10 +42,10 @@ CFG = dict(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_
 BATCH, LENGTH = 8, 8192
 CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
 # DRAM bytes moved per algorithmic byte, measured with ncu on a small case of the same kernel
-# (profiles/tc_bwd_chunk_small.md: 254.9 MB over 1024 blocks of (K, V) = (64, 64) scans and
-# 189.9 MB over 512 blocks of (128, 64), against 247.0 and 361.7 KB of algorithmic bytes per
+# (profiles/tc_bwd_chunk_small.md: 246.4 MB over 1024 blocks of (K, V) = (64, 64) scans and
+# 183.1 MB over 512 blocks of (128, 64), against 238.8 and 353.5 KB of algorithmic bytes per
 # block); the traffic of a full launch is its algorithmic bytes times this ratio.
-TRAFFIC_RATIO = {"tc_bwd_chunk": 1.02}
+TRAFFIC_RATIO = {"tc_bwd_chunk": 1.01}
 
 
 def peaks():
