@@ -136,13 +136,14 @@ def kernel_bytes(cfg, units, length):
 
     tc_bwd_chunk, per block of c tokens of a (K, V) scan: reads k, Wk, the dk partial and the
     accumulated dk (c K each, fp32), dW, U, v and the accumulated dv (c V each, fp32), W (c V,
-    bf16), the state snapshot S and its gradient D (K V each, fp32), A and T (c^2 each, fp32),
-    and the gates and the dG partial (3 c); writes dk (c K), dv (c V), dg and dbeta (2 c).
+    bf16), the state snapshot S and its gradient D (K V each, fp32), T (c^2, fp32; A is formed
+    again from k), and the gates and the dG partial (3 c); writes dk (c K), dv (c V), dg and
+    dbeta (2 c).
     """
     c = cfg["chunk_size"]
     nb = -(-length // c)
     inner, outer, rel = gdn_scans(cfg)
-    per = sum(4 * (2 * K * V + 2 * c * c + 5 * c * K + 5 * c * V + 5 * c) + 2 * c * V
+    per = sum(4 * (2 * K * V + c * c + 5 * c * K + 5 * c * V + 5 * c) + 2 * c * V
               for K, V in inner + outer + rel)
     return {"tc_bwd_chunk": units * nb * per}
 

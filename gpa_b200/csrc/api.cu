@@ -174,9 +174,10 @@ struct Saved {
   // chunk WY terms of every scan (U = T diag(b) V, Wk = T diag(b e^G) K), kept for the backward
   float *UA[kMaxLevels], *KA[kMaxLevels], *UB[kMaxLevels], *KB[kMaxLevels];
   float *UR[kMaxEdges], *KR[kMaxEdges];
-  // A and T = (I + A)^-1 of every block of every scan (tensor-core path only)
-  float *AA[kMaxLevels], *TA[kMaxLevels], *AB[kMaxLevels], *TB[kMaxLevels];
-  float *AR[kMaxEdges], *TR[kMaxEdges];
+  // T = (I + A)^-1 of every block of every scan (tensor-core path only; the backward forms A
+  // again from K and the gates, exactly as the forward did)
+  float *TA[kMaxLevels], *TB[kMaxLevels];
+  float *TR[kMaxEdges];
   size_t bytes;
 };
 
@@ -239,13 +240,10 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
   }
   const size_t nAT = g.fast ? (size_t)g.U * g.bl.nb * kMaxChunk * kMaxChunk : 0;
   for (int j = 0; j < g.L; ++j) {
-    s->AA[j] = g.fast ? b.take(nAT) : nullptr;
     s->TA[j] = g.fast ? b.take(nAT) : nullptr;
-    s->AB[j] = g.fast ? b.take(nAT) : nullptr;
     s->TB[j] = g.fast ? b.take(nAT) : nullptr;
   }
   for (int e = 0; e < g.E; ++e) {
-    s->AR[e] = g.fast ? b.take(nAT) : nullptr;
     s->TR[e] = g.fast ? b.take(nAT) : nullptr;
   }
   s->bytes = b.off + 256;
@@ -412,7 +410,6 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     in.W = s.WA[j];
     in.Ub = s.UA[j];
     in.Wk = s.KA[j];
-    in.Asv = s.AA[j];
     in.Tsv = s.TA[j];
     in.O = s.raw[j];
     in.S_final = so->inner[j];
@@ -430,7 +427,6 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
     ou.W = s.WB[j];
     ou.Ub = s.UB[j];
     ou.Wk = s.KB[j];
-    ou.Asv = s.AB[j];
     ou.Tsv = s.TB[j];
     ou.S_final = so->outer[j];
     CK(gdn_forward(sb, U, bl, true, st));
@@ -469,7 +465,6 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
       d.W = s.WR[e];
       d.Ub = s.UR[e];
       d.Wk = s.KR[e];
-      d.Asv = s.AR[e];
       d.Tsv = s.TR[e];
       d.O = s.msg[e];
       d.S_final = so->relation[e];
@@ -653,7 +648,6 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
       d.W = s.WR[e];
       d.Ub = s.UR[e];
       d.Wk = s.KR[e];
-      d.Asv = s.AR[e];
       d.Tsv = s.TR[e];
       d.dO = x.dmsg[e];
       d.dS_final = ds.relation[e];
@@ -749,7 +743,6 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     in.W = s.WA[j];
     in.Ub = s.UA[j];
     in.Wk = s.KA[j];
-    in.Asv = s.AA[j];
     in.Tsv = s.TA[j];
     in.dO = x.draw;
     in.ext = x.extA;
@@ -775,7 +768,6 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     ou = outer_desc(j);
     ou.Ub = s.UB[j];
     ou.Wk = s.KB[j];
-    ou.Asv = s.AB[j];
     ou.Tsv = s.TB[j];
     ou.ext = x.extB;
     ou.dS_final = ds.outer[j];

@@ -69,7 +69,6 @@ struct ScanDesc {
   float* sc_db;           // [U,T]   scratch (zeroed)
   float* sc_dA;           // [U,NB,64,64] scratch (zeroed)
   float* Dend;            // [U,NB,K,V] dS at each block end
-  float* Asv;             // [U,NB,64,64] A of every block (tensor-core path; forward writes)
   float* Tsv;             // [U,NB,64,64] T = (I + A)^-1 of every block (same)
 };
 

@@ -193,8 +193,6 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
   __syncthreads();
-  float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) As[i] = A[(i / C) * kAStride + (i % C)];
   invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
   float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) Ts[i] = Tm[(i / C) * kAStride + (i % C)];
@@ -740,14 +738,15 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
 struct LBwdChunk {
   // T (hi/lo) and the per-token vectors are fixed; a pool X holds, stage by stage,
   //   1 state terms: dWh, dWl, Sb, Db, Wb   2 U path: dWh, dWl, Uh, Ul
-  //   3 Wk path: Wkh, Wkl, dWkh, dWkl       4 dA: Mh, Ml, Mmb, A, Ks, Kl
+  //   3 Wk path: Wkh, Wkl, dWkh, dWkl       4 dA: Mh, Ml, Mmb, Ks, Kl (A = b e^G K K^T is
+  //   recomputed in the dA epilogue exactly as the forward formed it)
   // so that every shape with K, V <= 128 but (128, 128) fits two CTAs per SM.
   size_t Th, Tl, G, bt, dG, db, dlam, rw, red, X, total;
-  size_t dWh, dWl, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mh, Ml, dAf, A, Ks, Kl, Mmb;
+  size_t dWh, dWl, Sb, Db, Wb, Uh, Ul, Wkh, Wkl, dWkh, dWkl, Mh, Ml, dAf, Ks, Kl, Mmb;
   __host__ __device__ LBwdChunk(int K, int V) {
     Carve c;
     const size_t sK = 2 * C * ld16(K), sV = 2 * C * ld16(V), sS = 2 * K * ld16(V);
-    const size_t sA = 4 * C * kAStride, sT = 2 * C * LDT;
+    const size_t sT = 2 * C * LDT;
     Th = c.take(sT);
     Tl = c.take(sT);
     G = c.take(4 * C);
@@ -772,8 +771,7 @@ struct LBwdChunk {
     dWkl = s3.take(sK);
     Mh = s4.take(sT);
     Ml = s4.take(sT);
-    dAf = s4.take(sA);
-    A = s4.take(sA);
+    dAf = s4.take(sT);  // Mmb
     Ks = s4.take(sK);
     Kl = s4.take(sK);
     size_t pool = s1.off;
@@ -782,7 +780,7 @@ struct LBwdChunk {
     pool = pool > s4.off ? pool : s4.off;
     X = c.take(pool);
     size_t* const in_pool[] = {&dWh, &dWl, &Sb, &Db, &Wb, &Uh, &Ul, &Wkh, &Wkl,
-                               &dWkh, &dWkl, &Mh, &Ml, &dAf, &A, &Ks, &Kl};
+                               &dWkh, &dWkl, &Mh, &Ml, &dAf, &Ks, &Kl};
     for (size_t* q : in_pool) *q += X;
     Mmb = dAf;  // the dA epilogue writes Mm while other warps still read Mh, Ml
     total = c.off;
@@ -807,7 +805,6 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   bf16* Kl = (bf16*)(smem + L.Kl);
   bf16* Th = (bf16*)(smem + L.Th);
   bf16* Tl = (bf16*)(smem + L.Tl);
-  float* A = (float*)(smem + L.A);
   bf16* Mh = (bf16*)(smem + L.Mh);
   bf16* Ml = (bf16*)(smem + L.Ml);
   float* G = (float*)(smem + L.G);
@@ -994,17 +991,8 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     rw[t] = dlam[t] = 0.f;  // reused below for the row / column sums of dA o A
   }
   {
-    const float* As = d.Asv + ((int64_t)u * bl.nb + n) * C * C;
     const TileJob jobs[] = {tc::job(Ks, Kl, ldk, d.k + r0 * K, K, c, K, C)};
     tc::load_tiles(jobs);
-    for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
-      const float4 a = *reinterpret_cast<const float4*>(As + 4 * i);
-      float* dst = A + (4 * i / C) * kAStride + (4 * i) % C;
-      dst[0] = a.x;
-      dst[1] = a.y;
-      dst[2] = a.z;
-      dst[3] = a.w;
-    }
   }
 #pragma unroll
   for (int i = 0; i < kMT; ++i) {
@@ -1016,17 +1004,24 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   }
   __syncthreads();
   // dA = -T^T M (strictly lower, real rows), straight from the accumulators: the row and
-  // column sums of dA o A (into rw, dlam) and Mm = dA o b_t e^{G_t - G_s} (bf16, into Mmb)
+  // column sums of dA o A (into rw, dlam) and Mm = dA o b_t e^{G_t - G_s} (bf16, into Mmb).
+  // A = b_t e^{G_t - G_s} k_t.k_s of the same tile is formed again beside it (the forward's
+  // tc_build_a product on the same split K tiles: the same values).
   float* rsum = rw;
   float* csum = dlam;
   for_tiles<1, 1>(C, C, [&](int m0, int n0) {
-    Acc<1, 1> acc;
+    Acc<1, 1> acc, ak;
     acc.zero();
+    ak.zero();
     tc::mma_acc3<1, 1, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
+    tc::mma_acc3<1, 1, false, true>(ak, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
     float rp[2] = {0.f, 0.f}, cp[2][2] = {};
     acc.each2(m0, n0, [&](int p, int t, int s, float& v0, float& v1) {
       const float d0 = (s < t && t < c) ? -v0 : 0.f, d1 = (s + 1 < t && t < c) ? -v1 : 0.f;
-      const float p0 = d0 * A[t * kAStride + s], p1 = d1 * A[t * kAStride + s + 1];
+      const float k0 = ak.v[0][p >> 1][2 * (p & 1)], k1 = ak.v[0][p >> 1][2 * (p & 1) + 1];
+      const float a0 = bt[t] * (s < t ? __expf(G[t] - G[s]) * k0 : 0.f);
+      const float a1 = bt[t] * (s + 1 < t ? __expf(G[t] - G[s + 1]) * k1 : 0.f);
+      const float p0 = d0 * a0, p1 = d1 * a1;
       rp[(t - m0) >> 3] += p0 + p1;
       cp[(p >> 1) & 1][0] += p0;
       cp[(p >> 1) & 1][1] += p1;
