@@ -923,7 +923,7 @@ __global__ void __launch_bounds__(512, 2) tk_prep_bwd(int U, int T, int H, int D
 
 constexpr int kOTile = 64;     // output tile (P and Q)
 constexpr int kORows = 64;     // token rows per step
-constexpr int kOSplit = 4096;  // tokens per CTA
+constexpr int kOSplit = 2048;  // tokens per CTA
 
 struct LOuter {
   size_t Xh, Xl, Yh, Yl, total;
