@@ -1121,11 +1121,12 @@ cudaError_t tc_launch(const char* name, Kern k, dim3 grid, size_t smem, cudaStre
 // Launch one kernel per group of scans with the same (K, V): each group gets the shared
 // memory its own shape needs, so narrow scans fit more CTAs per SM.
 // gx: CTAs per scan along x; with `sliced`, times the state slices of the group's shape.
-// With `halve`, a group whose layout fits two CTAs per SM (113 KB) runs 256 threads per CTA.
+// A group whose layout is at most `half_kb` KB runs 256 threads per CTA (0: never): at
+// 113 KB two such CTAs share an SM, at 74 KB three (more CTAs in flight than two of 512).
 template <class Lay, class Kern>
 cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& b, int U,
                              const Blocks& bl, cudaStream_t st, bool sliced = false,
-                             bool halve = false) {
+                             int half_kb = 0) {
   bool done[kMaxScans] = {};
   for (int i = 0; i < b.n; ++i) {
     if (done[i]) continue;
@@ -1141,7 +1142,7 @@ cudaError_t tc_launch_groups(const char* name, Kern k, int gx, const ScanBatch& 
     const int x = sliced ? gx * state_slices(K, V) : gx;
     const size_t smem = Lay(K, V).total;
     const int threads =
-        sliced ? kStateThreads : (halve && smem <= 113 * 1024 ? kThreads / 2 : kThreads);
+        sliced ? kStateThreads : (smem <= (size_t)half_kb * 1024 ? kThreads / 2 : kThreads);
     const cudaError_t e = tc_launch(name, k, dim3(x, sub.n), smem, st, sub, U, bl, threads);
     if (e != cudaSuccess) return e;
   }
@@ -1156,7 +1157,8 @@ bool tc_supported(int K, int V) {
 
 cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
                        cudaStream_t st) {
-  cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st);
+  cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st,
+                                              false, 74);
   if (e != cudaSuccess) return e;
   e = tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess || !with_output) return e;
@@ -1164,7 +1166,7 @@ cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_ou
 }
 
 cudaError_t tc_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  return tc_launch_groups<LFwdOut>("tc_fwd_out", tc_fwd_out, U * bl.nb, b, U, bl, st);
+  return tc_launch_groups<LFwdOut>("tc_fwd_out", tc_fwd_out, U * bl.nb, b, U, bl, st, false, 74);
 }
 
 cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
@@ -1176,7 +1178,7 @@ cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaSt
   cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess) return e;
   return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st,
-                                     false, true);
+                                     false, 113);
 }
 
 }  // namespace gpa
