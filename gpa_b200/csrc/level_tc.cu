@@ -921,86 +921,99 @@ __global__ void __launch_bounds__(512, 2) tk_prep_bwd(int U, int T, int H, int D
 
 // -------------------------------------------- parameter-gradient reductions
 
-constexpr int kOTile = 64;     // output tile (P and Q)
+constexpr int kOTile = 64;     // output tile unit (P and Q)
 constexpr int kORows = 64;     // token rows per step
-constexpr int kOSplit = 2048;  // tokens per CTA
+constexpr int kOSplit = 2048;  // tokens per CTA of a 64 x 64 output tile
 
+// out[h] (P x Q) += cscale * scale[h] * sum_{b,t} X^T Y over the rows of head h; P, Q
+// multiples of 16.  Operands are hi/lo bf16 pairs (sums run over every token).  A CTA owns a
+// (64 WP) x (64 WQ) output tile, WP * WQ <= 2: wide X or Y operands are read by fewer CTAs
+// (a 128 x 64 tile reads 192 values per token where two 64 x 64 tiles read 256).
+template <int WP, int WQ>
 struct LOuter {
   size_t Xh, Xl, Yh, Yl, total;
   __host__ __device__ LOuter(int, int, int) {
     Carve c;
-    Xh = c.take(2 * kORows * ld16(kOTile));
-    Xl = c.take(2 * kORows * ld16(kOTile));
-    Yh = c.take(2 * kORows * ld16(kOTile));
-    Yl = c.take(2 * kORows * ld16(kOTile));
+    Xh = c.take(2 * kORows * ld16(kOTile * WP));
+    Xl = c.take(2 * kORows * ld16(kOTile * WP));
+    Yh = c.take(2 * kORows * ld16(kOTile * WQ));
+    Yl = c.take(2 * kORows * ld16(kOTile * WQ));
     total = c.off;
   }
 };
 
-// out[h] (P x Q) += cscale * scale[h] * sum_{b,t} X^T Y over the rows of head h; P, Q
-// multiples of 16.  Operands are hi/lo bf16 pairs (sums run over every token).
-__global__ void __launch_bounds__(256) tk_head_outer(int B, int T, int H, const float* X, int P,
-                                                     int xmode, const float* Y, int Q,
-                                                     const float* scale, int64_t scale_stride,
-                                                     float cscale, float* out) {
+template <int WP, int WQ>
+__global__ void __launch_bounds__(256, 2) tk_head_outer(int B, int T, int H, const float* X,
+                                                        int P, int xmode, const float* Y, int Q,
+                                                        const float* scale,
+                                                        int64_t scale_stride, float cscale,
+                                                        float* out, int split) {
+  constexpr int TP = kOTile * WP, TQ = kOTile * WQ;
   const int h = blockIdx.x;
-  const int tq = (Q + kOTile - 1) / kOTile;
-  const int p0 = (blockIdx.y / tq) * kOTile, q0 = (blockIdx.y % tq) * kOTile;
-  const int pw = min(kOTile, P - p0), qw = min(kOTile, Q - q0);
+  const int tq = (Q + TQ - 1) / TQ;
+  const int p0 = (blockIdx.y / tq) * TP, q0 = (blockIdx.y % tq) * TQ;
+  const int pw = min(TP, P - p0), qw = min(TQ, Q - q0);
   const int64_t total = (int64_t)B * T;
-  const int64_t r0 = (int64_t)blockIdx.z * kOSplit;
-  const int64_t r1 = min(total, r0 + kOSplit);
+  const int64_t r0 = (int64_t)blockIdx.z * split;
+  const int64_t r1 = min(total, r0 + split);
   extern __shared__ __align__(16) unsigned char smem[];
-  const LOuter Lo(0, 0, 0);
+  const LOuter<WP, WQ> Lo(0, 0, 0);
   bf16* Xh = (bf16*)(smem + Lo.Xh);
   bf16* Xl = (bf16*)(smem + Lo.Xl);
   bf16* Yh = (bf16*)(smem + Lo.Yh);
   bf16* Yl = (bf16*)(smem + Lo.Yl);
-  const int lo = ld16(kOTile);
-  // the 64x64 output tile is 16 16x16 tiles; warp w owns tiles w and w + 8
+  const int lx = ld16(TP), ly = ld16(TQ);
+  // the output tile is (TP / 16) x (TQ / 16) tiles of 16 x 16; warp w owns tiles w + 8 i
+  constexpr int kT = 2 * WP * WQ, kTN = TQ / 16;
   const int w = threadIdx.x >> 5;
-  Acc<1, 1> acc[2];
-  int tm[2], tn[2];
-  bool act[2];
+  Acc<1, 1> acc[kT];
+  int tm[kT], tn[kT];
+  bool act[kT];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < kT; ++i) {
     const int idx = w + 8 * i;
-    tm[i] = (idx >> 2) * 16;
-    tn[i] = (idx & 3) * 16;
+    tm[i] = (idx / kTN) * 16;
+    tn[i] = (idx % kTN) * 16;
     act[i] = tm[i] < pw && tn[i] < qw;
     acc[i].zero();
   }
-  // Each thread moves 4 float4 of X and 4 of Y per 64-row step; the next step's values are
-  // loaded into registers while the current step's MMAs run.
-  constexpr int kPer = kORows * (kOTile / 4) / 256;
-  float4 xn[kPer], yn[kPer];
+  // Each thread moves 4 WP float4 of X and 4 WQ of Y per 64-row step; the next step's values
+  // are loaded into registers while the current step's MMAs run.
+  constexpr int kPX = kORows * (TP / 4) / 256, kPY = kORows * (TQ / 4) / 256;
+  float4 xn[kPX], yn[kPY];
   auto fetch = [&](int64_t rr) {
     const int rows = (int)min((int64_t)kORows, r1 - rr);
     const int b0 = (int)(rr / T), t0 = (int)(rr - (int64_t)b0 * T);  // one division per step
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int i = threadIdx.x + j * 256;
-      const int rw = i / (kOTile / 4), cc = (i % (kOTile / 4)) * 4;
-      xn[j] = yn[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (rw < rows) {
-        int b = b0, t = t0 + rw;
-        while (t >= T) {  // rows of a step cross at most a few sequence ends
-          t -= T;
-          ++b;
-        }
-        const int64_t o = row(b * H + h, T, t);
-        if (cc < pw) xn[j] = *reinterpret_cast<const float4*>(X + o * P + p0 + cc);
-        if (cc < qw) yn[j] = *reinterpret_cast<const float4*>(Y + o * Q + q0 + cc);
+    auto at = [&](int rw) {  // token row of step row rw (rows of a step cross few sequence ends)
+      int b = b0, t = t0 + rw;
+      while (t >= T) {
+        t -= T;
+        ++b;
       }
+      return row(b * H + h, T, t);
+    };
+#pragma unroll
+    for (int j = 0; j < kPX; ++j) {
+      const int i = threadIdx.x + j * 256;
+      const int rw = i / (TP / 4), cc = (i % (TP / 4)) * 4;
+      xn[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rw < rows && cc < pw) xn[j] = *reinterpret_cast<const float4*>(X + at(rw) * P + p0 + cc);
+    }
+#pragma unroll
+    for (int j = 0; j < kPY; ++j) {
+      const int i = threadIdx.x + j * 256;
+      const int rw = i / (TQ / 4), cc = (i % (TQ / 4)) * 4;
+      yn[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rw < rows && cc < qw) yn[j] = *reinterpret_cast<const float4*>(Y + at(rw) * Q + q0 + cc);
     }
   };
   if (r0 < r1) fetch(r0);
   for (int64_t rr = r0; rr < r1; rr += kORows) {
     __syncthreads();  // the previous step's MMAs are done with the tiles
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
+    for (int j = 0; j < kPX; ++j) {
       const int i = threadIdx.x + j * 256;
-      const int rw = i / (kOTile / 4), cc = (i % (kOTile / 4)) * 4;
+      const int rw = i / (TP / 4), cc = (i % (TP / 4)) * 4;
       float4 xv = xn[j];
       if (xmode == 1) {
         xv.x = gelu(xv.x);
@@ -1008,20 +1021,25 @@ __global__ void __launch_bounds__(256) tk_head_outer(int B, int T, int H, const 
         xv.z = gelu(xv.z);
         xv.w = gelu(xv.w);
       }
-      tc::put4(Xh, Xl, rw * lo + cc, xv);
-      tc::put4(Yh, Yl, rw * lo + cc, yn[j]);
+      tc::put4(Xh, Xl, rw * lx + cc, xv);
+    }
+#pragma unroll
+    for (int j = 0; j < kPY; ++j) {
+      const int i = threadIdx.x + j * 256;
+      const int rw = i / (TQ / 4), cc = (i % (TQ / 4)) * 4;
+      tc::put4(Yh, Yl, rw * ly + cc, yn[j]);
     }
     __syncthreads();
     if (rr + kORows < r1) fetch(rr + kORows);
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < kT; ++i)
       if (act[i])
-        tc::mma_acc3<1, 1, true, false>(acc[i], Xh, Xl, lo, Yh, Yl, lo, tm[i], tn[i], kORows);
+        tc::mma_acc3<1, 1, true, false>(acc[i], Xh, Xl, lx, Yh, Yl, ly, tm[i], tn[i], kORows);
   }
   const float s = cscale * (scale ? scale[(int64_t)h * scale_stride] : 1.f);
   float* o = out + (int64_t)h * P * Q;
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < kT; ++i)
     if (act[i])
       acc[i].each(tm[i], tn[i], [&](int p, int q, float& v) {
         atomicAdd(&o[(p0 + p) * Q + q0 + q], s * v);
@@ -1126,10 +1144,20 @@ cudaError_t tc_head_outer(int B, int T, int H, const float* X, int P, int xmode,
                           int Q, const float* scale, int64_t scale_stride, float cscale,
                           float* out, cudaStream_t st) {
   const int64_t total = (int64_t)B * T;
-  const int tp = (P + kOTile - 1) / kOTile, tq = (Q + kOTile - 1) / kOTile;
-  dim3 grid(H, tp * tq, (unsigned)((total + kOSplit - 1) / kOSplit));
-  return tk_launch("tc_head_outer", tk_head_outer, grid, smem_of<LOuter>(0, 0, 0), st, B, T, H,
-                   X, P, xmode, Y, Q, scale, scale_stride, cscale, out);
+  // the wider operand gets the 128-wide side of the CTA tile; half the tokens per CTA keep
+  // the CTA count (and its work) as with 64 x 64 tiles
+  const int wp = P >= 2 * kOTile && P >= Q ? 2 : 1, wq = wp == 1 && Q >= 2 * kOTile ? 2 : 1;
+  const int split = kOSplit / (wp * wq);
+  const int tp = (P + kOTile * wp - 1) / (kOTile * wp), tq = (Q + kOTile * wq - 1) / (kOTile * wq);
+  dim3 grid(H, tp * tq, (unsigned)((total + split - 1) / split));
+  if (wp == 2)
+    return tk_launch("tc_head_outer", tk_head_outer<2, 1>, grid, smem_of<LOuter<2, 1>>(0, 0, 0), st,
+                     B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, split);
+  if (wq == 2)
+    return tk_launch("tc_head_outer", tk_head_outer<1, 2>, grid, smem_of<LOuter<1, 2>>(0, 0, 0), st,
+                     B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, split);
+  return tk_launch("tc_head_outer", tk_head_outer<1, 1>, grid, smem_of<LOuter<1, 1>>(0, 0, 0), st,
+                   B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, split);
 }
 
 }  // namespace gpa
