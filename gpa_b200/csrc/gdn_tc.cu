@@ -106,25 +106,55 @@ GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
     for (int r = 0; r < 16; ++r) Tm[(b0 + r) * kAStride + b0 + j] = x[r];
   }
   __syncthreads();
+  // Off-diagonal 16 x 16 blocks by distance dd = ib - jb: Xs_jb = sum_{jb <= kb < ib}
+  // A[ib][kb] T[kb][jb], then T[ib][jb] = -T[ib][ib] Xs_jb.  A lane computes rows r and r + 8,
+  // columns c .. c + 3 of a block: 6 shared loads per 8 FMAs (one warp per block).
   for (int dd = 1; dd < 4; ++dd) {
     const int nblk = 4 - dd;
-    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
-      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
-      float s = 0.f;
-      for (int kb = jb; kb < ib; ++kb)
+    if (w < nblk) {
+      const int jb = w, ib = jb + dd, r = lane >> 2, c = (lane & 3) << 2;
+      float x[2][4] = {};
+      for (int kb = jb; kb < ib; ++kb) {
+        const float* a0 = A + (16 * ib + r) * kAStride + 16 * kb;
+        const float* t = Tm + (16 * kb) * kAStride + 16 * jb + c;
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-          s += A[(16 * ib + r) * kAStride + 16 * kb + q] * Tm[(16 * kb + q) * kAStride + 16 * jb + cc];
-      Xs[e] = s;
+        for (int q = 0; q < 16; ++q) {
+          const float u0 = a0[q], u1 = a0[8 * kAStride + q];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float tv = t[q * kAStride + k];
+            x[0][k] = fmaf(u0, tv, x[0][k]);
+            x[1][k] = fmaf(u1, tv, x[1][k]);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        Xs[(jb << 8) + (r << 4) + c + k] = x[0][k];
+        Xs[(jb << 8) + ((r + 8) << 4) + c + k] = x[1][k];
+      }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
-      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
-      float s = 0.f;
+    if (w < nblk) {
+      const int jb = w, ib = jb + dd, r = lane >> 2, c = (lane & 3) << 2;
+      const float* d0 = Tm + (16 * ib + r) * kAStride + 16 * ib;
+      const float* xs = Xs + (jb << 8) + c;
+      float y[2][4] = {};
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        s += Tm[(16 * ib + r) * kAStride + 16 * ib + q] * Xs[(jb << 8) + (q << 4) + cc];
-      Tm[(16 * ib + r) * kAStride + 16 * jb + cc] = -s;
+      for (int q = 0; q < 16; ++q) {
+        const float u0 = d0[q], u1 = d0[8 * kAStride + q];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float xv = xs[(q << 4) + k];
+          y[0][k] = fmaf(u0, xv, y[0][k]);
+          y[1][k] = fmaf(u1, xv, y[1][k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        Tm[(16 * ib + r) * kAStride + 16 * jb + c + k] = -y[0][k];
+        Tm[(16 * ib + r + 8) * kAStride + 16 * jb + c + k] = -y[1][k];
+      }
     }
     __syncthreads();
   }
