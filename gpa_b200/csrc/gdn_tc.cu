@@ -163,7 +163,11 @@ GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
 // A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
 GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
                         const float* bt, float* A, float* Atil) {
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+  // only the 10 of 16 tiles on or below the diagonal: the upper ones are never read
+  static_assert(C == 64, "4 x 4 tiles of 16 x 16");
+  for (int i = threadIdx.x >> 5; i < 10; i += blockDim.x >> 5) {
+    const int mi = i < 1 ? 0 : i < 3 ? 1 : i < 6 ? 2 : 3;
+    const int m0 = 16 * mi, n0 = 16 * (i - mi * (mi + 1) / 2);
     Acc<1, 1> acc;
     acc.zero();
     tc::mma_acc3<1, 1, false, true>(acc, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
@@ -172,7 +176,7 @@ GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const fl
       A[t * kAStride + s] = bt[t] * at;
       if (Atil) Atil[t * kAStride + s] = at;
     });
-  });
+  }
 }
 
 // ------------------------------------------------------------------ forward
