@@ -160,14 +160,21 @@ GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
   }
 }
 
-// A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
-GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
-                        const float* bt, float* A, float* Atil) {
-  // only the 10 of 16 tiles on or below the diagonal: the upper ones are never read
+// The 10 of the 4 x 4 tiles (16 x 16) of a 64 x 64 block on or below the diagonal, round-robin
+// over the warps: body(m0, n0).  A product with a lower-triangular block operand reads no other.
+template <class Body>
+GPA_DEV void for_lower_tiles(Body body) {
   static_assert(C == 64, "4 x 4 tiles of 16 x 16");
   for (int i = threadIdx.x >> 5; i < 10; i += blockDim.x >> 5) {
     const int mi = i < 1 ? 0 : i < 3 ? 1 : i < 6 ? 2 : 3;
-    const int m0 = 16 * mi, n0 = 16 * (i - mi * (mi + 1) / 2);
+    body(16 * mi, 16 * (i - mi * (mi + 1) / 2));
+  }
+}
+
+// A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
+GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
+                        const float* bt, float* A, float* Atil) {
+  for_lower_tiles([&](int m0, int n0) {  // the upper tiles are never read
     Acc<1, 1> acc;
     acc.zero();
     tc::mma_acc3<1, 1, false, true>(acc, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
@@ -176,7 +183,7 @@ GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const fl
       A[t * kAStride + s] = bt[t] * at;
       if (Atil) Atil[t * kAStride + s] = at;
     });
-  }
+  });
 }
 
 // ------------------------------------------------------------------ forward
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Vs, nullptr, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Vs, nullptr, ldv, m0, n0, m0 + 16);
     acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
       if (t < c) st2(d.Ub + row(u, T, t0 + t) * V + col, v0, v1);
     });
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Ks, Kl, ldk, m0, n0, C);
+    tc::mma_acc3<1, NI, false, false>(acc, Fh, Fl, LDT, Ks, Kl, ldk, m0, n0, m0 + 16);
     acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
       if (t < c) st2(d.Wk + row(u, T, t0 + t) * K + col, v0, v1);
     });
@@ -435,7 +442,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, nullptr);
   }
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+  for_lower_tiles([&](int m0, int n0) {  // P is lower triangular
     Acc<1, 1> acc;
     acc.zero();
     mma_acc<1, 1, false, true>(acc, Qs, ldk, Ks, ldk, m0, n0, K);
@@ -451,7 +458,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_out(ScanBatch b, int U, Block
     acc.zero();
     mma_acc<1, NI, false, false>(acc, Qs, ldk, Ss, ldv, m0, n0, K);
     acc.each(m0, n0, [&](int t, int, float& v) { v *= __expf(G[t]); });
-    tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, nullptr, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, false, false>(acc, Ph, Pl, LDT, Wh, nullptr, ldv, m0, n0, m0 + 16);
     acc.each2(m0, n0, [&](int, int t, int col, float& v0, float& v1) {
       if (t < c) st2(d.O + row(u, T, t0 + t) * V + col, v0, v1);
     });
@@ -518,8 +525,9 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
     gate_finish(gr, c, G, nullptr);
   }
   // P = (Q K^T) o Gamma and dP = dO W^T on the same tile: rowsum / colsum of P o dP and
-  // dX = dP o Gamma straight from the accumulators
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+  // dX = dP o Gamma straight from the accumulators (both lower triangular: the products
+  // below read no upper tile of P or dX)
+  for_lower_tiles([&](int m0, int n0) {
     Acc<1, 1> pa, da;
     pa.zero();
     mma_acc<1, 1, false, true>(pa, Qs, ldk, Ks, ldk, m0, n0, K);
@@ -606,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
         v1 *= e;
       });
       racc_add(m0, part[0], part[1]);
-      tc::mma_acc3<1, NI, false, false>(acc, dXh, dXl, LDT, Ks, nullptr, ldk, m0, n0, C);
+      tc::mma_acc3<1, NI, false, false>(acc, dXh, dXl, LDT, Ks, nullptr, ldk, m0, n0, m0 + 16);
       acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
         if (t < c) st2(d.dq + row(u, T, t0 + t) * K + col, dq[p].x + v0, dq[p].y + v1);
       });
@@ -618,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
   tiles_n<1, 2>(C, K, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, dXh, dXl, LDT, Qs, nullptr, ldk, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, dXh, dXl, LDT, Qs, nullptr, ldk, m0, n0, C, m0);
     acc.each2(m0, n0, [&](int, int s, int col, float& v0, float& v1) {
       if (s < c) st2(d.sc_dK + row(u, T, t0 + s) * K + col, v0, v1);
     });
@@ -626,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_bwd_local(ScanBatch b, int U, 
   tiles_n<1, 2>(C, V, [&]<int NI>(int m0, int n0) {
     Acc<1, NI> acc;
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, Ph, Pl, LDT, dOs, nullptr, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Ph, Pl, LDT, dOs, nullptr, ldv, m0, n0, C, m0);
     acc.each2(m0, n0, [&](int, int s, int col, float& v0, float& v1) {
       if (s < c) st2(d.sc_dW + row(u, T, t0 + s) * V + col, v0, v1);
     });
@@ -950,7 +958,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       if (t < c) vv[p] = ld2(d.v + (r0 + t) * V + col);
     });
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWh, dWl, ldv, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWh, dWl, ldv, m0, n0, C, m0);  // T^T: upper
     float part[2] = {0.f, 0.f};
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) {
@@ -994,7 +1002,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       }
     });
     acc.zero();
-    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWkh, dWkl, ldk, m0, n0, C);
+    tc::mma_acc3<1, NI, true, false>(acc, Th, Tl, LDT, dWkh, dWkl, ldk, m0, n0, C, m0);
     float part[2] = {0.f, 0.f};
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) {
@@ -1041,13 +1049,15 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
   // column sums of dA o A (into rw, dlam) and Mm = dA o b_t e^{G_t - G_s} (bf16, into Mmb).
   // A = b_t e^{G_t - G_s} k_t.k_s of the same tile is formed again beside it (the forward's
   // tc_build_a product on the same split K tiles: the same values).
+  // Only the 10 tiles on or below the diagonal are formed (T^T is upper triangular: the
+  // product for row tile m0 runs over k >= m0); the dK products below read no upper tile of Mm.
   float* rsum = rw;
   float* csum = dlam;
-  for_tiles<1, 1>(C, C, [&](int m0, int n0) {
+  for_lower_tiles([&](int m0, int n0) {
     Acc<1, 1> acc, ak;
     acc.zero();
     ak.zero();
-    tc::mma_acc3<1, 1, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C);
+    tc::mma_acc3<1, 1, true, false>(acc, Th, Tl, LDT, Mh, Ml, LDT, m0, n0, C, m0);
     tc::mma_acc3<1, 1, false, true>(ak, Ks, Kl, ldk, Ks, Kl, ldk, m0, n0, K);
     float rp[2] = {0.f, 0.f}, cp[2][2] = {};
     acc.each2(m0, n0, [&](int p, int t, int s, float& v0, float& v1) {
@@ -1097,8 +1107,9 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       }
     });
     acc.zero();
-    tc::mma_acc3<1, NI, false, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
-    tc::mma_acc3<1, NI, true, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C);
+    // Mm is strictly lower: Mm K needs k < m0 + 16, Mm^T K needs k >= m0
+    tc::mma_acc3<1, NI, false, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, m0 + 16);
+    tc::mma_acc3<1, NI, true, false>(acc, Mmb, nullptr, LDT, Ks, Kl, ldk, m0, n0, C, m0);
     acc.each2(m0, n0, [&](int p, int t, int col, float& v0, float& v1) {
       if (t < c) st2(d.dk + (r0 + t) * K + col, a[p].x + s2[p].x + v0, a[p].y + s2[p].y + v1);
     });

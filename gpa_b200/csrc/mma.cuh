@@ -105,11 +105,12 @@ struct Acc {
   }
 };
 
-// acc += A[m0:m0+16MI, 0:K] * B[0:K, n0:n0+16NI]
+// acc += A[m0:m0+16MI, kb:K] * B[kb:K, n0:n0+16NI] (kb a multiple of 16: a triangular
+// operand skips its zero blocks)
 template <int MI, int NI, bool TA, bool TB>
 GPA_DEV void mma_acc(Acc<MI, NI>& acc, const bf16* A, int lda, const bf16* B, int ldb, int m0,
-                     int n0, int K) {
-  for (int k0 = 0; k0 < K; k0 += 16) {
+                     int n0, int K, int kb = 0) {
+  for (int k0 = kb; k0 < K; k0 += 16) {
     uint32_t a[MI][4], b[NI][4];
 #pragma unroll
     for (int i = 0; i < MI; ++i) load_a<TA>(a[i], A, lda, m0 + 16 * i, k0);
@@ -127,11 +128,11 @@ GPA_DEV void mma_acc(Acc<MI, NI>& acc, const bf16* A, int lda, const bf16* B, in
 
 // Split-operand product: acc += Ah*Bh + Ah*Bl + Al*Bh, where x = xh + xl is an
 // fp32 value carried as two bf16 (hi = bf16(x), lo = bf16(x - hi)); either lo
-// may be null.  Products then carry ~16 significant bits instead of 8.
+// may be null.  Products then carry ~16 significant bits instead of 8.  k runs over [kb, K).
 template <int MI, int NI, bool TA, bool TB>
 GPA_DEV void mma_acc3(Acc<MI, NI>& acc, const bf16* Ah, const bf16* Al, int lda, const bf16* Bh,
-                      const bf16* Bl, int ldb, int m0, int n0, int K) {
-  for (int k0 = 0; k0 < K; k0 += 16) {
+                      const bf16* Bl, int ldb, int m0, int n0, int K, int kb = 0) {
+  for (int k0 = kb; k0 < K; k0 += 16) {
     uint32_t a[MI][4], b[NI][4], x[4];
 #pragma unroll
     for (int i = 0; i < MI; ++i) load_a<TA>(a[i], Ah, lda, m0 + 16 * i, k0);
