@@ -726,18 +726,26 @@ __global__ void __launch_bounds__(512) tk_post_bwd(
     float pk = 0.f, pv = 0.f;
     tiles_n<1, 2>(R, D, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 dk[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int t, int d, float&, float&) {
+        dk[p] = t < c ? tc::ld2(dkey + row(u, T, t0 + t) * D + d) : make_float2(0.f, 0.f);
+      });
       acc.zero();
       mma_acc<1, NI, false, true>(acc, Wb, lm, Af, lm, m0, n0, M);
-      acc.each(m0, n0, [&](int t, int d, float& v) {
-        if (t < c) pk += v * dkey[row(u, T, t0 + t) * D + d];
+      acc.each2(m0, n0, [&](int p, int, int, float& v0, float& v1) {
+        pk += v0 * dk[p].x + v1 * dk[p].y;
       });
     });
     tiles_n<1, 2>(R, Dv, [&]<int NI>(int m0, int n0) {
       Acc<1, NI> acc;
+      float2 dv[Acc<1, NI>::kPairs];
+      acc.each2(m0, n0, [&](int p, int t, int vv, float&, float&) {
+        dv[p] = t < c ? tc::ld2(dval + row(u, T, t0 + t) * Dv + vv) : make_float2(0.f, 0.f);
+      });
       acc.zero();
       mma_acc<1, NI, false, false>(acc, Wb, lm, Bf, lv, m0, n0, M);
-      acc.each(m0, n0, [&](int t, int vv, float& v) {
-        if (t < c) pv += v * dval[row(u, T, t0 + t) * Dv + vv];
+      acc.each2(m0, n0, [&](int p, int, int, float& v0, float& v1) {
+        pv += v0 * dv[p].x + v1 * dv[p].y;
       });
     });
     pk = warp_sum(pk);
