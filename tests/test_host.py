@@ -118,3 +118,21 @@ def test_workspace_queries_and_argument_errors():
     assert lib.gpa_b200_last_error(buf, 256) == 1 and b"params" in buf.value
     with pytest.raises(ValueError, match="params"):
         _lib.check(rc, "gpa_b200_forward")
+
+
+def test_config2_workspaces_fit_one_b200():
+    """The forward's saved buffer and the backward scratch of BASELINE config 2 (B=8, T=8192,
+    H=16, 128/128, slots 64/64/64/128, chunk 64, bf16) leave most of a 180 GB B200 to the
+    caller's tensors; a width above the supported 128 reports no size (unsupported)."""
+    lib = _lib.load()
+    d = _lib.GpaDims()
+    d.batch, d.length, d.heads, d.key_dim, d.value_dim, d.levels = 8, 8192, 16, 128, 128, 4
+    for j, m in enumerate((64, 64, 64, 128)):
+        d.slots[j] = m
+    d.chunk_size, d.chunk_offset, d.input_dtype = 64, 0, 1
+    d.read_scale, d.query_scale, d.beta_max = 1., 1 / 16, .9
+    saved, scratch = lib.gpa_b200_saved_bytes(d), lib.gpa_b200_scratch_bytes(d)
+    io = 7 * 8 * 8192 * 16 * 128 * 2  # q, k, v, out and dq, dk, dv in bf16
+    assert 0 < saved + scratch + io < 110e9
+    d.slots[3] = 256
+    assert lib.gpa_b200_saved_bytes(d) == 0 and lib.gpa_b200_scratch_bytes(d) == 0
