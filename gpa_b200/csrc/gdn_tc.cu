@@ -171,9 +171,9 @@ GPA_DEV void for_lower_tiles(Body body) {
   }
 }
 
-// A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t), Atil without b_t (optional); k split hi/lo
+// A[t][s] = b_t exp(G_t - G_s) k_t.k_s (s < t); k split hi/lo
 GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const float* G,
-                        const float* bt, float* A, float* Atil) {
+                        const float* bt, float* A) {
   for_lower_tiles([&](int m0, int n0) {  // the upper tiles are never read
     Acc<1, 1> acc;
     acc.zero();
@@ -181,7 +181,6 @@ GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const fl
     acc.each(m0, n0, [&](int t, int s, float& v) {
       const float at = s < t ? __expf(G[t] - G[s]) * v : 0.f;
       A[t * kAStride + s] = bt[t] * at;
-      if (Atil) Atil[t * kAStride + s] = at;
     });
   });
 }
@@ -232,7 +231,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
     tc::load_tiles<false>(jobs);
     gate_finish(gr, c, G, bt);
   }
-  tc_build_a(Ks, Kl, ldk, K, G, bt, A, nullptr);
+  tc_build_a(Ks, Kl, ldk, K, G, bt, A);
   __syncthreads();
   invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
   float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
@@ -1091,7 +1090,7 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
       }
   });
   __syncthreads();
-  // A = b_t Atil: rowsum(dA o Atil) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
+  // A = b_t A~ (A~ without b_t): rowsum(dA o A~) = rowsum(dA o A) / b_t (b_t > 0 on real rows)
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     if (t < c) db[t] += rsum[t] / bt[t];
     dG[t] += rsum[t] - csum[t];
