@@ -15,7 +15,8 @@ MAX_EDGES = 56
 ABI_VERSION = 1
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgpa_b200.so")
 
-STATUS = {0: "ok", 1: "bad argument", 2: "unsupported configuration", 3: "CUDA launch failure"}
+STATUS = {0: "ok", 1: "bad argument", 2: "unsupported configuration", 3: "CUDA launch failure",
+          4: "device timeout"}
 
 
 class GpaDims(ctypes.Structure):
@@ -52,7 +53,7 @@ EXPORTS = ("gpa_b200_saved_bytes", "gpa_b200_scratch_bytes", "gpa_b200_forward",
            "gpa_b200_backward", "gpa_b200_routes", "gpa_b200_last_error",
            "gpa_b200_abi_version", "gpa_b200_launch_count", "gpa_b200_profile_start",
            "gpa_b200_profile_stop", "gpa_b200_forward_noalloc", "gpa_b200_noalloc_capacity",
-           "gpa_b200_step")
+           "gpa_b200_step", "gpa_b200_umma_selftest", "gpa_b200_device_status")
 
 _lib = None
 
@@ -86,6 +87,10 @@ def load():
     lib.gpa_b200_step.argtypes = [POINTER(GpaDims), POINTER(GpaParams), c_void_p, c_void_p,
                                   c_void_p, POINTER(GpaStateRef), c_void_p, c_void_p, c_void_p]
     lib.gpa_b200_step.restype = c_int
+    lib.gpa_b200_device_status.argtypes = [c_int]
+    lib.gpa_b200_device_status.restype = c_int
+    lib.gpa_b200_umma_selftest.argtypes = [c_int] * 7 + [c_void_p] * 6
+    lib.gpa_b200_umma_selftest.restype = c_int
     lib.gpa_b200_noalloc_capacity.argtypes = []
     lib.gpa_b200_noalloc_capacity.restype = c_size_t
     lib.gpa_b200_routes.argtypes = [POINTER(GpaDims), c_void_p, POINTER(c_void_p), c_void_p]
@@ -137,3 +142,8 @@ def profile_stop() -> dict:
 
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def device_status(clear: bool = False) -> int:
+    """0, or 4 (device timeout) when a bounded wait inside a tensor-core kernel gave up."""
+    return int(load().gpa_b200_device_status(int(clear)))

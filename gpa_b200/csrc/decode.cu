@@ -1,7 +1,9 @@
 // One-token decode step for lag-block caches (chunk_size >= 2), fused into a single kernel
 // per call: one CTA per (batch, head) unit walks the whole layer for its token and updates
-// the cache in place.  The chunk offset lives in device memory and is advanced by a second
-// one-thread kernel, so a sequence of steps can be captured once in a CUDA graph and replayed.
+// the cache in place.  The chunk offset lives in device memory; the last CTA to finish
+// advances it (a completion counter beside the offset tells it that every CTA has read the
+// old value), so a step is one launch and a sequence of steps can be captured once in a CUDA
+// graph and replayed.
 //
 // Per unit and level j (src/gpa/attention.py:299-345 with a one-token block):
 //   slot = C_j k, gates from u(k); A <- GDN(A, u(k), slot) and raw = u(q)^T A;
@@ -15,7 +17,7 @@
 // Each state matrix is read from HBM once into shared memory, updated there and written
 // back once (the outer states, and the frozen snapshots when the token opens a block, are
 // read a second time): the step is HBM-bound on the cache, 2 x 4 x 155,968 bytes per unit at
-// the config-2 widths.
+// the widths Dk = Dv = 128, slots (64, 64, 64, 128).
 #include "decode.cuh"
 
 namespace gpa {
@@ -424,10 +426,18 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   }
   for (int i = threadIdx.x, c = 0; i < Dv; i += blockDim.x, ++c)
     store_out(a.out, (int64_t)u * Dv + i, outacc[c], a.dt);
-}
-
-__global__ void k_advance_offset(int* offset, int C) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) *offset = (*offset + 1) % C;
+  // Offset advance: every CTA read the offset on entry, before it counts itself done here, so
+  // the last CTA to arrive may overwrite it.  It also resets the counter for the next step.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(reinterpret_cast<unsigned*>(a.offset + 1), 1u);
+    if (done == gridDim.x - 1) {
+      a.offset[0] = (o + 1) % a.C;
+      a.offset[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 }  // namespace
@@ -443,10 +453,6 @@ cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st) {
   {
     Launch scope("decode_step", st);
     k_decode_step<<<a.U, kStepThreads, smem, st>>>(a);
-  }
-  {
-    Launch scope("advance_offset", st);
-    k_advance_offset<<<1, 32, 0, st>>>(a.offset, a.C);
   }
   return cudaGetLastError();
 }

@@ -17,13 +17,14 @@ struct StepArgs {
   GpaStateRef s;  // updated in place; frozen_* required
   const void *q, *k, *v;
   void* out;
-  int* offset;  // device int: the cache's chunk offset, advanced by the step
+  int* offset;  // device int[2]: the cache's chunk offset (advanced by the step) and the
+                // step's completion counter (0 between steps)
 };
 
 // Shared memory the step kernel needs for these widths (bytes).
 size_t decode_step_smem(const StepArgs& a);
-// Stream-ordered: the step kernel, then the one-thread offset advance.  No allocation, no
-// host synchronization (capturable in a CUDA graph).
+// Stream-ordered, one kernel (its last CTA advances the offset).  No allocation, no host
+// synchronization (capturable in a CUDA graph).
 cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st);
 
 }  // namespace gpa

@@ -1204,7 +1204,9 @@ cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_ou
   cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st,
                                               false, 74);
   if (e != cudaSuccess) return e;
-  e = tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U, bl, st, true);
+  e = tc5_sweeps_enabled() ? tc5_fwd_state_launch(b, U, bl, st)
+                           : tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U,
+                                                         bl, st, true);
   if (e != cudaSuccess || !with_output) return e;
   return tc_output(b, U, bl, st);
 }

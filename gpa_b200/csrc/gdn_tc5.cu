@@ -1,0 +1,437 @@
+// State sweeps of the chunked GDN scans on the 5th-generation tensor cores (tcgen05, TMEM
+// accumulators, bulk TMA copies of the next block's operands).
+//
+// The forward sweep carries the state S [K x V] of one unit across its blocks:
+//   W = U - Wk S,            S <- e^{G_c} S + K^T diag(lambda) W,   lambda_t = e^{G_c - G_t}
+// (the WY / UT chunk form of gdn.cuh).  Both products run transposed, so that a TMEM lane is a
+// value column v of the state for both of them:
+//   W^T [V x c]  = S^T Wk^T          (A = S^T, 128 rows v, reduction over k; B = Wk, rows t)
+//   S'^T [V x K] = (lambda W)^T K    (A = (lambda W)^T, rows v, reduction over t; B = K, rows k)
+// and S' = e^{G_c} S + S'^T^T is formed in the epilogue from the fp32 state each thread keeps in
+// registers (thread (v, half) holds S[k][v] for half of the k).  The MMAs use M = 128 (rows v >=
+// V are zero) and bf16 operands: Wk, K, lambda W as hi + lo pairs (three products: hi hi, hi lo,
+// lo hi), S as hi only, the same precision split as the mma.sync sweep it replaces.
+//
+// Per block n of a unit (one CTA per unit and scan, 256 threads):
+//   land the fp32 rows of Wk(n), K(n) (bulk copies issued during block n-1), convert them into
+//   the bf16 operand tiles, issue the copies of block n+1, then
+//   MMA 1 -> epilogue 1 (W = U - acc, W to global as bf16, lambda W to shared memory)
+//   MMA 2 -> epilogue 2 (S update, boundary state to global, S^T hi to shared memory).
+// One thread issues every MMA and commit; every wait on an mbarrier is bounded and a wait that
+// gives up sets the library's device status to GPA_B200_DEVICE_TIMEOUT and ends the sweep.
+#include "../../include/gpa_b200.h"
+#include "gdn.cuh"
+#include "gdn_dev.cuh"
+#include "tc5.cuh"
+
+#include <cuda_bf16.h>
+
+#include <cstdlib>
+#include <cstring>
+
+namespace gpa {
+
+__device__ int g_device_status = 0;
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int C = kMaxChunk;       // 64 tokens per block tile
+constexpr int kSweepThreads = 256;  // 8 warps: two per TMEM lane quarter
+constexpr int kSweepCols = 256;     // TMEM columns: W^T at 0 (64), S^T at 64 (<= 128)
+
+struct SweepGates {
+  float g0, g1;
+};
+
+// gates of block (t0, c) in registers of warp 0 (t = lane, lane + 32)
+GPA_DEV SweepGates sweep_gate_fetch(const ScanDesc& d, int u, int t0, int c) {
+  SweepGates r{0.f, 0.f};
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    if (t < c) r.g0 = gate_at(d.g, d, u, t0 + t);
+    if (t + 32 < c) r.g1 = gate_at(d.g, d, u, t0 + t + 32);
+  }
+  return r;
+}
+
+// G = inclusive cumsum of g (rows >= c hold G[c-1]) and lambda_t = e^{G_{c-1} - G_t} (0 for
+// t >= c), written to shared memory by warp 0; the caller synchronizes.
+GPA_DEV void sweep_gate_finish(const SweepGates& r, int c, float* G, float* lam) {
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    float x0 = r.g0, x1 = r.g1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (t >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    const float last = __shfl_sync(0xffffffffu, c - 1 < 32 ? x0 : x1, (c - 1) & 31);
+    G[t] = t < c ? x0 : last;
+    G[t + 32] = t + 32 < c ? x1 : last;
+    lam[t] = t < c ? __expf(last - x0) : 0.f;
+    lam[t + 32] = t + 32 < c ? __expf(last - x1) : 0.f;
+  }
+}
+
+// 8 consecutive fp32 values -> their bf16 hi and lo parts as two 16-byte groups
+GPA_DEV void split8(const float (&x)[8], uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    const float2 f = __bfloat1622float2(p);
+    const __nv_bfloat162 q = __floats2bfloat162_rn(x[2 * i] - f.x, x[2 * i + 1] - f.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&p);
+    l[i] = *reinterpret_cast<const uint32_t*>(&q);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+GPA_DEV uint4 pack8(const float (&x)[8]) {
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    h[i] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// fp32 rows [c x K] staged in shared memory (row stride K) -> bf16 hi / lo operand tiles of 64
+// rows t (rows >= c zero): K-major (rows t, reduction k) when kmajor, else MN-major with the
+// rows k and the reduction over t.  A thread converts 8 consecutive k of one row per step;
+// the 8 lanes of a shared-memory phase take 8 different t (conflict-free 16-byte stores).
+GPA_DEV void stage_to_tiles(const float* raw, int c, int K, bool kmajor, unsigned char* hi,
+                            unsigned char* lo) {
+  const int k8n = K >> 3, n = C * k8n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int t = (i & 7) | ((i / (8 * k8n)) << 3), k8 = (i >> 3) % k8n;
+    float x[8];
+    if (t < c) {
+      const float4 a = *reinterpret_cast<const float4*>(raw + t * K + 8 * k8);
+      const float4 b = *reinterpret_cast<const float4*>(raw + t * K + 8 * k8 + 4);
+      x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = 0.f;
+    }
+    uint4 h, l;
+    split8(x, h, l);
+    // the 8 k of this group form one core-matrix row in both layouts
+    const uint32_t o = kmajor ? tc5::kmajor_off(t, 8 * k8, K) : tc5::mnmajor_off(8 * k8, t, C);
+    *reinterpret_cast<uint4*>(hi + o) = h;
+    if (lo) *reinterpret_cast<uint4*>(lo + o) = l;
+  }
+}
+
+struct LFwdSweep {
+  uint32_t St, WkH, WkL, WtH, WtL, KbH, KbL, rawWk, rawK, G, lam, bar, slot, total;
+  __host__ __device__ LFwdSweep(int K, int V) {
+    uint32_t o = 0;
+    auto take = [&](uint32_t b) {
+      o = (o + 127u) & ~127u;
+      const uint32_t r = o;
+      o += b;
+      return r;
+    };
+    St = take(128 * K * 2);   // S^T hi: A of MMA 1, K-major, rows v (128), reduction k
+    WkH = take(C * K * 2);    // Wk: B of MMA 1, K-major, rows t, reduction k
+    WkL = take(C * K * 2);
+    WtH = take(128 * C * 2);  // (lambda W)^T: A of MMA 2, K-major, rows v, reduction t
+    WtL = take(128 * C * 2);
+    KbH = take(K * C * 2);    // K: B of MMA 2, MN-major, rows k, reduction t
+    KbL = take(K * C * 2);
+    rawWk = take(C * K * 4);  // fp32 rows of the next block, landed by bulk copies
+    rawK = take(C * K * 4);
+    G = take(C * 4);
+    lam = take(C * 4);
+    bar = take(2 * 8);
+    slot = take(16);
+    total = o;
+    (void)V;
+  }
+};
+
+GPA_DEV void fail_status() { atomicExch(&g_device_status, GPA_B200_DEVICE_TIMEOUT); }
+
+// grid (U, nscan), 256 threads.  KMAX bounds the key width K (64: two CTAs per SM).
+//
+// Per block n: MMA 1 (W^T) -> epilogue 1 (issues the U loads of block n+1 when done) -> MMA 2
+// (S^T), during which the landed fp32 Wk rows of block n+1 become its MMA-1 operand -> epilogue
+// 2 -> the K rows of block n+1 become its MMA-2 operand -> the bulk copies of block n+2 start.
+template <int KMAX>
+__global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
+    tc5_fwd_state(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x, K = d.K, V = d.V, T = bl.T;
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const LFwdSweep L(K, V);
+  unsigned char* St = sm + L.St;
+  unsigned char* WkH = sm + L.WkH;
+  unsigned char* WkL = sm + L.WkL;
+  unsigned char* WtH = sm + L.WtH;
+  unsigned char* WtL = sm + L.WtL;
+  unsigned char* KbH = sm + L.KbH;
+  unsigned char* KbL = sm + L.KbL;
+  float* rawWk = reinterpret_cast<float*>(sm + L.rawWk);
+  float* rawK = reinterpret_cast<float*>(sm + L.rawK);
+  float* G = reinterpret_cast<float*>(sm + L.G);
+  float* lam = reinterpret_cast<float*>(sm + L.lam);
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L.bar);
+  uint64_t* bar_tma = bar_mma + 1;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
+  constexpr int SH = KMAX / 2;  // state values per thread (max)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, half = warp >> 2;
+  const int v = 32 * q + lane;
+  const bool active = 32 * q < V;  // warp-uniform: the quarter holds state columns
+  const bool vok = v < V;
+  const int KH = K >> 1, k0 = half * KH;  // this thread's state rows k0 .. k0 + KH - 1
+  const int64_t KV = (int64_t)K * V;
+  bf16* Wout = reinterpret_cast<bf16*>(d.W);
+
+  // A tiles: rows v >= V stay zero for the whole sweep
+  for (uint32_t i = tid * 16; i < 128u * K * 2; i += blockDim.x * 16)
+    *reinterpret_cast<uint4*>(St + i) = make_uint4(0, 0, 0, 0);
+  for (uint32_t i = tid * 16; i < 128u * C * 2; i += blockDim.x * 16) {
+    *reinterpret_cast<uint4*>(WtH + i) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(WtL + i) = make_uint4(0, 0, 0, 0);
+  }
+  if (warp == 0) tc5::tmem_alloc(slot, kSweepCols);
+  if (tid == 0) {
+    tc5::mbar_init(bar_mma, 1);
+    tc5::mbar_init(bar_tma, 1);
+    tc5::mbar_fence_init();
+  }
+  auto issue_rows = [&](int n) {  // bulk copies of block n's fp32 rows of Wk and K
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    const uint32_t bytes = (uint32_t)(c * K * 4);
+    tc5::mbar_expect_tx(bar_tma, 2 * bytes);
+    tc5::bulk_g2s(rawWk, d.Wk + row(u, T, t0) * K, bytes, bar_tma);
+    tc5::bulk_g2s(rawK, d.k + row(u, T, t0) * K, bytes, bar_tma);
+  };
+  float ub[32];  // U[t][v] of this thread's 32 tokens of the coming epilogue 1
+  auto load_u = [&](int n) {
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = 32 * half + j;
+      ub[j] = (active && vok && t < c) ? d.Ub[row(u, T, t0 + t) * V + v] : 0.f;
+    }
+  };
+  float s[SH];
+#pragma unroll
+  for (int i = 0; i < SH; ++i) s[i] = 0.f;
+  tc5::fence_before_sync();
+  __syncthreads();  // barriers initialised, tiles zeroed, TMEM allocated
+  tc5::fence_after_sync();
+  if (tid == 0) issue_rows(0);
+  // initial state: S_0 into registers, the first boundary and the S^T hi tile
+  if (active) {
+    float* sb0 = d.Sb + (int64_t)u * (bl.nb + 1) * KV;
+#pragma unroll
+    for (int i = 0; i < SH; i += 8) {
+      if (i < KH) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[j] = vok ? d.S0[(int64_t)u * KV + (int64_t)(k0 + i + j) * V + v] : 0.f;
+          s[i + j] = x[j];
+          if (vok) sb0[(int64_t)(k0 + i + j) * V + v] = x[j];
+        }
+        *reinterpret_cast<uint4*>(St + tc5::kmajor_off(v, k0 + i, K)) = pack8(x);
+      }
+    }
+  }
+  load_u(0);
+  uint32_t tph = 0, mph = 0;
+  bool ok = true, all_ok = true;
+  {
+    const int c0 = bl.end(0) - bl.start(0);
+    sweep_gate_finish(sweep_gate_fetch(d, u, 0, c0), c0, G, lam);
+    ok = tc5::mbar_wait(bar_tma, tph);
+    tph ^= 1;
+    stage_to_tiles(rawWk, c0, K, true, WkH, WkL);
+    stage_to_tiles(rawK, c0, K, false, KbH, KbL);
+  }
+  SweepGates gr{0.f, 0.f};
+  if (bl.nb > 1) gr = sweep_gate_fetch(d, u, bl.start(1), bl.end(1) - bl.start(1));
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  all_ok = __syncthreads_and(ok);
+  tc5::fence_after_sync();
+  const uint32_t tbase = *slot;
+  if (tid == 0 && all_ok && bl.nb > 1) issue_rows(1);
+  const uint32_t id1 = tc5::idesc_bf16(128, C, false, false);
+  const uint32_t id2 = tc5::idesc_bf16(128, K, false, true);
+  for (int n = 0; all_ok && n < bl.nb; ++n) {
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    const bool more = n + 1 < bl.nb;
+    if (tid == 0) {  // MMA 1: W^T = S^T Wk^T (Wk hi and lo)
+      const uint32_t a = tc5::saddr(St), bh = tc5::saddr(WkH), bl_ = tc5::saddr(WkL);
+      for (int ks = 0; ks < K / 16; ++ks)
+        tc5::mma(tbase, tc5::sdesc(a, K, ks), tc5::sdesc(bh, K, ks), id1, ks > 0);
+      for (int ks = 0; ks < K / 16; ++ks)
+        tc5::mma(tbase, tc5::sdesc(a, K, ks), tc5::sdesc(bl_, K, ks), id1, true);
+      tc5::commit(bar_mma);
+    }
+    ok = ok && tc5::mbar_wait(bar_mma, mph);
+    mph ^= 1;
+    tc5::fence_after_sync();
+    if (active) {  // epilogue 1: W = U - acc; W out (bf16); lambda W hi / lo -> (lambda W)^T
+#pragma unroll
+      for (int c16 = 0; c16 < 2; ++c16) {
+        float acc[16];
+        tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half + 16 * c16), acc);
+        tc5::tmem_wait_ld();
+#pragma unroll
+        for (int j8 = 0; j8 < 2; ++j8) {
+          float x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int jj = 16 * c16 + 8 * j8 + j, t = 32 * half + jj;
+            const float w = (vok && t < c) ? ub[jj] - acc[8 * j8 + j] : 0.f;
+            if (vok && t < c) Wout[row(u, T, t0 + t) * V + v] = __float2bfloat16(w);
+            x[j] = w * lam[t];
+          }
+          uint4 h, l;
+          split8(x, h, l);
+          const uint32_t o = tc5::kmajor_off(v, 32 * half + 16 * c16 + 8 * j8, C);
+          *reinterpret_cast<uint4*>(WtH + o) = h;
+          *reinterpret_cast<uint4*>(WtL + o) = l;
+        }
+      }
+    }
+    if (more) load_u(n + 1);
+    tc5::fence_async_smem();
+    tc5::fence_before_sync();
+    __syncthreads();
+    tc5::fence_after_sync();
+    if (tid == 0 && ok) {  // MMA 2: S'^T = (lambda W)^T K (hi hi, hi lo, lo hi)
+      const uint32_t ah = tc5::saddr(WtH), al = tc5::saddr(WtL);
+      const uint32_t bh = tc5::saddr(KbH), bl_ = tc5::saddr(KbL);
+      const uint32_t d2 = tbase + C;
+      for (int ks = 0; ks < C / 16; ++ks) {
+        tc5::mma(d2, tc5::sdesc(ah, C, ks), tc5::sdesc(bh, C, ks), id2, ks > 0);
+        tc5::mma(d2, tc5::sdesc(ah, C, ks), tc5::sdesc(bl_, C, ks), id2, true);
+        tc5::mma(d2, tc5::sdesc(al, C, ks), tc5::sdesc(bh, C, ks), id2, true);
+      }
+      tc5::commit(bar_mma);
+    }
+    int cn = 0;
+    if (more) {  // while MMA 2 runs: the next block's Wk rows -> its MMA-1 operand
+      cn = bl.end(n + 1) - bl.start(n + 1);
+      ok = ok && tc5::mbar_wait(bar_tma, tph);
+      tph ^= 1;
+      stage_to_tiles(rawWk, cn, K, true, WkH, WkL);
+    }
+    ok = ok && tc5::mbar_wait(bar_mma, mph);
+    mph ^= 1;
+    tc5::fence_after_sync();
+    const float gc = __expf(G[c - 1]);
+    if (active) {  // epilogue 2: S <- e^{G_c} S + acc; boundary state out; S^T hi tile
+      float* sbn = d.Sb + ((int64_t)u * (bl.nb + 1) + n + 1) * KV;
+#pragma unroll
+      for (int i = 0; i < SH; i += 16) {
+        if (i < KH) {
+          float acc[16];
+          tc5::tmem_ld16(tc5::tmem_at(tbase, C + k0 + i), acc);
+          tc5::tmem_wait_ld();
+#pragma unroll
+          for (int h8 = 0; h8 < 16; h8 += 8) {
+            if (i + h8 < KH) {
+              float x[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float sv = gc * s[i + h8 + j] + acc[h8 + j];
+                s[i + h8 + j] = sv;
+                x[j] = sv;
+                if (vok) sbn[(int64_t)(k0 + i + h8 + j) * V + v] = sv;
+              }
+              *reinterpret_cast<uint4*>(St + tc5::kmajor_off(v, k0 + i + h8, K)) = pack8(x);
+            }
+          }
+        }
+      }
+    }
+    if (more) {  // the next block's K rows -> its MMA-2 operand; its gates
+      stage_to_tiles(rawK, cn, K, false, KbH, KbL);
+      __syncthreads();  // every thread has read G[c - 1]
+      sweep_gate_finish(gr, cn, G, lam);
+      if (n + 2 < bl.nb) gr = sweep_gate_fetch(d, u, bl.start(n + 2), bl.end(n + 2) - bl.start(n + 2));
+    }
+    tc5::fence_async_smem();
+    tc5::fence_before_sync();
+    all_ok = __syncthreads_and(ok);
+    tc5::fence_after_sync();
+    if (tid == 0 && all_ok && n + 2 < bl.nb) issue_rows(n + 2);  // the staging rows were read
+  }
+  if (all_ok && d.S_final && active && vok) {
+#pragma unroll
+    for (int i = 0; i < SH; ++i)
+      if (i < KH) d.S_final[(int64_t)u * KV + (int64_t)(k0 + i) * V + v] = s[i];
+  }
+  if (!all_ok && tid == 0) {
+    fail_status();
+    tc5::mbar_wait(bar_tma, tph);  // a bulk copy may still be landing: bounded wait
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc5::tmem_free(tbase, kSweepCols);
+}
+
+}  // namespace
+
+size_t tc5_fwd_state_smem(int K, int V) { return LFwdSweep(K, V).total; }
+
+int tc5_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
+bool tc5_sweeps_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GPA_B200_SWEEPS");
+    return !(e && std::strcmp(e, "mma") == 0);
+  }();
+  return on;
+}
+
+cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  bool done[kMaxScans] = {};
+  for (int i = 0; i < b.n; ++i) {
+    if (done[i]) continue;
+    ScanBatch sub;
+    sub.tc = b.tc;
+    sub.n = 0;
+    for (int j = i; j < b.n; ++j)
+      if (!done[j] && b.s[j].K == b.s[i].K && b.s[j].V == b.s[i].V) {
+        sub.s[sub.n++] = b.s[j];
+        done[j] = true;
+      }
+    const size_t smem = tc5_fwd_state_smem(b.s[i].K, b.s[i].V);
+    if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+    const auto kern = b.s[i].K <= 64 ? tc5_fwd_state<64> : tc5_fwd_state<128>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    Launch scope("tc5_fwd_state", st);
+    kern<<<dim3(U, sub.n), kSweepThreads, smem, st>>>(sub, U, bl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace gpa

@@ -3,7 +3,7 @@
 ``DenseGPA.forward`` with a one-token input is the reference's decode call
 (src/gpa/attention.py:347-414): it returns a new ``GPAState`` each time.  For
 serving, :class:`DecodeSession` keeps the cache in fixed fp32 buffers that one
-fused kernel per step updates in place, with the lag-block offset in device
+fused kernel per step (a single launch) updates in place, with the lag-block offset in device
 memory, so a step allocates nothing, never synchronizes with the host and can be
 captured once in a CUDA graph (:meth:`DecodeSession.capture`) and replayed.  Its
 outputs and caches are those of the one-token ``forward`` calls it replaces
@@ -54,7 +54,9 @@ class DecodeSession:
         else:  # written by the step that opens the next lag block
             self._flat += [torch.zeros(s, device=dev, dtype=torch.float32) for s in shapes[base:]]
         self._edges = model.edges
-        self.offset = torch.tensor([state.chunk_offset], device=dev, dtype=torch.int32)
+        # [chunk offset, completion counter of the step kernel (0 between steps)]
+        self._offset = torch.tensor([state.chunk_offset, 0], device=dev, dtype=torch.int32)
+        self.offset = self._offset[:1]
         self.position = state.position
         self._graph = None
 
@@ -73,7 +75,7 @@ class DecodeSession:
         with torch.cuda.device(q.device):
             rc = lib.gpa_b200_step(plan.dims, plan.params_ref(params), q.data_ptr(), k.data_ptr(),
                                    v.data_ptr(), plan.state_ref(self._flat, True),
-                                   self.offset.data_ptr(), out.data_ptr(), _stream(q.device))
+                                   self._offset.data_ptr(), out.data_ptr(), _stream(q.device))
         _lib.check(rc, "gpa_b200_step")
         self.position += 1
         return out
@@ -82,13 +84,13 @@ class DecodeSession:
         """Capture one step on the static inputs ``q, k, v`` in a CUDA graph; returns the
         static output.  :meth:`replay` then runs a step on whatever ``q, k, v`` hold."""
         self._static = (q, k, v, torch.empty(self._shape_v, device=q.device, dtype=self.dtype))
-        rewind = [t.clone() for t in self._flat] + [self.offset.clone()]
+        rewind = [t.clone() for t in self._flat] + [self._offset.clone()]
         self.step(*self._static[:3], out=self._static[3])  # warm-up (library load, attributes)
         torch.cuda.synchronize(q.device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):  # recorded, not run
             self.step(*self._static[:3], out=self._static[3])
-        for t, r in zip(self._flat + [self.offset], rewind):  # undo the warm-up step
+        for t, r in zip(self._flat + [self._offset], rewind):  # undo the warm-up step
             t.copy_(r)
         self.position -= 2
         self._graph = graph

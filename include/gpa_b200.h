@@ -18,7 +18,9 @@
  * input dtype (fp32 / bf16 / fp16).  Parameters, states and their gradients
  * are contiguous fp32 tensors with the reference's shapes
  * (src/gpa/attention.py:104-135, src/gpa/state.py:30-58).  Status codes:
- * 0 ok, 1 bad argument, 2 unsupported configuration, 3 CUDA launch failure.
+ * 0 ok, 1 bad argument, 2 unsupported configuration, 3 CUDA launch failure,
+ * 4 device timeout (a bounded wait inside a tensor-core kernel gave up; the
+ * kernel returned without its result and the context stays usable).
  */
 #ifndef GPA_B200_H
 #define GPA_B200_H
@@ -34,7 +36,7 @@ extern "C" {
 #define GPA_B200_MAX_EDGES 56
 
 enum { GPA_B200_OK = 0, GPA_B200_BAD_ARGUMENT = 1, GPA_B200_UNSUPPORTED = 2,
-       GPA_B200_LAUNCH_FAILURE = 3 };
+       GPA_B200_LAUNCH_FAILURE = 3, GPA_B200_DEVICE_TIMEOUT = 4 };
 enum { GPA_B200_F32 = 0, GPA_B200_BF16 = 1, GPA_B200_F16 = 2 };
 
 /* Shapes and the scalar GPAConfig fields the core reads (src/gpa/attention.py:17-43). */
@@ -128,7 +130,10 @@ int gpa_b200_backward(const GpaDims* dims, const GpaParams* params, const GpaSta
  * bytes (64 MiB) that every GPU loading this library holds until the process
  * exits; calls whose workspace would exceed it return GPA_B200_UNSUPPORTED.
  * The first call on a device looks the array's address up (with that device
- * current); make that first call before any stream capture.  Every call shares
+ * current) and keeps it for the life of the process; make that first call before
+ * any stream capture, and do not call this entry point on a device after its
+ * primary context was destroyed (cudaDeviceReset), which would leave the kept
+ * address stale.  Every call shares
  * the array and overwrites all of it that it reads, so nothing needs clearing,
  * but calls that overlap on the GPU (other streams, other threads) race.  The
  * array is reused by the next call, so this entry point has no backward. */
@@ -141,12 +146,14 @@ size_t gpa_b200_noalloc_capacity(void);
  * replacing a one-token DenseGPA.forward call (src/gpa/attention.py:347-414 with
  * T = 1, which runs _block_segment :299-345 on a one-token block).  The cache is
  * updated IN PLACE (state->frozen_* required: the snapshots of the current lag
- * block, written by this call when the token opens a block), and *offset (device
- * int32, the cache's chunk_offset) is advanced to (offset + 1) % chunk_size on the
- * device; dims->chunk_offset is ignored.  out: [B,1,H,Dv] in the input dtype.
- * Stream-ordered, allocates nothing and never synchronizes with the host, so a
- * sequence of steps can be captured in a CUDA graph.  Widths must be multiples
- * of 4. */
+ * block, written by this call when the token opens a block).  offset points to two
+ * device int32: offset[0] is the cache's chunk_offset, advanced to
+ * (offset[0] + 1) % chunk_size on the device; offset[1] is the step's completion
+ * counter, which must be 0 before the first step and is left at 0 by every step
+ * (steps on the same offset buffer must not overlap on the GPU).  dims->chunk_offset
+ * is ignored.  out: [B,1,H,Dv] in the input dtype.  One kernel launch, stream-ordered,
+ * allocates nothing and never synchronizes with the host, so a sequence of steps can
+ * be captured in a CUDA graph.  Widths must be multiples of 4. */
 int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, const void* k,
                   const void* v, const GpaStateRef* state, int32_t* offset, void* out,
                   void* stream);
@@ -155,6 +162,27 @@ int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, c
  * saved buffer into routes[j] ([B,T,H,M_j], input dtype).  Replaces the
  * return_diagnostics routes of DenseGPA.forward (src/gpa/attention.py:407-413). */
 int gpa_b200_routes(const GpaDims* dims, const void* saved, void* const* routes, void* stream);
+
+/* Device status of the tensor-core kernels (no counterpart in the reference): 0, or
+ * GPA_B200_DEVICE_TIMEOUT once a bounded wait inside one of them gave up since the
+ * last clear (that kernel returned without its result).  Reads the device word
+ * synchronously (the device must be current); clear != 0 resets it.  -1 if the
+ * read failed. */
+int gpa_b200_device_status(int clear);
+
+/* Self-test of the tensor-core building blocks (no counterpart in the reference):
+ * one CTA computes D = A B on the 5th-generation tensor cores (tcgen05.mma, bf16
+ * operands in shared memory, fp32 accumulator in tensor memory).  A [M x Kd] and
+ * B [Kd x N] are row-major bf16 device arrays, D [M x N] fp32; mma_m (64 or 128)
+ * is the instruction's M (rows >= M are zero); a_mn / b_mn select the MN-major
+ * operand layouts; with a_bulk, A is read instead from A_tiled, its 128-row
+ * K-major or MN-major shared-memory image, by one bulk (TMA) copy.  *status
+ * (device int) is set to GPA_B200_DEVICE_TIMEOUT if a wait gave up.  Returns
+ * GPA_B200_UNSUPPORTED for shapes outside M <= mma_m, 16 <= N <= 256,
+ * 16 <= Kd <= 128 (multiples of 16). */
+int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int a_bulk,
+                           const void* A, const void* B, const void* A_tiled, float* D,
+                           int* status, void* stream);
 
 /* Message of the last failure on the calling thread (0 if none). */
 int gpa_b200_last_error(char* buf, size_t len);

@@ -120,9 +120,9 @@ def test_workspace_queries_and_argument_errors():
         _lib.check(rc, "gpa_b200_forward")
 
 
-def test_config2_workspaces_fit_one_b200():
-    """The forward's saved buffer and the backward scratch of BASELINE config 2 (B=8, T=8192,
-    H=16, 128/128, slots 64/64/64/128, chunk 64, bf16) leave most of a 180 GB B200 to the
+def test_bench_layer_workspaces_fit_one_b200():
+    """The forward's saved buffer and the backward scratch of the benched training step (B=8,
+    T=8192, H=16, 128/128, slots 64/64/64/128, chunk 64, bf16) leave most of a 180 GB B200 to the
     caller's tensors; a width above the supported 128 reports no size (unsupported)."""
     lib = _lib.load()
     d = _lib.GpaDims()
@@ -136,3 +136,12 @@ def test_config2_workspaces_fit_one_b200():
     assert 0 < saved + scratch + io < 110e9
     d.slots[3] = 256
     assert lib.gpa_b200_saved_bytes(d) == 0 and lib.gpa_b200_scratch_bytes(d) == 0
+
+
+def test_umma_selftest_rejects_unsupported_shapes_on_the_host():
+    """Shape checks run before any CUDA call, so they answer without a GPU."""
+    lib = _lib.load()
+    for shape in ((129, 128, 64, 64), (64, 96, 64, 64), (64, 128, 8, 64), (64, 128, 64, 40),
+                  (64, 128, 64, 256)):
+        rc = lib.gpa_b200_umma_selftest(*shape, 0, 0, 0, 1, 1, 1, 1, 1, None)
+        assert rc == 2, shape
