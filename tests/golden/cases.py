@@ -12,9 +12,12 @@ import hashlib
 
 import torch
 
-# name -> spec.  dims: heads, key_dim, value_dim, slots, chunk_size.
+# name -> spec.  dims: heads, key_dim, value_dim, slots, chunk_size.  ``execution`` (default
+# "reference") selects the reference's schedule: "packed" (src/gpa/packed.py, taken for uniform
+# slots) or "staged" (src/gpa/staged.py, taken for uniform slots with key_dim == slots[0] on
+# runs of >= 4 whole chunks starting at a block boundary).
 CASES = {
-    # fp32, chunk 1, B=2, T=16, H=4, 32/48, slots (64,64,64,128)
+    # fp32, chunk 1, B=2, T=16, H=4, 32/48, slots (64,64,64,128): the reference's CPU-runnable case
     "config1": dict(cfg=dict(heads=4, key_dim=32, value_dim=48, slots=(64, 64, 64, 128),
                              chunk_size=1), batch=2, length=16, dtype="float32", seed=0,
                     reference_init=True, decode=1),
@@ -34,10 +37,26 @@ CASES = {
     "chunk64_f32": dict(cfg=dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
                                  chunk_size=64), batch=1, length=130, dtype="float32", seed=5,
                         prefix_std=.02, partitions=((0, 47), (47, 65), (65, 130)), decode=1),
-    # config-2 head shape (D=Dv=128, slots (64,64,64,128)), bf16 activations, fp32 state
+    # the benched head shape (D=Dv=128, slots (64,64,64,128)), bf16 activations, fp32 state
     "c2head_bf16": dict(cfg=dict(heads=2, key_dim=128, value_dim=128, slots=(64, 64, 64, 128),
                                  chunk_size=64), batch=1, length=80, dtype="bfloat16", seed=7,
                         prefix_std=.02, unit_qk=True, decode=1),
+    # uniform slots through the reference's packed schedule (src/gpa/attention.py:301-303)
+    "packed_uniform": dict(cfg=dict(heads=2, key_dim=16, value_dim=12, slots=(16, 16, 16),
+                                    chunk_size=8), execution="packed", batch=2, length=37,
+                           dtype="float32", seed=21, prefix_std=.02,
+                           partitions=((0, 11), (11, 12), (12, 37)), decode=2),
+    # uniform slots with key_dim == slots[0]: the reference's staged schedule runs the first
+    # 256 tokens (src/gpa/attention.py:370-373), its lag-block path the 44-token tail
+    "staged_uniform": dict(cfg=dict(heads=2, key_dim=32, value_dim=24, slots=(32, 32, 32, 32),
+                                    chunk_size=64), execution="staged", batch=1, length=300,
+                           dtype="float32", seed=22, prefix_std=.02, decode=1),
+    # the staged schedule in bf16 rounds at other points than the lag-block schedule that the
+    # oracle restates: token-summed scalar parameter gradients (edge_logits) differ by ~2.3e-2
+    "staged_bf16": dict(cfg=dict(heads=2, key_dim=64, value_dim=64, slots=(64, 64, 64, 64),
+                                 chunk_size=64), execution="staged", batch=1, length=320,
+                        dtype="bfloat16", seed=23, prefix_std=.02, unit_qk=True, decode=1,
+                        oracle_param_tol=5e-2),
 }
 
 DTYPES = {"float32": torch.float32, "float64": torch.float64, "bfloat16": torch.bfloat16}
@@ -67,7 +86,7 @@ def build(name: str):
     b, t, h = spec["batch"], spec["length"], cfg["heads"]
     d, dv = cfg["key_dim"], cfg["value_dim"]
     if spec.get("reference_init"):
-        # BASELINE config 1 draws q, k, v right after the model under seed 0.
+        # the reference's CPU-runnable case draws q, k, v right after the model under seed 0
         q = torch.randn(b, t, h, d)
         k = torch.randn(b, t, h, d)
         v = torch.randn(b, t, h, dv)

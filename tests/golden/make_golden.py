@@ -44,7 +44,7 @@ def run_case(gpa, name):
         same = all(torch.equal(fresh.state_dict()[k], params[k]) for k in params)
         record["reference_init_matches"] = bool(same)
         assert same, "oracle.init_parameters does not reproduce the reference draw order"
-    model = gpa.DenseGPA(gpa.GPAConfig(**cfg))
+    model = gpa.DenseGPA(gpa.GPAConfig(**cfg, execution=spec.get("execution", "reference")))
     if dtype == torch.float64:
         model = model.double()
     missing = model.load_state_dict(params, strict=True)

@@ -18,7 +18,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from gpa_b200.dist import allreduce_gradients, batch_shard, head_slice
+from gpa_b200.dist import (allreduce_gradients, batch_shard, head_axis, head_parallel_state_dict,
+                           head_slice)
 
 CFG = oracle.OracleConfig(heads=2, key_dim=8, value_dim=8, slots=(4, 8), chunk_size=4)
 
@@ -129,3 +130,56 @@ def test_allreduce_without_process_group_is_a_no_op():
     before = m.weight.grad.clone()
     assert allreduce_gradients(m) == 0
     assert torch.equal(m.weight.grad, before)
+
+
+def _head_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        xs = _inputs()
+        params = _params()
+        full = _Params(params)
+        full.zero_grad(set_to_none=True)
+        out_full, _ = oracle.forward(CFG, full.as_oracle(), *xs)
+        (out_full * out_full).sum().backward()
+        hs = head_slice(CFG.heads, world, rank)
+        local_cfg = oracle.OracleConfig(**{**CFG.__dict__, "heads": hs.stop - hs.start})
+        local = _Params(head_parallel_state_dict(params, hs))
+        out, _ = oracle.forward(local_cfg, local.as_oracle(), *(x[:, :, hs] for x in xs))
+        (out * out).sum().backward()
+        # outputs of all ranks, gathered along heads, are the full model's output
+        parts = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(parts, out.contiguous())
+        err_out = float((torch.cat(parts, 2) - out_full).abs().max())
+        # local gradients are the full gradients' head slice: no reduction needed
+        err_grad = 0.0
+        for n, p in local.p.items():
+            name = n.replace("__", ".")
+            if full.p[n].grad is None:  # a parameter the default flags never read
+                assert p.grad is None
+                continue
+            ref = full.p[n].grad.narrow(head_axis(name), hs.start, hs.stop - hs.start)
+            err_grad = max(err_grad, float((p.grad - ref).abs().max()))
+        q.put((rank, err_out, err_grad))
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_parallel_ranks_compute_the_full_model():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_head_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err_out, err_grad in results:
+        assert err_out is not None, (rank, err_grad)
+        assert err_out < 1e-12 and err_grad < 1e-12, (rank, err_out, err_grad)

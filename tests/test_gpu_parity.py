@@ -148,7 +148,7 @@ def test_golden_reference_vectors(name, cpu_threads):
     cfg, params, inputs = build(name)
     dt = torch.bfloat16 if spec["dtype"] == "bfloat16" else torch.float32
     tol = BF16_TOL if dt == torch.bfloat16 else FP32_TOL
-    model = DenseGPA(GPAConfig(**cfg)).cuda()
+    model = DenseGPA(GPAConfig(**cfg, execution=spec.get("execution", "reference"))).cuda()
     model.load_state_dict({k: v.float() for k, v in params.items()})
     q, k, v = (inputs[x].to(dt).cuda().requires_grad_() for x in ("q", "k", "v"))
     out, st = model(q, k, v)
@@ -156,9 +156,19 @@ def test_golden_reference_vectors(name, cpu_threads):
     assert compare_summary(out.float().cpu(), rec["out"]) <= tol
     for x, t in zip("qkv", (q, k, v)):
         assert compare_summary(t.grad.float().cpu(), rec["grad_inputs"][x]) <= tol, x
-    if dt == torch.float32:
-        for n, g in rec["grad_params"].items():
-            assert compare_summary(dict(model.named_parameters())[n].grad.cpu(), g) <= tol, n
+    grads = {n: p.grad.cpu() for n, p in model.named_parameters() if p.grad is not None}
+    bad = {n: compare_summary(grads[n], g) for n, g in rec["grad_params"].items()
+           if not compare_summary(grads[n], g) <= tol}
+    if bad and dt == torch.bfloat16:
+        # bf16: a token-summed parameter gradient may instead be within max(2e-2, 2.5 x the bf16
+        # reference's own error) of the exact (fp64) value.  The golden loss reads the output of
+        # one short sequence only, so the relation gradients are small sums dominated by bf16
+        # rounding: on the benched head shape (T=80) the reference's own bf16 relation-prefix and
+        # edge-scalar gradients are 2.4-27 % off fp64, and this backend's 5-7 %.
+        exact = _golden_f64_param_grads(name)
+        bad = {n: e for n, e in bad.items()
+               if not rel(grads[n], exact[n]) <= max(tol, 2.5 * compare_summary(exact[n], rec["grad_params"][n]))}
+    assert not bad, bad
     for i, (a, b) in enumerate(zip(tensors(st), rec["state"])):
         assert compare_summary(a.cpu(), b) <= tol, f"state[{i}]"
     meta = rec["state_meta"]
@@ -186,6 +196,17 @@ def test_golden_reference_vectors(name, cpu_threads):
                 assert compare_summary(a.cpu(), b) <= tol, f"decode_state[{i}]"
             dm = rec["decode_meta"]
             assert running.position == dm["position"] and running.chunk_offset == dm["chunk_offset"]
+
+
+def _golden_f64_param_grads(name):
+    """Parameter gradients of a golden case's loss, out.float().square().mean(), from the oracle
+    in float64 on the case's own parameters and inputs."""
+    cfg, params, inputs = build(name)
+    p = {n: t.double().clone().requires_grad_() for n, t in params.items()}
+    xs = [inputs[x].double().clone().requires_grad_() for x in ("q", "k", "v")]
+    out, _ = oracle.forward(oracle.OracleConfig(**cfg), p, *xs)
+    out.square().mean().backward()
+    return {n: t.grad for n, t in p.items() if t.grad is not None}
 
 
 # ------------------------------------------------------- cache and call contracts
@@ -250,7 +271,8 @@ def _rebuild(state, flat):
 
 
 def test_config1_forward_backward_and_decode(cpu_threads):
-    """BASELINE config 1 on the GPU: fwd, out.square().mean() bwd, one-token decode."""
+    """H=4, Dk=32, Dv=48, slots (64,64,64,128), chunk 1, B=2, T=16 in fp32 on the GPU: fwd,
+    out.square().mean() bwd, one-token decode."""
     torch.manual_seed(0)
     cfg = dict(heads=4, key_dim=32, value_dim=48, slots=(64, 64, 64, 128), chunk_size=1)
     model = DenseGPA(GPAConfig(**cfg)).cuda()

@@ -49,7 +49,9 @@ def _call(lib, model, q, k, v, state, noalloc: bool):
         _lib.check(rc, "gpa_b200_forward_noalloc")
     else:
         nbytes = lib.gpa_b200_saved_bytes(plan.dims)
-        saved = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
+        # all bytes 0xFF (an fp32 NaN): a read of any region this call did not write first
+        # would poison the compared outputs
+        saved = torch.full((nbytes,), 255, device=q.device, dtype=torch.uint8)
         rc = lib.gpa_b200_forward(*args, saved.data_ptr(), nbytes, _stream(q.device))
         _lib.check(rc, "gpa_b200_forward")
     torch.cuda.synchronize()
@@ -83,6 +85,10 @@ def test_noalloc_forward_matches_caller_buffer_forward(dtype):
     prefill = [torch.randn(1, 9, 4, 32, generator=g).to("cuda", dtype) for _ in range(3)]
     step = [torch.randn(1, 1, 4, 32, generator=g).to("cuda", dtype) for _ in range(3)]
     with torch.no_grad():
+        # a larger call first leaves unrelated values all over the shared array, so the
+        # compared calls below only match if they write every part of it that they read
+        big = [torch.randn(2, 48, 4, 32, generator=g).to("cuda", dtype) for _ in range(3)]
+        _call(lib, model, *big, model.initial_state(2, device="cuda", dtype=dtype), noalloc=True)
         state = model.initial_state(1, device="cuda", dtype=dtype)
         ref_state = new_state = state
         for xs in (prefill, step):  # two calls in a row, the second continuing the cache
