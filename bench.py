@@ -1,24 +1,29 @@
 #!/usr/bin/env python
-"""DenseGPA fwd+bwd throughput on B200 (BASELINE config 2), one process per GPU.
+"""DenseGPA fwd+bwd throughput on B200, one process per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--scaling weak|strong] [--workload train|decode]
     torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
 
-Workload per rank (weak scaling): H=16, Dk=Dv=128, slots (64,64,64,128),
-chunk 64, B=8, T=8192, bf16 activations, fp32 state; q, k ~ N(0,1)
-L2-normalised per head, v ~ N(0,1), learnable prefixes re-drawn at N(0,0.02);
-seed 0 (data seeded 1000 + rank).  One step = forward, out.float().square().mean(),
-backward (every parameter, input and prefix gradient); with N > 1 the
-parameter gradients are all-reduced over NCCL (data parallel), the only
-cross-GPU exchange the path has.
+Training workload: one DenseGPA layer with H=16, Dk=Dv=128, slots (64,64,64,128),
+chunk 64, T=8192, bf16 activations, fp32 state; q, k ~ N(0,1) L2-normalised per
+head, v ~ N(0,1), learnable prefixes re-drawn at N(0,0.02); seed 0.  One step =
+forward, out.float().square().mean(), backward (every parameter, input and prefix
+gradient).
+  * weak scaling (default): every rank runs B=8 (data seeded 1000 + rank) and the
+    parameter gradients are all-reduced over NCCL once per step (data parallel),
+    the only cross-GPU exchange the path has; the all-reduce is timed separately;
+  * strong scaling: one global B=8 x H=16 problem, each rank owning a contiguous
+    head slice of every parameter and of the inputs (16/N heads, all 8 batch
+    rows); head slices never interact, so the step has no collective at all.
 
 Prints one JSON line (rank 0).  ``value`` is the device-timed tokens/s of the
-whole job with inputs resident in HBM (inputs are 805 MB per rank, larger than
-the 126 MB L2, and each step streams tens of GB of activations, so no L2 flush
-is needed); ``e2e`` is the same step through the public API with the inputs
-copied from pinned host memory and the loss read back every step.
-``--impl reference`` times the reference algorithm's CPU implementation (the
-test oracle, a restatement of the reference torch backend) on the host cores.
+whole job with inputs resident in HBM (inputs are 805 MB per B=8 rank, larger than
+the 126 MB L2, and each step streams tens of GB of activations, so no L2 flush is
+needed); ``e2e`` is the same step through the public API with the inputs copied
+from pinned host memory and the loss read back every step.  ``--impl reference``
+times the reference algorithm's CPU implementation (the test oracle, a
+restatement of the reference torch backend) on the host cores.
 """
 from __future__ import annotations
 
@@ -41,11 +46,13 @@ METRIC = "DenseGPA fwd+bwd tokens/s at 1/2/4/8 B200 (T=8192) + % of roofline"
 CFG = dict(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
 BATCH, LENGTH = 8, 8192
 CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
-# DRAM bytes moved per algorithmic byte, measured with ncu on a small case of the same kernel
-# (profiles/tc_bwd_chunk_small.md: 246.4 MB over 1024 blocks of (K, V) = (64, 64) scans and
-# 183.1 MB over 512 blocks of (128, 64), against 238.8 and 353.5 KB of algorithmic bytes per
-# block); the traffic of a full launch is its algorithmic bytes times this ratio.
-TRAFFIC_RATIO = {"tc_bwd_chunk": 1.01}
+# DRAM bytes per algorithmic byte of tc_bwd_chunk, from an ncu capture of a small case of the
+# same kernel (B=1, T=2048 of the same layer); a full launch's traffic is its algorithmic
+# bytes times this ratio.
+TRAFFIC_RATIO = {"tc_bwd_chunk": 1.00}
+# kernels of the chunked GDN scans: tensor-core bound by their algorithmic FLOPs
+CHUNK_KERNELS = ("tc_fwd_chunk", "tc_fwd_state", "tc_fwd_out", "tc_bwd_local", "tc_bwd_state",
+                 "tc_bwd_chunk")
 
 
 def peaks():
@@ -132,9 +139,10 @@ def kernel_flops(cfg, units, length):
 
 
 def kernel_bytes(cfg, units, length):
-    """Algorithmic HBM bytes per training step of the kernels whose bound is memory.
+    """HBM bytes per training step of the intermediates that tc_bwd_chunk streams (this
+    design's own fp32 terms, not the layer's algorithmic I/O).
 
-    tc_bwd_chunk, per block of c tokens of a (K, V) scan: reads k, Wk, the dk partial and the
+    Per block of c tokens of a (K, V) scan: reads k, Wk, the dk partial and the
     accumulated dk (c K each, fp32), dW, U, v and the accumulated dv (c V each, fp32), W (c V,
     bf16), the state snapshot S and its gradient D (K V each, fp32), T (c^2, fp32; A is formed
     again from k), and the gates and the dG partial (3 c); writes dk (c K), dv (c V), dg and
@@ -230,24 +238,55 @@ def make_inputs(batch, length, seed, device="cpu", dtype=torch.bfloat16, cfg=CFG
     return [x.to(dtype).to(device) for x in (q, k, v)]
 
 
+def reader_bytes_per_token_head(cfg):
+    """Standalone dense reader, per (token, head): read the base logits (sum_i M_i), the
+    incoming messages (sum_j (L-1) M_j), write the routes (sum_i M_i), all fp32."""
+    M, L = cfg["slots"], len(cfg["slots"])
+    return 4 * (2 * sum(M) + (L - 1) * sum(M))
+
+
+def build_rank_model(args, rank, world, device):
+    """(model, heads on this rank, batch on this rank) for the scaling mode."""
+    from gpa_b200 import DenseGPA, GPAConfig
+    from gpa_b200.dist import head_parallel_state_dict, head_slice
+    if args.scaling == "weak" or world == 1:
+        return make_model(device), CFG["heads"], BATCH
+    hs = head_slice(CFG["heads"], world, rank)
+    full = make_model("cpu")
+    cfg = dict(CFG, heads=hs.stop - hs.start)
+    model = DenseGPA(GPAConfig(**cfg))
+    model.load_state_dict(head_parallel_state_dict(full.state_dict(), hs))
+    return model.to(device), cfg["heads"], BATCH
+
+
 def run_b200(args, rank, world, local):
     from gpa_b200 import _lib
     from gpa_b200.dist import allreduce_gradients
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    model = make_model(device)
-    q, k, v = make_inputs(BATCH, LENGTH, 1000 + rank, device)
+    model, heads, batch = build_rank_model(args, rank, world, device)
+    cfg = dict(CFG, heads=heads)
+    reduce_grads = args.scaling == "weak" and world > 1
+    q, k, v = make_inputs(batch, LENGTH, 1000 + rank, device, cfg=cfg)
     for x in (q, k, v):
         x.requires_grad_(True)
+    stream = torch.cuda.current_stream()
+    ar_events = []  # (start, end) of each timed step's all-reduce
 
-    def step():
+    def step(timed=False):
         model.zero_grad(set_to_none=True)
         for x in (q, k, v):
             x.grad = None
         out, _ = model(q, k, v)
         loss = out.float().square().mean()
         loss.backward()
-        allreduce_gradients(model)
+        if reduce_grads:
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(stream)
+            allreduce_gradients(model)
+            e[1].record(stream)
+            if timed:
+                ar_events.append(e)
         return loss
 
     def barrier():
@@ -259,14 +298,13 @@ def run_b200(args, rank, world, local):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream()
     launches0 = _lib.launch_count()
     _lib.profile_start()
     with ClockSampler(local) as clocks:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            step(timed=True)
         ev1.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -274,10 +312,11 @@ def run_b200(args, rank, world, local):
     prof = _lib.profile_stop()
     launches = _lib.launch_count() - launches0
     ms = ev0.elapsed_time(ev1) / args.steps
-    ms_all = torch.tensor([ms], device=device)
+    ar_ms = sum(a.elapsed_time(b) for a, b in ar_events) / args.steps if ar_events else 0.0
+    ms_all = torch.tensor([ms, ar_ms], device=device)
     if world > 1:
         dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
-    ms = float(ms_all.item())
+    ms, ar_ms = float(ms_all[0].item()), float(ms_all[1].item())
 
     # end-to-end through the public API with pinned host inputs: every step's q, k, v are
     # copied host -> device (double-buffered, on a copy stream, while the previous step
@@ -305,7 +344,8 @@ def run_b200(args, rank, world, local):
         out, _ = model(*xs)
         loss = out.float().square().mean()
         loss.backward()
-        allreduce_gradients(model)
+        if reduce_grads:
+            allreduce_gradients(model)
         return loss.item()
 
     issue_copy(0)
@@ -328,72 +368,94 @@ def run_b200(args, rank, world, local):
         dist.all_reduce(e2e_all, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_all.item())
 
-    tokens = BATCH * LENGTH * world
+    strong = args.scaling == "strong"
+    tokens = batch * LENGTH * (1 if strong else world)
     value = tokens / (ms / 1e3)
     pk = peaks()
-    units = BATCH * CFG["heads"]
-    kf = kernel_flops(CFG, units, LENGTH)
-    kb = kernel_bytes(CFG, units, LENGTH)
-    # dominant kernel by device time
+    units = batch * heads
+    kf = kernel_flops(cfg, units, LENGTH)
+    kb = kernel_bytes(cfg, units, LENGTH)
+    per_step_ms = {n: round(t / args.steps, 3) for n, (c, t) in prof.items()}
+    # dominant kernel by device time; the chunked-scan kernels are tensor-core bound on their
+    # algorithmic FLOPs, timed inside a long step: the sustained bf16 peak is the denominator
     top = max(prof, key=lambda n: prof[n][1])
     n_launch, tot_ms = prof[top]
-    per_step_ms = {n: round(t / args.steps, 3) for n, (c, t) in prof.items()}
-    if top in kf:
-        # the bound is whichever of the algorithmic FLOPs and bytes needs more time at peak
-        step_s = tot_ms / args.steps / 1e3
-        lps = n_launch / args.steps
-        t_flop = kf[top] / (pk["bf16_tflops"] * 1e12)
-        t_byte = kb.get(top, 0) / (pk["hbm_gbs"] * 1e9)
-        traffic = None
-        if top in TRAFFIC_RATIO:
-            traffic = round(kb[top] / lps * TRAFFIC_RATIO[top])
-        if t_byte >= t_flop:
-            achieved = kb[top] / step_s / 1e9
-            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
-                    "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4)}
-        else:
-            achieved = kf[top] / step_s / 1e12
-            roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": pk["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 5)}
-        roof.update({"traffic": traffic,
-                     "traffic_source": "algorithmic bytes x DRAM/algorithmic ratio of an ncu small case",
-                     "kernel": top, "launches_per_step": round(lps),
-                     "avg_launch_ms": round(tot_ms / n_launch, 4),
-                     "bytes_per_step": kb.get(top), "flops_per_step": kf[top],
-                     "tensor_frac": round(kf[top] / step_s / 1e12 / pk["bf16_tflops"], 5),
-                     "peak_source": pk["source"]})
+    step_s = tot_ms / args.steps / 1e3
+    lps = n_launch / args.steps
+    if top in CHUNK_KERNELS:
+        peak = pk["bf16_tflops_sustained"]
+        achieved = kf[top] / step_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 5),
+                "traffic": round(kb[top] / lps * TRAFFIC_RATIO[top]) if top in TRAFFIC_RATIO else None,
+                "traffic_unit": "DRAM bytes per launch",
+                "traffic_source": "algorithmic intermediate bytes per launch x the DRAM/algorithmic "
+                                  "ratio of an ncu capture of a small case of the same kernel",
+                "kernel": top, "launches_per_step": round(lps),
+                "avg_launch_ms": round(tot_ms / n_launch, 4), "flops_per_step": kf[top],
+                "flops_per_launch": round(kf[top] / lps),
+                "peak_which": "bf16_tflops_sustained (kernel timed inside a long step)",
+                "peak_source": pk["source"]}
+        if top in kb:
+            gbs = kb[top] / step_s / 1e9
+            roof["intermediates_hbm"] = {
+                "bytes_per_step": kb[top], "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
+                "note": "bytes of this design's own fp32 intermediates (k, Wk, U, dW, S and D "
+                        "snapshots, T) that the kernel streams, not the layer's algorithmic I/O"}
     else:
-        roof = {"bound": "tensor", "achieved": None, "peak": pk["bf16_tflops"],
+        roof = {"bound": "tensor", "achieved": None, "peak": pk["bf16_tflops_sustained"],
                 "unit": "TFLOP/s", "frac": None, "traffic": None, "kernel": top,
                 "peak_source": pk["source"]}
-    step_flops = 3 * layer_flops_per_token_head(CFG) * CFG["heads"] * BATCH * LENGTH
+    reader = None
+    if "tc_bridge" in prof:
+        rb = reader_bytes_per_token_head(cfg) * units * LENGTH
+        r_s = prof["tc_bridge"][1] / args.steps / 1e3
+        reader = {"bound": "hbm", "kernel": "tc_bridge", "bytes_per_step": rb,
+                  "bytes_per_token_head": reader_bytes_per_token_head(cfg),
+                  "ms_per_step": round(r_s * 1e3, 3), "achieved": round(rb / r_s / 1e9, 1),
+                  "peak": pk["hbm_gbs"], "unit": "GB/s",
+                  "frac": round(rb / r_s / 1e9 / pk["hbm_gbs"], 4),
+                  "note": "forward dense reader (edge mix, centred tanh, route softmax, route MLP "
+                          "and query projection of every level) against the standalone reader's "
+                          "bytes: base logits and messages read, routes written, fp32"}
+    step_flops = 3 * layer_flops_per_token_head(cfg) * heads * batch * LENGTH
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), q/k L2-normalised; random-init weights, prefixes N(0,0.02))",
-        "config": {"workload": "config 2: DenseGPA layer fwd+bwd", "model": "DenseGPA",
-                   "global_batch": BATCH * world, "seq_len": LENGTH, "heads": CFG["heads"],
+        "config": {"workload": "DenseGPA layer fwd+bwd, H=16, Dk=Dv=128, slots 64/64/64/128, "
+                               "chunk 64, B=8, T=8192" + (" (global, head-sharded)" if strong else
+                                                          " per rank"),
+                   "model": "DenseGPA", "global_batch": batch * (1 if strong else world),
+                   "seq_len": LENGTH, "heads": CFG["heads"], "heads_per_rank": heads,
                    "key_dim": CFG["key_dim"], "value_dim": CFG["value_dim"],
                    "slots": list(CFG["slots"]), "chunk_size": CFG["chunk_size"],
-                   "state_dtype": "fp32", "parallelism": f"dp{world} (batch x heads per rank)",
-                   "l2": "inputs 805 MB/rank > 126 MB L2; no flush"},
+                   "state_dtype": "fp32",
+                   "parallelism": (f"head-parallel {world} (16/{world} heads x all batch rows per "
+                                   "rank, no collective)") if strong else
+                                  f"dp{world} (batch rows per rank, gradient all-reduce)",
+                   "l2": f"inputs {h2d / 1e6:.0f} MB/rank > 126 MB L2; no flush"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "note": "each step's inputs copied from pinned host memory on a copy stream "
                         "during the previous step (double buffer); loss read back every step"},
         "gpu_launches": launches,
         "roofline": roof,
+        "reader_roofline": reader,
         "step_roofline": {"flops_per_step": step_flops,
                           "achieved_tflops": round(step_flops / (ms / 1e3) / 1e12, 3),
                           "frac_of_bf16_peak": round(step_flops / (ms / 1e3) / 1e12 / pk["bf16_tflops_sustained"], 5)},
+        "allreduce_ms_per_step": round(ar_ms, 3) if reduce_grads else None,
         "kernel_ms_per_step": per_step_ms,
         "clocks": clocks.summary(),
     }
     return result
 
 
-# --------------------------------------------------------------- decode (config 4)
+# --------------------------------------------------------------- decode
 
 DECODE_BATCHES = (1, 64, 256)
 DECODE_PREFILL = 4096
@@ -416,7 +478,8 @@ def decode_param_bytes(cfg):
 
 
 def run_decode(args):
-    """Config 4: config 2's layer, prefill 4096 tokens, one-token steps under a CUDA graph."""
+    """The training layer decoding: prefill 4096 tokens, then one-token steps replayed from a
+    CUDA graph at each batch size."""
     from gpa_b200 import _lib
     from gpa_b200.decode import DecodeSession
     dev = torch.device("cuda", 0)
@@ -482,17 +545,17 @@ def run_decode(args):
     Bt = batches[-1]
     h2d = 2 * Bt * H * (2 * D + Dv)
     result = {
-        "metric": "DenseGPA decode tokens/s (config 4: config-2 layer, prefill 4096, CUDA graph)",
+        "metric": "DenseGPA decode tokens/s (H=16, Dk=Dv=128, slots 64/64/64/128, prefill 4096, CUDA graph)",
         "value": top["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": max(args.steps, 64),
         "warmup": max(args.warmup, 3), "ms_per_step": round(top["us_per_step"] / 1e3, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, random-init weights)",
-        "config": {"workload": f"config 4 decode, B={Bt}", "model": "DenseGPA", "global_batch": Bt,
+        "config": {"workload": f"one-token decode steps, B={Bt}", "model": "DenseGPA", "global_batch": Bt,
                    "seq_len": 1, "prefill": args.prefill, "state_dtype": "fp32",
                    "l2": f"cache {Bt * H * per_unit / 1e9:.2f} GB per step > 126 MB L2; no flush"},
         "e2e": {"value": top["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": Bt * H * Dv * 2},
-        "gpu_launches": 2,
+        "gpu_launches": 1,
         "roofline": {"bound": "hbm", "achieved": top["achieved_gbs"], "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": top["frac"], "traffic": None, "kernel": "decode_step",
                      "bytes_per_step": top["bytes_per_step"], "peak_source": pk["source"]},
@@ -504,16 +567,23 @@ def run_decode(args):
 
 # --------------------------------------------------------------- CPU (oracle) arm
 
-def cpu_sample_step(threads):
-    """One fwd+bwd of the reference algorithm (oracle) on the bounded CPU sample."""
+def _oracle_cfg(cfg):
+    import oracle
+    return oracle.OracleConfig(heads=cfg["heads"], key_dim=cfg["key_dim"],
+                               value_dim=cfg["value_dim"], slots=cfg["slots"],
+                               chunk_size=cfg["chunk_size"])
+
+
+def cpu_sample_step(threads, dtype=torch.bfloat16, batch=None, length=None):
+    """One fwd+bwd of the reference algorithm (oracle) on a bounded CPU sample of the layer."""
     import oracle
     torch.set_num_threads(threads)
     model = make_model("cpu")
     p = {n: t.detach().clone().requires_grad_() for n, t in model.state_dict().items()}
-    ocfg = oracle.OracleConfig(heads=CFG["heads"], key_dim=CFG["key_dim"],
-                               value_dim=CFG["value_dim"], slots=CFG["slots"],
-                               chunk_size=CFG["chunk_size"])
-    xs = [x.requires_grad_() for x in make_inputs(CPU_SAMPLE["batch"], CPU_SAMPLE["length"], 1000)]
+    ocfg = _oracle_cfg(CFG)
+    xs = [x.requires_grad_() for x in make_inputs(batch or CPU_SAMPLE["batch"],
+                                                   length or CPU_SAMPLE["length"], 1000,
+                                                   dtype=dtype)]
 
     def step():
         for t in list(p.values()) + xs:
@@ -524,17 +594,65 @@ def cpu_sample_step(threads):
     return step
 
 
-def cpu_baseline(threads):
-    step = cpu_sample_step(threads)
-    step()
+def _timed(fn, reps=1):
+    fn()
     t0 = time.perf_counter()
-    step()
-    dt = time.perf_counter() - t0
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_legs(threads):
+    """Further CPU legs of the same reference algorithm, each a bounded sample."""
+    import oracle
+    torch.set_num_threads(threads)
+    legs = []
+    b, t = CPU_SAMPLE["batch"], CPU_SAMPLE["length"]
+    dt = _timed(cpu_sample_step(threads, torch.float32))
+    legs.append({"workload": f"training layer fwd+bwd, fp32 activations, B={b}, T={t}",
+                 "tokens_per_s": round(b * t / dt, 3), "seconds": round(dt, 3)})
+    # the reference's CPU-runnable case: H=4, Dk=32, Dv=48, slots (64,64,64,128), chunk 1,
+    # B=2, T=16, fp32; fwd, out.square().mean() bwd, then a one-token decode
+    torch.manual_seed(0)
+    c1 = oracle.OracleConfig(heads=4, key_dim=32, value_dim=48, slots=(64, 64, 64, 128))
+    p1 = {n: v.requires_grad_() for n, v in oracle.init_parameters(c1).items()}
+    x1 = [torch.randn(2, 16, 4, d).requires_grad_() for d in (32, 32, 48)]
+    x1d = [torch.randn(2, 1, 4, d) for d in (32, 32, 48)]
+
+    def c1_step():
+        out, st = oracle.forward(c1, p1, *x1)
+        out.square().mean().backward()
+        with torch.no_grad():
+            oracle.forward(c1, p1, *x1d, oracle.OracleState(
+                tuple(tuple(z.detach() for z in lv) for lv in st.levels),
+                tuple(z.detach() for z in st.relations), st.position, st.chunk_size,
+                st.chunk_offset, None))
+    dt = _timed(c1_step)
+    legs.append({"workload": "H=4, Dk=32, Dv=48, slots 64/64/64/128, chunk 1, B=2, T=16, fp32: "
+                             "fwd+bwd and a one-token decode", "tokens_per_s": round(32 / dt, 3),
+                 "seconds": round(dt, 3)})
+    # one decode step of the training layer (B=1) after a 64-token prefill, fp32 state
+    model = make_model("cpu")
+    p = {n: v.detach() for n, v in model.state_dict().items()}
+    ocfg = _oracle_cfg(CFG)
+    with torch.no_grad():
+        _, st = oracle.forward(ocfg, p, *make_inputs(1, 64, 7))
+        xs = make_inputs(1, 1, 8)
+        dt = _timed(lambda: oracle.forward(ocfg, p, *xs, st), reps=3)
+    legs.append({"workload": "training layer, one-token decode step, B=1, after a 64-token "
+                             "prefill, bf16 activations / fp32 state",
+                 "tokens_per_s": round(1 / dt, 3), "seconds": round(dt, 4)})
+    return legs
+
+
+def cpu_baseline(threads):
+    dt = _timed(cpu_sample_step(threads))
     toks = CPU_SAMPLE["batch"] * CPU_SAMPLE["length"]
     return {"value": round(toks / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"oracle (restated reference torch backend) fwd+bwd, config-2 layer, "
+            "sample": f"oracle (restated reference torch backend) fwd+bwd of the training layer, "
                       f"B={CPU_SAMPLE['batch']}, T={CPU_SAMPLE['length']}, bf16 activations, "
-                      f"{dt:.2f} s"}
+                      f"{dt:.2f} s",
+            "legs": cpu_legs(threads)}
 
 
 def run_reference(args, rank):
@@ -554,7 +672,8 @@ def run_reference(args, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config 2: DenseGPA layer fwd+bwd (bounded CPU sample)",
+            "config": {"workload": "DenseGPA layer fwd+bwd, H=16, Dk=Dv=128, slots 64/64/64/128, "
+                                   "chunk 64 (bounded CPU sample)",
                        "model": "DenseGPA", "global_batch": CPU_SAMPLE["batch"],
                        "seq_len": CPU_SAMPLE["length"], "parallelism": "cpu"},
             "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
@@ -572,16 +691,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["train", "decode"], default="train",
-                    help="train: config-2 fwd+bwd (the headline); decode: config-4 one-token steps")
+                    help="train: layer fwd+bwd at B=8, T=8192 (the headline); decode: one-token steps")
     ap.add_argument("--decode-batches", default=",".join(str(b) for b in DECODE_BATCHES),
                     help="decode: batch sizes (the last one is the headline line)")
     ap.add_argument("--prefill", type=int, default=DECODE_PREFILL,
-                    help="decode: prefill length before the steps (config 4: 4096)")
+                    help="decode: prefill length before the steps (default 4096)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: B=8 per rank, data parallel; strong: global B=8 x 16 heads "
+                         "split by heads over the ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
-                    help="per-rank batch (default: config 2); smaller values are for profiling")
+                    help="per-rank batch (default 8); smaller values are for profiling")
     ap.add_argument("--length", type=int, default=LENGTH,
-                    help="sequence length (default: config 2); smaller values are for profiling")
+                    help="sequence length (default 8192); smaller values are for profiling")
     args = ap.parse_args()
     BATCH, LENGTH = args.batch, args.length
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -8,7 +8,8 @@ no communication in the forward.  Two layouts are supported:
   and all heads; parameters are replicated and their gradients are averaged
   once per step with one bucketed all-reduce (NCCL over NVLink on B200);
 * head parallel: a rank owns a contiguous head slice of every parameter (see
-  ``head_slice``); parameter gradients are then disjoint and need no reduction.
+  ``head_slice`` and ``head_parallel_state_dict``); parameter gradients are then
+  disjoint and need no reduction.
 """
 from __future__ import annotations
 
@@ -26,6 +27,28 @@ def batch_shard(batch: int, world: int, rank: int) -> slice:
 def head_slice(heads: int, world: int, rank: int) -> slice:
     """Contiguous heads owned by `rank` under head parallelism."""
     return batch_shard(heads, world, rank)
+
+
+# parameters whose head axis is dim 1 ([levels or edges, H, ...]); every other DenseGPA
+# parameter (per-level lists and relation prefixes) is [H, ...]
+_HEAD_DIM1 = ("residual_raw", "count_gain_raw", "moment_gain", "route_mlp_gain", "output_logits",
+              "edge_logits", "relation_gain", "relation_decay_raw", "relation_beta_raw")
+
+
+def head_axis(name: str) -> int:
+    """Axis of the head index in the DenseGPA parameter `name` (src/gpa/attention.py:104-135)."""
+    return 1 if name.split(".")[0] in _HEAD_DIM1 else 0
+
+
+def head_parallel_state_dict(state_dict: dict, heads: slice) -> dict:
+    """The parameters of a DenseGPA restricted to the head slice `heads`: load it into a
+    DenseGPA whose config has ``heads = heads.stop - heads.start`` (all else unchanged).  The
+    heads never interact, so that model computes exactly those heads of the full one."""
+    out = {}
+    for name, t in state_dict.items():
+        ax = head_axis(name)
+        out[name] = t.narrow(ax, heads.start, heads.stop - heads.start).contiguous()
+    return out
 
 
 def allreduce_gradients(module: torch.nn.Module, group=None, average: bool = True,

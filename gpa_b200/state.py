@@ -6,32 +6,39 @@ exactly like a reference cache.  ``detach()`` is explicit, never automatic.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, fields, is_dataclass
-from typing import Any
+from dataclasses import dataclass, fields, is_dataclass, replace
 
 from torch import Tensor
 
 
-def _map(value: Any, fn):
-    if isinstance(value, Tensor):
-        return fn(value)
-    if isinstance(value, tuple):
-        return tuple(_map(x, fn) for x in value)
-    if is_dataclass(value):
-        return type(value)(**{f.name: _map(getattr(value, f.name), fn) for f in fields(value)})
-    return value
+def _flatten(node):
+    """Split a cache tree into its tensors (depth first, fields in declaration order, the
+    order of src/gpa/state.py:16-24) and a function that builds the same tree around a new
+    sequence of tensors given in that order.  Ints, None and other leaves are kept."""
+    if isinstance(node, Tensor):
+        return [node], lambda it: next(it)
+    if isinstance(node, tuple) or is_dataclass(node):
+        names = None if isinstance(node, tuple) else [f.name for f in fields(node)]
+        parts = [_flatten(x) for x in (node if names is None else
+                                       (getattr(node, n) for n in names))]
+        leaves = [t for sub, _ in parts for t in sub]
+
+        def build(it):
+            kids = [make(it) for _, make in parts]
+            return tuple(kids) if names is None else replace(node, **dict(zip(names, kids)))
+        return leaves, build
+    return [], lambda it: node
+
+
+def _map(value, fn):
+    """The same tree with fn applied to every tensor."""
+    leaves, build = _flatten(value)
+    return build(iter([fn(t) for t in leaves]))
 
 
 def tensors(value):
     """Every tensor of a cache in field order (src/gpa/state.py:16-24)."""
-    if isinstance(value, Tensor):
-        yield value
-    elif isinstance(value, tuple):
-        for x in value:
-            yield from tensors(x)
-    elif is_dataclass(value):
-        for f in fields(value):
-            yield from tensors(getattr(value, f.name))
+    return iter(_flatten(value)[0])
 
 
 @dataclass(frozen=True)
