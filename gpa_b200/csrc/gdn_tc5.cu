@@ -110,9 +110,13 @@ GPA_DEV uint4 pack8(const float (&x)[8]) {
 // the 8 lanes of a shared-memory phase take 8 different t (conflict-free 16-byte stores).
 GPA_DEV void stage_to_tiles(const float* raw, int c, int K, bool kmajor, unsigned char* hi,
                             unsigned char* lo) {
+  // item i: row t = 8 * (i / (8 * k8n)) + j and column group k8 = (i / 8 + j) % k8n with
+  // j = i % 8: the 8 lanes of a shared-memory phase read 8 rows at 8 different column groups
+  // (2-way bank conflicts at most) and write 8 different core-matrix rows (none)
   const int k8n = K >> 3, n = C * k8n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int t = (i & 7) | ((i / (8 * k8n)) << 3), k8 = (i >> 3) % k8n;
+    const int j = i & 7, g = i >> 3, tq = g / k8n;
+    const int t = 8 * tq + j, k8 = (g - tq * k8n + j) % k8n;
     float x[8];
     if (t < c) {
       const float4 a = *reinterpret_cast<const float4*>(raw + t * K + 8 * k8);
@@ -120,7 +124,7 @@ GPA_DEV void stage_to_tiles(const float* raw, int c, int K, bool kmajor, unsigne
       x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = 0.f;
+      for (int q = 0; q < 8; ++q) x[q] = 0.f;
     }
     uint4 h, l;
     split8(x, h, l);
@@ -129,6 +133,14 @@ GPA_DEV void stage_to_tiles(const float* raw, int c, int K, bool kmajor, unsigne
     *reinterpret_cast<uint4*>(hi + o) = h;
     if (lo) *reinterpret_cast<uint4*>(lo + o) = l;
   }
+}
+
+// A global load issued exactly here (the compiler may not sink it to the value's first use):
+// the U values of the next block are in flight during this block's MMA 2 and epilogue 2.
+GPA_DEV float ld_pinned(const float* p) {
+  float x;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(x) : "l"(p));
+  return x;
 }
 
 struct LFwdSweep {
@@ -220,11 +232,10 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
   float ub[32];  // U[t][v] of this thread's 32 tokens of the coming epilogue 1
   auto load_u = [&](int n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
+    const float* up = d.Ub + row(u, T, t0 + 32 * half) * V + v;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = 32 * half + j;
-      ub[j] = (active && vok && t < c) ? d.Ub[row(u, T, t0 + t) * V + v] : 0.f;
-    }
+    for (int j = 0; j < 32; ++j)
+      ub[j] = (active && vok && 32 * half + j < c) ? ld_pinned(up + (int64_t)j * V) : 0.f;
   };
   float s[SH];
 #pragma unroll
@@ -287,10 +298,13 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
     tc5::fence_after_sync();
     if (active) {  // epilogue 1: W = U - acc; W out (bf16); lambda W hi / lo -> (lambda W)^T
 #pragma unroll
+      float acc2[2][16];
+      tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half), acc2[0]);
+      tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half + 16), acc2[1]);
+      tc5::tmem_wait_ld();
+#pragma unroll
       for (int c16 = 0; c16 < 2; ++c16) {
-        float acc[16];
-        tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half + 16 * c16), acc);
-        tc5::tmem_wait_ld();
+        const float(&acc)[16] = acc2[c16];
 #pragma unroll
         for (int j8 = 0; j8 < 2; ++j8) {
           float x[8];
@@ -337,6 +351,7 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
     tc5::fence_after_sync();
     const float gc = __expf(G[c - 1]);
     if (active) {  // epilogue 2: S <- e^{G_c} S + acc; boundary state out; S^T hi tile
+      // (the boundary stores stay here: issued under the next MMA they slowed the sweep down)
       float* sbn = d.Sb + ((int64_t)u * (bl.nb + 1) + n + 1) * KV;
 #pragma unroll
       for (int i = 0; i < SH; i += 16) {
