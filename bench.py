@@ -565,6 +565,103 @@ def run_decode(args):
     return result
 
 
+# --------------------------------------------------------------- all-GPA LM
+
+def run_lm(args, rank, world, local):
+    """Qwen3-0.6B-shaped all-GPA LM: a training step (fwd + bwd, per-layer checkpointing,
+    chunked loss; gradients all-reduced over the ranks) at B=8, T=8192 per rank on uniform
+    random token ids, then greedy generation of 256 tokens after a 512-token prompt."""
+    from gpa_b200 import _lib
+    from gpa_b200.dist import allreduce_gradients
+    from gpa_b200.lm import GPALM, GPALMConfig, num_parameters
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    torch.manual_seed(0)
+    cfg = GPALMConfig()
+    model = GPALM(cfg).to(device)
+    model.gradient_checkpointing = True
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (BATCH, LENGTH), device=device, generator=g)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        model.train()
+        model.zero_grad(set_to_none=True)
+        loss, _ = model(ids, labels=ids)
+        loss.backward()
+        allreduce_gradients(model)
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches0 = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = _lib.launch_count() - launches0
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    # end to end: the step's token ids copied from pinned host memory, the loss read back
+    host_ids = ids.cpu().pin_memory()
+    t0 = time.perf_counter()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    ids.copy_(host_ids, non_blocking=True)
+    loss_v = step().item()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3)
+    peak_gb = torch.cuda.max_memory_allocated(device) / 1e9
+    # greedy generation: 512-token prompt, 256 new tokens, fused one-kernel decode per layer
+    model.eval()
+    gen_b, prompt, new = BATCH, 512, 256
+    with torch.no_grad():
+        p_ids = ids[:gen_b, :prompt].contiguous()
+        model.generate(p_ids, 4)
+        torch.cuda.synchronize()
+        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e4.record(stream)
+        model.generate(p_ids, new)
+        e5.record(stream)
+        torch.cuda.synchronize()
+    gen_ms = e4.elapsed_time(e5)
+    tokens = BATCH * LENGTH * world
+    return {
+        "metric": "all-GPA Qwen3-0.6B-shaped LM train-step tokens/s (28 DenseGPA layers, T=8192)",
+        "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform random token ids; random-init weights)",
+        "config": {"workload": "all-GPA LM train step (fwd+bwd, per-layer checkpointing, chunked CE)",
+                   "model": "GPALM 28 x (hidden 1024, 16 heads x 128, 8 KV heads, SwiGLU 3072), "
+                            "vocab 151936, DenseGPA slots 64/64/64/128",
+                   "parameters": num_parameters(model), "global_batch": BATCH * world,
+                   "seq_len": LENGTH, "parallelism": f"dp{world}",
+                   "l2": "activations of tens of GB per step > 126 MB L2; no flush"},
+        "loss": round(loss_v, 4), "peak_memory_gb": round(peak_gb, 1),
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": host_ids.numel() * host_ids.element_size(),
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": launches // max(1, args.steps),
+        "generation": {"batch": gen_b, "prompt": prompt, "new_tokens": new,
+                       "ms": round(gen_ms, 1),
+                       "tokens_per_s": round(gen_b * new / (gen_ms / 1e3), 1),
+                       "note": "prompt prefill plus 255 fused decode steps (one DecodeSession "
+                               "kernel per layer and token) and the torch projections / MLP"},
+        "clocks": clocks.summary(),
+    }
+
+
 # --------------------------------------------------------------- CPU (oracle) arm
 
 def _oracle_cfg(cfg):
@@ -690,8 +787,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["train", "decode"], default="train",
-                    help="train: layer fwd+bwd at B=8, T=8192 (the headline); decode: one-token steps")
+    ap.add_argument("--workload", choices=["train", "decode", "lm"], default="train",
+                    help="train: layer fwd+bwd at B=8, T=8192 (the headline); decode: one-token "
+                         "steps; lm: the all-GPA Qwen-shaped LM train step and generation")
     ap.add_argument("--decode-batches", default=",".join(str(b) for b in DECODE_BATCHES),
                     help="decode: batch sizes (the last one is the headline line)")
     ap.add_argument("--prefill", type=int, default=DECODE_PREFILL,
@@ -721,8 +819,16 @@ def main():
     if world > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(minutes=10),
+        dist.init_process_group("nccl", timeout=timedelta(minutes=3),
                                 device_id=torch.device("cuda", local))
+    if args.workload == "lm":
+        res = run_lm(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res = run_b200(args, rank, world, local)
     if rank == 0:
         if not args.no_cpu_baseline:
