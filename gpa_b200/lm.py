@@ -257,7 +257,8 @@ class GPALM(nn.Module):
 
         The prompt runs as one cached call per layer; each new token then runs every layer
         once: with ``fused_decode`` through a DecodeSession per layer (one kernel per layer
-        and token, the cache in fixed buffers), else through one-token DenseGPA calls."""
+        and token, the cache in fixed buffers), the whole token step replayed from one CUDA
+        graph; else through one-token DenseGPA calls."""
         logits, cache = self.forward(ids, use_cache=True)
         nxt = logits[:, -1].argmax(-1)
         out = [nxt]
@@ -272,19 +273,22 @@ class GPALM(nn.Module):
         from .decode import DecodeSession
         sessions = [DecodeSession(blk.attn.gpa, m.state, torch.bfloat16)
                     for blk, m in zip(self.blocks, cache.layers)]
-        tails = [m.tail for m in cache.layers]
+        tails = [m.tail.clone() for m in cache.layers]  # updated in place by every step
         cfg = self.cfg
         h, kv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
-        for _ in range(max_new_tokens - 1):
-            x = self.embed(nxt[:, None])
+        tok = nxt.clone()  # the token fed to the next step; the step overwrites it
+
+        def one_token():
+            b = tok.shape[0]
+            x = self.embed(tok[:, None])
             with torch.autocast("cuda", dtype=torch.bfloat16):
                 for i, (blk, sess) in enumerate(zip(self.blocks, sessions)):
                     a = blk.attn
                     y = blk.input_norm(x)
                     proj = torch.cat((a.q_proj(y), a.k_proj(y), a.v_proj(y)), -1)
-                    proj, tails[i] = causal_conv(proj, a.conv, tails[i])
+                    proj, tail = causal_conv(proj, a.conv, tails[i])
+                    tails[i].copy_(tail)
                     q, k, v = proj.split((h * d, kv * d, kv * d), -1)
-                    b = x.shape[0]
                     q = a.q_norm(q.reshape(b, 1, h, d))
                     k = a.k_norm(k.reshape(b, 1, kv, d))
                     v = v.reshape(b, 1, kv, d)
@@ -293,8 +297,22 @@ class GPALM(nn.Module):
                     x = x + a.o_proj(o.reshape(b, 1, h * d).to(x.dtype))
                     x = x + blk.mlp(blk.post_norm(x))
                 x = self.norm(x)
-                nxt = self.lm_head(x[:, -1]).float().argmax(-1)
-            out.append(nxt)
+                tok.copy_(self.lm_head(x[:, -1]).float().argmax(-1))
+
+        # every decode step is the same sequence of launches on fixed buffers: record one in a
+        # CUDA graph (after an eager warm-up whose cache updates are undone) and replay it
+        live = [t for sess in sessions for t in sess._flat + [sess._offset]] + tails + [tok]
+        saved = [t.clone() for t in live]
+        one_token()
+        torch.cuda.synchronize()
+        for t, r in zip(live, saved):
+            t.copy_(r)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_token()
+        for _ in range(max_new_tokens - 1):
+            graph.replay()
+            out.append(tok.clone())
         return torch.stack(out, 1)
 
 
