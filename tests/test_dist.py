@@ -183,3 +183,18 @@ def test_head_parallel_ranks_compute_the_full_model():
     for rank, err_out, err_grad in results:
         assert err_out is not None, (rank, err_grad)
         assert err_out < 1e-12 and err_grad < 1e-12, (rank, err_out, err_grad)
+
+
+def test_head_slices_load_into_a_narrower_model():
+    """bench.py --scaling strong builds each rank's model this way: every parameter of the
+    full model sliced along its head axis loads strictly into DenseGPA(heads = slice size)."""
+    from gpa_b200 import DenseGPA, GPAConfig
+    full = DenseGPA(GPAConfig(heads=8, key_dim=16, value_dim=16, slots=(8, 16), chunk_size=4))
+    sd = full.state_dict()
+    for r in range(4):
+        hs = head_slice(8, 4, r)
+        part = DenseGPA(GPAConfig(heads=hs.stop - hs.start, key_dim=16, value_dim=16,
+                                  slots=(8, 16), chunk_size=4))
+        part.load_state_dict(head_parallel_state_dict(sd, hs), strict=True)
+        assert torch.equal(part.edge_logits, full.edge_logits[:, hs])
+        assert torch.equal(part.center[1], full.center[1][hs])
