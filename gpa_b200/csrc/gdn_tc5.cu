@@ -302,14 +302,9 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
       tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half), acc2[0]);
       tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half + 16), acc2[1]);
       tc5::tmem_wait_ld();
-      // W goes out as bf16 pairs: lanes 2i and 2i+1 swap halves of each 16-token chunk, so
-      // lane 2i stores columns (v, v+1) of tokens 0-7 and lane 2i+1 those of tokens 8-15
-      const bool odd = lane & 1;
-      bf16* wbase = Wout + row(u, T, t0 + 32 * half) * V + (v & ~1);
 #pragma unroll
       for (int c16 = 0; c16 < 2; ++c16) {
         const float(&acc)[16] = acc2[c16];
-        float w16[16];
 #pragma unroll
         for (int j8 = 0; j8 < 2; ++j8) {
           float x[8];
@@ -317,7 +312,7 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
           for (int j = 0; j < 8; ++j) {
             const int jj = 16 * c16 + 8 * j8 + j, t = 32 * half + jj;
             const float w = (vok && t < c) ? ub[jj] - acc[8 * j8 + j] : 0.f;
-            w16[8 * j8 + j] = w;
+            if (vok && t < c) Wout[row(u, T, t0 + t) * V + v] = __float2bfloat16(w);
             x[j] = w * lam[t];
           }
           uint4 h, l;
@@ -325,15 +320,6 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
           const uint32_t o = tc5::kmajor_off(v, 32 * half + 16 * c16 + 8 * j8, C);
           *reinterpret_cast<uint4*>(WtH + o) = h;
           *reinterpret_cast<uint4*>(WtL + o) = l;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? w16[j] : w16[j + 8], 1);
-          const int jj = 16 * c16 + j + (odd ? 8 : 0);
-          const __nv_bfloat162 pr = odd ? __floats2bfloat162_rn(other, w16[j + 8])
-                                        : __floats2bfloat162_rn(w16[j], other);
-          if (vok && 32 * half + jj < c)
-            *reinterpret_cast<__nv_bfloat162*>(wbase + (int64_t)jj * V) = pr;
         }
       }
     }
@@ -382,26 +368,10 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
                 const float sv = gc * s[i + h8 + j] + acc[h8 + j];
                 s[i + h8 + j] = sv;
                 x[j] = sv;
+                if (vok) sbn[(int64_t)(k0 + i + h8 + j) * V + v] = sv;
               }
               *reinterpret_cast<uint4*>(St + tc5::kmajor_off(v, k0 + i + h8, K)) = pack8(x);
             }
-          }
-          // boundary state as float2 pairs: lane 2i stores columns (v, v+1) of rows i .. i+7,
-          // lane 2i+1 those of rows i+8 .. i+15; a last chunk of 8 rows (KH is a multiple of
-          // 8) goes out as single values
-          if (i + 16 <= KH) {
-            const bool odd = lane & 1;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float other = __shfl_xor_sync(0xffffffffu, odd ? s[i + j] : s[i + j + 8], 1);
-              const int kk = k0 + i + j + (odd ? 8 : 0);
-              const float2 pr = odd ? make_float2(other, s[i + j + 8]) : make_float2(s[i + j], other);
-              if (vok) *reinterpret_cast<float2*>(sbn + (int64_t)kk * V + (v & ~1)) = pr;
-            }
-          } else if (i + 8 <= KH) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              if (vok) sbn[(int64_t)(k0 + i + j) * V + v] = s[i + j];
           }
         }
       }
