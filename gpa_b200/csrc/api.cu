@@ -971,17 +971,18 @@ size_t gpa_b200_noalloc_capacity(void) { return kNoAllocBytes; }
 
 int gpa_b200_device_status(int clear) { return gpa::tc5_device_status(clear != 0); }
 
-int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int a_bulk,
+int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int flags,
                            const void* A, const void* B, const void* A_tiled, float* D,
                            int* status, void* stream) {
   g_last_error.clear();
-  if (!gpa::umma_probe_shape_ok(M, mma_m, N, Kd))
-    return fail(GPA_B200_UNSUPPORTED, "umma self-test: unsupported shape");
+  if (!gpa::umma_probe_shape_ok(M, mma_m, N, Kd, flags))
+    return fail(GPA_B200_UNSUPPORTED, "umma self-test: unsupported shape or flags");
+  const bool a_bulk = flags & GPA_B200_UMMA_BULK_A;
   if (!B || !D || !status || (a_bulk ? !A_tiled : !A))
     return fail(GPA_B200_BAD_ARGUMENT, "umma self-test: NULL operand");
   if (a_bulk && (reinterpret_cast<uintptr_t>(A_tiled) & 15))
     return fail(GPA_B200_BAD_ARGUMENT, "umma self-test: A_tiled must be 16-byte aligned");
-  const int rc = gpa::umma_probe(M, mma_m, N, Kd, a_mn, b_mn, a_bulk, A, B, A_tiled, D, status,
+  const int rc = gpa::umma_probe(M, mma_m, N, Kd, a_mn, b_mn, flags, A, B, A_tiled, D, status,
                                  static_cast<cudaStream_t>(stream));
   return rc ? fail(rc, "umma self-test: launch failed") : GPA_B200_OK;
 }

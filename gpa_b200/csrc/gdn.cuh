@@ -98,13 +98,17 @@ cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaSt
 // mma.sync sweeps instead (kept for comparison)
 bool tc5_sweeps_enabled();
 cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+// tcgen05 WY / UT transform of every block (gdn_tc5.cu): A, T (kept), U, Wk;
+// GPA_B200_WY=mma selects the mma.sync kernel instead
+bool tc5_wy_enabled();
+cudaError_t tc5_fwd_chunk_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 // device status word of the tcgen05 kernels (GPA_B200_DEVICE_TIMEOUT after a wait gave up);
 // synchronous read, optionally clearing it; -1 if the read failed
 int tc5_device_status(bool clear);
 
 // tcgen05 self-test (tc5_probe.cu): D = A B on one CTA; returns a GPA_B200_* status
-int umma_probe(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int a_bulk, const void* A,
+int umma_probe(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int flags, const void* A,
                const void* B, const void* A_tiled, float* D, int* status, cudaStream_t st);
-bool umma_probe_shape_ok(int M, int mma_m, int N, int Kd);
+bool umma_probe_shape_ok(int M, int mma_m, int N, int Kd, int flags);
 
 }  // namespace gpa

@@ -80,5 +80,78 @@ GPA_DEV void backward_subst(const float* A, float* Y, int c, int ncol, int ld) {
   }
 }
 
+// T = (I + A)^-1 for a strictly lower 64x64 A (row stride kAStride), into Tm (same stride).
+GPA_DEV void invert_unit_lower(const float* A, float* Tm) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kMaxChunk * kAStride; i += blockDim.x) Tm[i] = 0.f;
+  __syncthreads();
+  if (w < 4 && lane < 16) {
+    const int b0 = 16 * w, j = lane;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float s = (r == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int q = 0; q < r; ++q) s -= A[(b0 + r) * kAStride + b0 + q] * x[q];
+      x[r] = s;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Tm[(b0 + r) * kAStride + b0 + j] = x[r];
+  }
+  __syncthreads();
+  // Off-diagonal 16 x 16 blocks by distance dd = ib - jb: X = sum_{jb <= kb < ib}
+  // A[ib][kb] T[kb][jb], then T[ib][jb] = -T[ib][ib] X.  One warp owns block (ib, jb) for both
+  // products, so X is parked in that block of Tm (which nothing else reads during step dd)
+  // between two warp barriers.  A lane computes rows r and r + 8, columns c .. c + 3 of a
+  // block: 6 shared loads per 8 FMAs.
+  for (int dd = 1; dd < 4; ++dd) {
+    const int nblk = 4 - dd;
+    if (w < nblk) {
+      const int jb = w, ib = jb + dd, r = lane >> 2, c = (lane & 3) << 2;
+      float* blk = Tm + (16 * ib) * kAStride + 16 * jb;  // block (ib, jb)
+      float x[2][4] = {};
+      for (int kb = jb; kb < ib; ++kb) {
+        const float* a0 = A + (16 * ib + r) * kAStride + 16 * kb;
+        const float* t = Tm + (16 * kb) * kAStride + 16 * jb + c;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float u0 = a0[q], u1 = a0[8 * kAStride + q];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float tv = t[q * kAStride + k];
+            x[0][k] = fmaf(u0, tv, x[0][k]);
+            x[1][k] = fmaf(u1, tv, x[1][k]);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        blk[r * kAStride + c + k] = x[0][k];
+        blk[(r + 8) * kAStride + c + k] = x[1][k];
+      }
+      __syncwarp();
+      const float* d0 = Tm + (16 * ib + r) * kAStride + 16 * ib;
+      float y[2][4] = {};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const float u0 = d0[q], u1 = d0[8 * kAStride + q];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float xv = blk[q * kAStride + c + k];
+          y[0][k] = fmaf(u0, xv, y[0][k]);
+          y[1][k] = fmaf(u1, xv, y[1][k]);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        blk[r * kAStride + c + k] = -y[0][k];
+        blk[(r + 8) * kAStride + c + k] = -y[1][k];
+      }
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 }  // namespace gpa

@@ -87,79 +87,6 @@ GPA_DEV void gate_finish(const GateRegs& r, int c, float* G, float* bt) {
   __syncthreads();
 }
 
-// T = (I + A)^-1 for a strictly lower 64x64 A (row stride kAStride).  Xs: 768 floats.
-GPA_DEV void invert_unit_lower(const float* A, float* Tm, float* Xs) {
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < C * kAStride; i += blockDim.x) Tm[i] = 0.f;
-  __syncthreads();
-  if (w < 4 && lane < 16) {
-    const int b0 = 16 * w, j = lane;
-    float x[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float s = (r == j) ? 1.f : 0.f;
-#pragma unroll
-      for (int q = 0; q < r; ++q) s -= A[(b0 + r) * kAStride + b0 + q] * x[q];
-      x[r] = s;
-    }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) Tm[(b0 + r) * kAStride + b0 + j] = x[r];
-  }
-  __syncthreads();
-  // Off-diagonal 16 x 16 blocks by distance dd = ib - jb: Xs_jb = sum_{jb <= kb < ib}
-  // A[ib][kb] T[kb][jb], then T[ib][jb] = -T[ib][ib] Xs_jb.  A lane computes rows r and r + 8,
-  // columns c .. c + 3 of a block: 6 shared loads per 8 FMAs (one warp per block).
-  for (int dd = 1; dd < 4; ++dd) {
-    const int nblk = 4 - dd;
-    if (w < nblk) {
-      const int jb = w, ib = jb + dd, r = lane >> 2, c = (lane & 3) << 2;
-      float x[2][4] = {};
-      for (int kb = jb; kb < ib; ++kb) {
-        const float* a0 = A + (16 * ib + r) * kAStride + 16 * kb;
-        const float* t = Tm + (16 * kb) * kAStride + 16 * jb + c;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const float u0 = a0[q], u1 = a0[8 * kAStride + q];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float tv = t[q * kAStride + k];
-            x[0][k] = fmaf(u0, tv, x[0][k]);
-            x[1][k] = fmaf(u1, tv, x[1][k]);
-          }
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        Xs[(jb << 8) + (r << 4) + c + k] = x[0][k];
-        Xs[(jb << 8) + ((r + 8) << 4) + c + k] = x[1][k];
-      }
-    }
-    __syncthreads();
-    if (w < nblk) {
-      const int jb = w, ib = jb + dd, r = lane >> 2, c = (lane & 3) << 2;
-      const float* d0 = Tm + (16 * ib + r) * kAStride + 16 * ib;
-      const float* xs = Xs + (jb << 8) + c;
-      float y[2][4] = {};
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float u0 = d0[q], u1 = d0[8 * kAStride + q];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float xv = xs[(q << 4) + k];
-          y[0][k] = fmaf(u0, xv, y[0][k]);
-          y[1][k] = fmaf(u1, xv, y[1][k]);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        Tm[(16 * ib + r) * kAStride + 16 * jb + c + k] = -y[0][k];
-        Tm[(16 * ib + r + 8) * kAStride + 16 * jb + c + k] = -y[1][k];
-      }
-    }
-    __syncthreads();
-  }
-}
-
 // The 10 of the 4 x 4 tiles (16 x 16) of a 64 x 64 block on or below the diagonal, round-robin
 // over the warps: body(m0, n0).  A product with a lower-triangular block operand reads no other.
 template <class Body>
@@ -188,15 +115,15 @@ GPA_DEV void tc_build_a(const bf16* Ks, const bf16* Kl, int ldk, int K, const fl
 // ------------------------------------------------------------------ forward
 
 struct LFwdChunk {
-  // after the inversion, the A + Xs region holds the hi/lo factor of one product at a time
-  size_t Ks, Kl, Vs, A, Xs, Tm, Fh, Fl, G, bt, total;
+  // after the inversion, the A + Fpad region holds the hi/lo factor of one product at a time
+  size_t Ks, Kl, Vs, A, Fpad, Tm, Fh, Fl, G, bt, total;
   __host__ __device__ LFwdChunk(int K, int V) {
     Carve c;
     Ks = c.take(2 * C * ld16(K));
     Kl = c.take(2 * C * ld16(K));
     Vs = c.take(2 * C * ld16(V));
     A = c.take(4 * C * kAStride);
-    Xs = c.take(4 * 768);
+    Fpad = c.take(4 * 768);
     Tm = c.take(4 * C * kAStride);
     G = c.take(4 * C);
     bt = c.take(4 * C);
@@ -219,7 +146,6 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   bf16* Vs = (bf16*)(smem + L.Vs);
   float* A = (float*)(smem + L.A);
   float* Tm = (float*)(smem + L.Tm);
-  float* Xs = (float*)(smem + L.Xs);
   bf16* Fh = (bf16*)(smem + L.Fh);
   bf16* Fl = (bf16*)(smem + L.Fl);
   float* G = (float*)(smem + L.G);
@@ -233,7 +159,7 @@ __global__ void __launch_bounds__(kThreads) tc_fwd_chunk(ScanBatch b, int U, Blo
   }
   tc_build_a(Ks, Kl, ldk, K, G, bt, A);
   __syncthreads();
-  invert_unit_lower(A, Tm, Xs);  // ends with __syncthreads: A is free below
+  invert_unit_lower(A, Tm);  // ends with __syncthreads: A is free below
   float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
   for (int i = threadIdx.x; i < C * C; i += blockDim.x) Ts[i] = Tm[(i / C) * kAStride + (i % C)];
   for (int i = threadIdx.x; i < C * C / 2; i += blockDim.x) {
@@ -1201,8 +1127,9 @@ bool tc_supported(int K, int V) {
 
 cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_output,
                        cudaStream_t st) {
-  cudaError_t e = tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk, U * bl.nb, b, U, bl, st,
-                                              false, 74);
+  cudaError_t e = tc5_wy_enabled() ? tc5_fwd_chunk_launch(b, U, bl, st)
+                                   : tc_launch_groups<LFwdChunk>("tc_fwd_chunk", tc_fwd_chunk,
+                                                                 U * bl.nb, b, U, bl, st, false, 74);
   if (e != cudaSuccess) return e;
   e = tc5_sweeps_enabled() ? tc5_fwd_state_launch(b, U, bl, st)
                            : tc_launch_groups<LFwdState>("tc_fwd_state", tc_fwd_state, U, b, U,

@@ -39,6 +39,7 @@ using bf16 = __nv_bfloat16;
 constexpr int C = kMaxChunk;       // 64 tokens per block tile
 constexpr int kSweepThreads = 256;  // 8 warps: two per TMEM lane quarter
 constexpr int kSweepCols = 256;     // TMEM columns: W^T at 0 (64), S^T at 64 (<= 128)
+constexpr int kMaxScanWidth = 128;  // K, V <= 128 (checked by the API)
 
 struct SweepGates {
   float g0, g1;
@@ -297,7 +298,6 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
     mph ^= 1;
     tc5::fence_after_sync();
     if (active) {  // epilogue 1: W = U - acc; W out (bf16); lambda W hi / lo -> (lambda W)^T
-#pragma unroll
       float acc2[2][16];
       tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half), acc2[0]);
       tc5::tmem_ld16(tc5::tmem_at(tbase, 32 * half + 16), acc2[1]);
@@ -402,6 +402,334 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
   if (warp == 0) tc5::tmem_free(tbase, kSweepCols);
 }
 
+// ------------------------------------------------------------------ WY / UT transform
+
+// Per block of c <= 64 tokens of a (K, V) scan (gdn.cuh):
+//   A = strict_lower(b_t e^{G_t - G_s} k_t . k_s),   T = (I + A)^-1,
+//   U = T diag(b) V,   Wk = T diag(b e^G) K.
+// The three products run on tcgen05 with M = 64 (rows t; TMEM lanes 0-15 of each quarter):
+//   A  = K K^T   (A and B the same K-major K tile, hi / lo: hi hi + hi lo + lo hi)
+//   U  = F V     (F = T diag(b), hi / lo, K-major; V hi, MN-major)
+//   Wk = F' K    (F' = T diag(b e^G), hi / lo; K read through the MN-major view of its tile)
+// T comes from the same SIMT unit-lower inversion as the mma.sync kernel.  Each CTA is one
+// dependent chain (loads, MMA, epilogue, inversion, MMA, stores), so throughput comes from
+// chains overlapping: three CTAs per SM (at most 80 registers; 73 KB of shared memory for
+// K = 128, V = 64).
+struct LFwdChunk5 {
+  uint32_t Kh, Kl, Vh, A, Tm, G, bt, bar, slot, total, Fh, Fl, F2h, F2l;
+  __host__ __device__ LFwdChunk5(int K, int V) {
+    uint32_t o = 0;
+    auto take = [&](uint32_t b) {
+      o = (o + 127u) & ~127u;
+      const uint32_t r = o;
+      o += b;
+      return r;
+    };
+    Kh = take(C * K * 2);  // K tile, K-major: rows t, reduction k
+    Kl = take(C * K * 2);
+    Vh = take(V * C * 2);  // V tile, MN-major: rows v, reduction t
+    A = take(4 * C * kAStride);
+    Tm = take(4 * C * kAStride);
+    G = take(4 * C);
+    bt = take(4 * C);
+    bar = take(8);
+    slot = take(16);
+    total = o;
+    Fh = A;  // F = T diag(b), K-major (rows t, reduction s), over A once T is formed
+    Fl = A + C * C * 2;
+    F2h = Tm;  // F' = T diag(b e^G) over T once every thread holds its T values in registers
+    F2l = Tm + C * C * 2;
+  }
+};
+
+// One operand tile built from rows [t0, t0 + c) of a [T, W] fp32 array (src at row t0): 64
+// rows t (rows >= c zero), K-major (rows t, reduction over w) or MN-major (rows w, reduction
+// over t); bf16 hi (+ lo when lo is set).
+struct RowTile {
+  const float* src;
+  int W;
+  bool kmajor;
+  unsigned char* hi;
+  unsigned char* lo;
+};
+
+// Items of 8 consecutive w of one row a thread takes per tile: C * W / 8 / threads, W <= 128.
+constexpr int kRowItems = C * kMaxScanWidth / 8 / kSweepThreads;
+static_assert(kRowItems * kSweepThreads * 8 == C * kMaxScanWidth, "row items cover the tile");
+using RowRegs = float4[kRowItems][2];
+
+// Item i of a tile: row t and column group w8 (8 columns).  The 8 lanes of a shared-memory
+// phase take 8 rows at 8 different column groups (conflict-free 16-byte stores).
+GPA_DEV void row_item(int i, int w8n, int& t, int& w8) {
+  const int j = i & 7, g = i >> 3, tq = g / w8n;
+  t = 8 * tq + j;
+  w8 = (g - tq * w8n + j) % w8n;
+}
+
+// Issue every global load of this thread's items of tile J (all in flight at once).
+GPA_DEV void tile_fetch(const RowTile& J, int c, RowRegs& v) {
+  const int w8n = J.W >> 3, n = C * w8n;
+#pragma unroll
+  for (int q = 0; q < kRowItems; ++q) {
+    const int i = threadIdx.x + q * kSweepThreads;
+    int t, w8;
+    row_item(i, w8n, t, w8);
+    if (i < n && t < c) {
+      const float* p = J.src + (int64_t)t * J.W + 8 * w8;
+      v[q][0] = *reinterpret_cast<const float4*>(p);
+      v[q][1] = *reinterpret_cast<const float4*>(p + 4);
+    } else {
+      v[q][0] = v[q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+// Convert the fetched items into the bf16 operand tile(s) of J.
+GPA_DEV void tile_store(const RowTile& J, const RowRegs& v) {
+  const int w8n = J.W >> 3, n = C * w8n;
+#pragma unroll
+  for (int q = 0; q < kRowItems; ++q) {
+    const int i = threadIdx.x + q * kSweepThreads;
+    if (i >= n) continue;
+    int t, w8;
+    row_item(i, w8n, t, w8);
+    const float4 a = v[q][0], b = v[q][1];
+    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const uint32_t o = J.kmajor ? tc5::kmajor_off(t, 8 * w8, J.W) : tc5::mnmajor_off(8 * w8, t, C);
+    if (J.lo) {
+      uint4 h, l;
+      split8(x, h, l);
+      *reinterpret_cast<uint4*>(J.hi + o) = h;
+      *reinterpret_cast<uint4*>(J.lo + o) = l;
+    } else {
+      *reinterpret_cast<uint4*>(J.hi + o) = pack8(x);
+    }
+  }
+}
+
+// Warp 0: G = inclusive cumsum of g over the block (rows >= c hold G[c-1]) and bt = beta
+// (0 for rows >= c).  The caller synchronizes.
+GPA_DEV void chunk_gates(const ScanDesc& d, int u, int t0, int c, float* G, float* bt) {
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    float x0 = t < c ? gate_at(d.g, d, u, t0 + t) : 0.f;
+    float x1 = t + 32 < c ? gate_at(d.g, d, u, t0 + t + 32) : 0.f;
+    const float b0 = t < c ? gate_at(d.beta, d, u, t0 + t) : 0.f;
+    const float b1 = t + 32 < c ? gate_at(d.beta, d, u, t0 + t + 32) : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (t >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    const float last = __shfl_sync(0xffffffffu, c - 1 < 32 ? x0 : x1, (c - 1) & 31);
+    G[t] = t < c ? x0 : last;
+    G[t + 32] = t + 32 < c ? x1 : last;
+    bt[t] = b0;
+    bt[t + 32] = b1;
+  }
+}
+
+// F / F' items a thread builds: C rows x C / 8 column groups over the threads
+constexpr int kFItems = C * (C / 8) / kSweepThreads;
+static_assert(kFItems * kSweepThreads == C * (C / 8), "F items cover the tile");
+
+// grid (U * NB, nscan), 256 threads.  Epilogues: TMEM lanes 0-15 of quarter q hold rows
+// t = 16 q + lane; the two warps of a quarter take alternate 16-column chunks.
+__global__ void __launch_bounds__(kSweepThreads, 3) tc5_fwd_chunk(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const LFwdChunk5 L(K, V);
+  unsigned char* Kh = sm + L.Kh;
+  unsigned char* Kl = sm + L.Kl;
+  unsigned char* Vh = sm + L.Vh;
+  unsigned char* Fh = sm + L.Fh;
+  unsigned char* Fl = sm + L.Fl;
+  unsigned char* F2h = sm + L.F2h;
+  unsigned char* F2l = sm + L.F2l;
+  float* A = reinterpret_cast<float*>(sm + L.A);
+  float* Tm = reinterpret_cast<float*>(sm + L.Tm);
+  float* G = reinterpret_cast<float*>(sm + L.G);
+  float* bt = reinterpret_cast<float*>(sm + L.bt);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L.bar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = warp >> 2, trow = 16 * (warp & 3) + (lane & 15);
+  const bool rowlane = lane < 16;
+  // 128 TMEM columns (three CTAs per SM fit the 512): U at [0, V) and Wk at [V, V + K) when
+  // both fit, else U and then Wk at [0, ...) in two rounds
+  const bool split = V + K > 128;
+  const int wc = split ? 0 : V;
+  constexpr uint32_t ncols = 128;
+  const int64_t r0 = row(u, T, t0);
+  const RowTile kt{d.k + r0 * K, K, true, Kh, Kl}, vt{d.v + r0 * V, V, false, Vh, nullptr};
+
+  if (warp == 0) tc5::tmem_alloc(slot, ncols);
+  if (tid == 0) {
+    tc5::mbar_init(bar, 1);
+    tc5::mbar_fence_init();
+  }
+  {
+    RowRegs kv;
+    tile_fetch(kt, c, kv);  // K loads in flight while warp 0 fetches and scans the gates
+    chunk_gates(d, u, t0, c, G, bt);
+    tile_store(kt, kv);
+  }
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tb = *slot;
+  uint32_t ph = 0;
+  bool ok = true;
+  if (tid == 0) {  // A = K K^T (hi hi + hi lo + lo hi)
+    const uint32_t id = tc5::idesc_bf16(C, C, false, false);
+    const uint32_t h = tc5::saddr(Kh), l = tc5::saddr(Kl);
+    for (int ks = 0; ks < K / 16; ++ks) {
+      tc5::mma(tb, tc5::sdesc(h, K, ks), tc5::sdesc(h, K, ks), id, ks > 0);
+      tc5::mma(tb, tc5::sdesc(h, K, ks), tc5::sdesc(l, K, ks), id, true);
+      tc5::mma(tb, tc5::sdesc(l, K, ks), tc5::sdesc(h, K, ks), id, true);
+    }
+    tc5::commit(bar);
+  }
+  RowRegs vv;
+  tile_fetch(vt, c, vv);  // V loads in flight during MMA 1 and its epilogue
+  ok = tc5::mbar_wait(bar, ph);
+  ph ^= 1;
+  tc5::fence_after_sync();
+  for (int ci = half; ci < C / 16; ci += 2) {  // A[t][s] = b_t e^{G_t - G_s} (k_t . k_s), s < t
+    float acc[16];
+    tc5::tmem_ld16(tc5::tmem_at(tb, 16 * ci), acc);
+    tc5::tmem_wait_ld();
+    if (rowlane) {
+      const float gt = G[trow], bb = bt[trow];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int s = 16 * ci + j;
+        A[trow * kAStride + s] = s < trow ? bb * __expf(gt - G[s]) * acc[j] : 0.f;
+      }
+    }
+  }
+  tile_store(vt, vv);  // read by MMA 2 after the proxy fence below
+  __syncthreads();
+  invert_unit_lower(A, Tm);  // ends with __syncthreads: A is free below
+  {
+    // T out, then every thread's T values (F / F' items) into registers before F' overwrites T
+    float* Ts = d.Tsv + ((int64_t)u * bl.nb + n) * C * C;
+    for (int i = tid; i < C * C; i += blockDim.x) Ts[i] = Tm[(i / C) * kAStride + (i % C)];
+    float x[kFItems][8];
+#pragma unroll
+    for (int q = 0; q < kFItems; ++q) {
+      const int i = tid + q * kSweepThreads, j = i & 7, g = i >> 3, tq = g >> 3;
+      const int t = 8 * tq + j, s8 = ((g & 7) + j) & 7;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[q][e] = Tm[t * kAStride + 8 * s8 + e] * bt[8 * s8 + e];
+    }
+    __syncthreads();
+    // F = T diag(b) and F' = T diag(b e^G), hi / lo, K-major (rows t, reduction s)
+#pragma unroll
+    for (int q = 0; q < kFItems; ++q) {
+      const int i = tid + q * kSweepThreads, j = i & 7, g = i >> 3, tq = g >> 3;
+      const int t = 8 * tq + j, s8 = ((g & 7) + j) & 7;
+      const uint32_t o = tc5::kmajor_off(t, 8 * s8, C);
+      uint4 h, l;
+      split8(x[q], h, l);
+      *reinterpret_cast<uint4*>(Fh + o) = h;
+      *reinterpret_cast<uint4*>(Fl + o) = l;
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = x[q][e] * __expf(G[8 * s8 + e]);
+      split8(y, h, l);
+      *reinterpret_cast<uint4*>(F2h + o) = h;
+      *reinterpret_cast<uint4*>(F2l + o) = l;
+    }
+  }
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t fh = tc5::saddr(Fh), fl = tc5::saddr(Fl), f2h = tc5::saddr(F2h),
+                 f2l = tc5::saddr(F2l), vh = tc5::saddr(Vh), kh = tc5::saddr(Kh), kl = tc5::saddr(Kl);
+  auto issue_u = [&] {  // U = F V -> columns [0, V)
+    const uint32_t idu = tc5::idesc_bf16(C, V, false, true);
+    for (int ks = 0; ks < C / 16; ++ks) {
+      tc5::mma(tb, tc5::sdesc(fh, C, ks), tc5::sdesc(vh, C, ks), idu, ks > 0);
+      tc5::mma(tb, tc5::sdesc(fl, C, ks), tc5::sdesc(vh, C, ks), idu, true);
+    }
+  };
+  auto issue_w = [&] {  // Wk = F' K -> columns [wc, wc + K)
+    const uint32_t idw = tc5::idesc_bf16(C, K, false, true);
+    for (int ks = 0; ks < C / 16; ++ks) {
+      tc5::mma(tb + wc, tc5::sdesc(f2h, C, ks), tc5::sdesc_mn_view(kh, K, ks), idw, ks > 0);
+      tc5::mma(tb + wc, tc5::sdesc(f2h, C, ks), tc5::sdesc_mn_view(kl, K, ks), idw, true);
+      tc5::mma(tb + wc, tc5::sdesc(f2l, C, ks), tc5::sdesc_mn_view(kh, K, ks), idw, true);
+    }
+  };
+  // rows of U and Wk out: 16-column chunks ci (U for ci < nu, then Wk), read through the
+  // 16-lane TMEM shape so that every lane holds data: lane l of quarter q has rows
+  // 16 q + l / 4 and + 8, columns 2 (l % 4) + {0, 1} and + 8 of the chunk, stored as float2
+  // (8 rows x 32 contiguous bytes per store instruction).  Two chunks per wait.
+  const int nu = V / 16, nch = nu + K / 16;
+  const int er = 16 * (warp & 3) + (lane >> 2), ec = 2 * (lane & 3);
+  auto chunk_col = [&](int ci) { return ci < nu ? 16 * ci : wc + 16 * (ci - nu); };
+  auto chunk_out = [&](int ci, const float (&v)[8]) {
+    if (!ok) return;
+    float* base = ci < nu ? d.Ub + r0 * V + 16 * ci + ec : d.Wk + r0 * K + 16 * (ci - nu) + ec;
+    const int ld = ci < nu ? V : K;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = er + 8 * h;
+      if (t < c) {
+        float* p = base + (int64_t)t * ld;
+        *reinterpret_cast<float2*>(p) = make_float2(v[2 * h], v[2 * h + 1]);
+        *reinterpret_cast<float2*>(p + 8) = make_float2(v[4 + 2 * h], v[5 + 2 * h]);
+      }
+    }
+  };
+  auto epilogue = [&](int lo, int hi) {  // chunks [lo, hi)
+    for (int ci = lo + half; ci < hi; ci += 4) {
+      const bool two = ci + 2 < hi;  // warp-uniform
+      float a0[8], a1[8];
+      tc5::tmem_ld16x16(tc5::tmem_at(tb, chunk_col(ci)), a0);
+      if (two) tc5::tmem_ld16x16(tc5::tmem_at(tb, chunk_col(ci + 2)), a1);
+      tc5::tmem_wait_ld();
+      chunk_out(ci, a0);
+      if (two) chunk_out(ci + 2, a1);
+    }
+  };
+  if (tid == 0 && ok) {
+    issue_u();
+    if (!split) issue_w();
+    tc5::commit(bar);
+  }
+  ok = ok && tc5::mbar_wait(bar, ph);
+  ph ^= 1;
+  tc5::fence_after_sync();
+  epilogue(0, split ? nu : nch);
+  if (split) {  // Wk reuses the columns once every warp has read U
+    tc5::fence_before_sync();
+    __syncthreads();
+    tc5::fence_after_sync();
+    if (tid == 0 && ok) {
+      issue_w();
+      tc5::commit(bar);
+    }
+    ok = ok && tc5::mbar_wait(bar, ph);
+    tc5::fence_after_sync();
+    epilogue(nu, nch);
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc5::tmem_free(tb, ncols);
+  if (!ok && tid == 0) fail_status();
+}
+
 }  // namespace
 
 size_t tc5_fwd_state_smem(int K, int V) { return LFwdSweep(K, V).total; }
@@ -443,6 +771,40 @@ cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cu
     if (e != cudaSuccess) return e;
     Launch scope("tc5_fwd_state", st);
     kern<<<dim3(U, sub.n), kSweepThreads, smem, st>>>(sub, U, bl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+bool tc5_wy_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GPA_B200_WY");
+    return !(e && std::strcmp(e, "mma") == 0);
+  }();
+  return on;
+}
+
+cudaError_t tc5_fwd_chunk_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  bool done[kMaxScans] = {};
+  for (int i = 0; i < b.n; ++i) {
+    if (done[i]) continue;
+    ScanBatch sub;
+    sub.tc = b.tc;
+    sub.n = 0;
+    for (int j = i; j < b.n; ++j)
+      if (!done[j] && b.s[j].K == b.s[i].K && b.s[j].V == b.s[i].V) {
+        sub.s[sub.n++] = b.s[j];
+        done[j] = true;
+      }
+    const size_t smem = LFwdChunk5(b.s[i].K, b.s[i].V).total;
+    if (smem > 227 * 1024 || b.s[i].K > kMaxScanWidth || b.s[i].V > kMaxScanWidth)
+      return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaFuncSetAttribute(tc5_fwd_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    Launch scope("tc5_fwd_chunk", st);
+    tc5_fwd_chunk<<<dim3(U * bl.nb, sub.n), kSweepThreads, smem, st>>>(sub, U, bl);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

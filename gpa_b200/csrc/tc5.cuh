@@ -48,6 +48,19 @@ GPA_DEV uint64_t sdesc(uint32_t a, int Kd, int ks) {
   return d;                                         // base offset 0, no swizzle
 }
 
+// Descriptor of a K-major tile X [rows r][cols c] (bytes kmajor_off(r, c, cols)) read as an
+// MN-major operand whose reduction index is r and whose M / N index is c: core matrices of 8 r
+// x 8 c, 128 bytes apart along c (stride byte offset) and 16 * cols bytes apart along r
+// (leading byte offset); the 16-wide reduction step `ks` starts 32 * cols bytes further.
+GPA_DEV uint64_t sdesc_mn_view(uint32_t a, int cols, int ks) {
+  const uint32_t start = a + (uint32_t)ks * 32u * (uint32_t)cols;
+  uint64_t d = (uint64_t)((start & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((16u * (uint32_t)cols) >> 4) << 16;  // leading byte offset (along r)
+  d |= (uint64_t)(128u >> 4) << 32;                    // stride byte offset (along c)
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
 // Instruction descriptor of kind::f16 with bf16 A and B, fp32 D; a_mn / b_mn select MN-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
@@ -145,6 +158,21 @@ GPA_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 16 lanes x 16 columns (16x256b shape, two repetitions along the columns), every thread of
+// the warp holding data: thread t gets lane t/4, columns 2 (t%4) + {0, 1} in v[0..1] and lane
+// 8 + t/4, the same columns, in v[2..3]; v[4..7] repeat that for columns 8 .. 15.  This is the
+// layout of an M = 64 accumulator's rows 16 q .. 16 q + 15 (lanes 32 q .. 32 q + 15).
+GPA_DEV void tmem_ld16x16(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 GPA_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // TMEM address of lane quarter (warp % 4), column `col`, from the allocation base.

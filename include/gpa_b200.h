@@ -175,12 +175,17 @@ int gpa_b200_device_status(int clear);
  * operands in shared memory, fp32 accumulator in tensor memory).  A [M x Kd] and
  * B [Kd x N] are row-major bf16 device arrays, D [M x N] fp32; mma_m (64 or 128)
  * is the instruction's M (rows >= M are zero); a_mn / b_mn select the MN-major
- * operand layouts; with a_bulk, A is read instead from A_tiled, its 128-row
- * K-major or MN-major shared-memory image, by one bulk (TMA) copy.  *status
+ * operand layouts (b_mn == 2: B stored as its own K-major tile, rows k, and
+ * read through an MN-major view of it).  flags: GPA_B200_UMMA_BULK_A reads A
+ * instead from A_tiled, its 128-row K-major or MN-major shared-memory image, by
+ * one bulk (TMA) copy; GPA_B200_UMMA_LD16 (mma_m 64, N a multiple of 16) reads D
+ * back through the 16-lane tcgen05.ld shape instead of the 32-lane one.  *status
  * (device int) is set to GPA_B200_DEVICE_TIMEOUT if a wait gave up.  Returns
  * GPA_B200_UNSUPPORTED for shapes outside M <= mma_m, 16 <= N <= 256,
- * 16 <= Kd <= 128 (multiples of 16). */
-int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int a_bulk,
+ * 16 <= Kd <= 128 (multiples of 16), or unknown flags. */
+#define GPA_B200_UMMA_BULK_A 1
+#define GPA_B200_UMMA_LD16 2
+int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int flags,
                            const void* A, const void* B, const void* A_tiled, float* D,
                            int* status, void* stream);
 

@@ -337,3 +337,20 @@ def test_backward_peak_memory_is_workspaces_plus_io():
     torch.cuda.synchronize()
     peak = torch.cuda.max_memory_allocated() - base
     assert peak <= work + io + (64 << 20), (peak, work, io)
+
+
+def test_mma_sync_fallback_kernels_match_in_a_child_process():
+    """The mma.sync WY transform and state sweep, kept behind GPA_B200_WY=mma and
+    GPA_B200_SWEEPS=mma (read once per process), pass the bf16 parity cases of the benched
+    widths in a child process."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, GPA_B200_WY="mma", GPA_B200_SWEEPS="mma")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.join(here, "test_gpu_parity.py"),
+                        "-x", "-q", "-p", "no:cacheprovider", "-k",
+                        "test_bf16_forward_backward and (c2head or odd_widths)"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout and "deselected" in r.stdout

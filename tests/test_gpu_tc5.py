@@ -32,19 +32,26 @@ def _tiled(A, Kd, mn):
     return img
 
 
-CASES = [  # (M, mma_m, N, Kd, a_mn, b_mn, a_bulk)
+BULK_A, LD16 = 1, 2  # GPA_B200_UMMA_BULK_A, GPA_B200_UMMA_LD16
+
+CASES = [  # (M, mma_m, N, Kd, a_mn, b_mn, flags)
     *[(128, 128, 128, 128, a, b, 0) for a in (0, 1) for b in (0, 1)],
     (128, 128, 64, 64, 0, 1, 0), (128, 128, 64, 64, 1, 0, 0),
     (64, 64, 64, 128, 0, 0, 0), (64, 64, 64, 128, 0, 1, 0), (64, 64, 128, 64, 1, 1, 0),
     (64, 128, 256, 64, 0, 1, 0), (48, 128, 16, 16, 1, 1, 0),
     (100, 128, 64, 128, 0, 1, 1), (128, 128, 128, 64, 1, 0, 1),
+    # B read through the MN-major view of its own K-major tile (the WY kernel's K tile)
+    (64, 64, 128, 64, 0, 2, 0), (64, 64, 64, 64, 0, 2, 0), (128, 128, 128, 64, 1, 2, 0),
+    # M = 64 accumulators read back through the 16-lane tcgen05.ld shape
+    (64, 64, 64, 128, 0, 0, LD16), (64, 64, 128, 64, 1, 1, LD16), (48, 64, 32, 64, 0, 2, LD16),
 ]
 
 
-@pytest.mark.parametrize("M,mma_m,N,Kd,a_mn,b_mn,a_bulk", CASES)
-def test_umma_matches_cpu_product(M, mma_m, N, Kd, a_mn, b_mn, a_bulk):
+@pytest.mark.parametrize("M,mma_m,N,Kd,a_mn,b_mn,flags", CASES)
+def test_umma_matches_cpu_product(M, mma_m, N, Kd, a_mn, b_mn, flags):
     lib = _lib.load()
-    g = torch.Generator().manual_seed(M * 7 + N * 3 + Kd + 11 * a_mn + 5 * b_mn + a_bulk)
+    a_bulk = flags & BULK_A
+    g = torch.Generator().manual_seed(M * 7 + N * 3 + Kd + 11 * a_mn + 5 * b_mn + flags)
     A = torch.randn(M, Kd, generator=g).bfloat16()
     B = torch.randn(Kd, N, generator=g).bfloat16()
     ref = A.double() @ B.double()
@@ -52,14 +59,20 @@ def test_umma_matches_cpu_product(M, mma_m, N, Kd, a_mn, b_mn, a_bulk):
     dT = _tiled(A, Kd, a_mn).cuda() if a_bulk else dA
     D = torch.full((M, N), float("nan"), device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = lib.gpa_b200_umma_selftest(M, mma_m, N, Kd, a_mn, b_mn, a_bulk, dA.data_ptr(),
+    rc = lib.gpa_b200_umma_selftest(M, mma_m, N, Kd, a_mn, b_mn, flags, dA.data_ptr(),
                                     dB.data_ptr(), dT.data_ptr(), D.data_ptr(),
                                     status.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _lib.check(rc, "gpa_b200_umma_selftest")
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    err = float((D.double().cpu() - ref).norm() / ref.norm())
-    assert err <= 1e-6, err
+    Dc = D.double().cpu()
+    err = float((Dc - ref).norm() / ref.norm())
+    # on a mismatch, name which product entry a few outputs hold (a read-layout error shows
+    # as a permutation)
+    where = [((r, c), divmod(int((ref - Dc[r, c]).abs().argmin()), N))
+             for r, c in ((0, 0), (0, 1), (0, 2), (1, 0), (4, 0), (8, 0), (0, 8))
+             if err > 1e-6 and r < M and c < N]
+    assert err <= 1e-6, (err, where)
 
 
 def test_no_tensor_core_kernel_timed_out():

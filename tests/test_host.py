@@ -145,3 +145,7 @@ def test_umma_selftest_rejects_unsupported_shapes_on_the_host():
                   (64, 128, 64, 256)):
         rc = lib.gpa_b200_umma_selftest(*shape, 0, 0, 0, 1, 1, 1, 1, 1, None)
         assert rc == 2, shape
+    # the 16-lane read is for M = 64 with N a multiple of 16; unknown flags are refused
+    for shape, flags in (((64, 128, 64, 64), 2), ((64, 64, 40, 64), 2), ((64, 64, 64, 64), 4)):
+        rc = lib.gpa_b200_umma_selftest(*shape, 0, 0, flags, 1, 1, 1, 1, 1, None)
+        assert rc == 2, (shape, flags)
