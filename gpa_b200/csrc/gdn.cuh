@@ -102,6 +102,10 @@ cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cu
 // GPA_B200_WY=mma selects the mma.sync kernel instead
 bool tc5_wy_enabled();
 cudaError_t tc5_fwd_chunk_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+// tcgen05 block outputs O = e^G Q S_n + P W (gdn_tc5.cu), selected by GPA_B200_OUT=tc5 (the
+// mma.sync kernel is the default)
+bool tc5_out_enabled();
+cudaError_t tc5_fwd_out_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 // device status word of the tcgen05 kernels (GPA_B200_DEVICE_TIMEOUT after a wait gave up);
 // synchronous read, optionally clearing it; -1 if the read failed
 int tc5_device_status(bool clear);

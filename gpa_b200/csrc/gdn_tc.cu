@@ -1139,6 +1139,7 @@ cudaError_t tc_forward(const ScanBatch& b, int U, const Blocks& bl, bool with_ou
 }
 
 cudaError_t tc_output(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  if (tc5_out_enabled()) return tc5_fwd_out_launch(b, U, bl, st);
   return tc_launch_groups<LFwdOut>("tc_fwd_out", tc_fwd_out, U * bl.nb, b, U, bl, st, false, 74);
 }
 

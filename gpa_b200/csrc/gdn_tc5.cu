@@ -442,18 +442,22 @@ struct LFwdChunk5 {
   }
 };
 
-// One operand tile built from rows [t0, t0 + c) of a [T, W] fp32 array (src at row t0): 64
-// rows t (rows >= c zero), K-major (rows t, reduction over w) or MN-major (rows w, reduction
-// over t); bf16 hi (+ lo when lo is set).
+// One operand tile built from `rows` (64 tokens, or K rows of a state) fp32 source rows of
+// width W (src at the tile's first row; rows >= the valid count zero): K-major (rows = the
+// source rows, reduction over w) or MN-major (rows w, reduction over the source rows); bf16 hi
+// (+ lo when lo is set); each source row t times e^{rowexp[t]} when rowexp is set.
 struct RowTile {
   const float* src;
   int W;
   bool kmajor;
   unsigned char* hi;
   unsigned char* lo;
+  int rows = C;
+  const float* rowexp = nullptr;
 };
 
-// Items of 8 consecutive w of one row a thread takes per tile: C * W / 8 / threads, W <= 128.
+// Items of 8 consecutive w of one row a thread takes per pass: C * W / 8 / threads for W <=
+// 128; a K x V state tile takes K / C passes.
 constexpr int kRowItems = C * kMaxScanWidth / 8 / kSweepThreads;
 static_assert(kRowItems * kSweepThreads * 8 == C * kMaxScanWidth, "row items cover the tile");
 using RowRegs = float4[kRowItems][2];
@@ -466,15 +470,16 @@ GPA_DEV void row_item(int i, int w8n, int& t, int& w8) {
   w8 = (g - tq * w8n + j) % w8n;
 }
 
-// Issue every global load of this thread's items of tile J (all in flight at once).
-GPA_DEV void tile_fetch(const RowTile& J, int c, RowRegs& v) {
-  const int w8n = J.W >> 3, n = C * w8n;
+// Issue every global load of this thread's items of pass `pass` of tile J (all in flight at
+// once); source rows >= `valid` read as zero.
+GPA_DEV void tile_fetch(const RowTile& J, int valid, RowRegs& v, int pass = 0) {
+  const int w8n = J.W >> 3, n = J.rows * w8n;
 #pragma unroll
   for (int q = 0; q < kRowItems; ++q) {
-    const int i = threadIdx.x + q * kSweepThreads;
+    const int i = threadIdx.x + (pass * kRowItems + q) * kSweepThreads;
     int t, w8;
     row_item(i, w8n, t, w8);
-    if (i < n && t < c) {
+    if (i < n && t < valid) {
       const float* p = J.src + (int64_t)t * J.W + 8 * w8;
       v[q][0] = *reinterpret_cast<const float4*>(p);
       v[q][1] = *reinterpret_cast<const float4*>(p + 4);
@@ -484,18 +489,24 @@ GPA_DEV void tile_fetch(const RowTile& J, int c, RowRegs& v) {
   }
 }
 
-// Convert the fetched items into the bf16 operand tile(s) of J.
-GPA_DEV void tile_store(const RowTile& J, const RowRegs& v) {
-  const int w8n = J.W >> 3, n = C * w8n;
+// Convert the fetched items of pass `pass` into the bf16 operand tile(s) of J.
+GPA_DEV void tile_store(const RowTile& J, const RowRegs& v, int pass = 0) {
+  const int w8n = J.W >> 3, n = J.rows * w8n;
 #pragma unroll
   for (int q = 0; q < kRowItems; ++q) {
-    const int i = threadIdx.x + q * kSweepThreads;
+    const int i = threadIdx.x + (pass * kRowItems + q) * kSweepThreads;
     if (i >= n) continue;
     int t, w8;
     row_item(i, w8n, t, w8);
     const float4 a = v[q][0], b = v[q][1];
     float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const uint32_t o = J.kmajor ? tc5::kmajor_off(t, 8 * w8, J.W) : tc5::mnmajor_off(8 * w8, t, C);
+    if (J.rowexp) {
+      const float f = __expf(J.rowexp[t]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] *= f;
+    }
+    const uint32_t o =
+        J.kmajor ? tc5::kmajor_off(t, 8 * w8, J.W) : tc5::mnmajor_off(8 * w8, t, J.rows);
     if (J.lo) {
       uint4 h, l;
       split8(x, h, l);
@@ -507,15 +518,39 @@ GPA_DEV void tile_store(const RowTile& J, const RowRegs& v) {
   }
 }
 
-// Warp 0: G = inclusive cumsum of g over the block (rows >= c hold G[c-1]) and bt = beta
-// (0 for rows >= c).  The caller synchronizes.
+// bf16 rows [C x W] (src at the tile's first row, row stride W; rows >= `valid` zero) -> the
+// MN-major bf16 tile with rows w and the reduction over the C rows: each item is one 16-byte
+// core-matrix row, loaded (all in flight) and stored as is.
+GPA_DEV void bf16_rows_to_mn(const bf16* src, int valid, int W, unsigned char* dst) {
+  const int w8n = W >> 3, n = C * w8n;
+  uint4 v[kRowItems];
+#pragma unroll
+  for (int q = 0; q < kRowItems; ++q) {
+    const int i = threadIdx.x + q * kSweepThreads;
+    int t, w8;
+    row_item(i, w8n, t, w8);
+    v[q] = i < n && t < valid ? *reinterpret_cast<const uint4*>(src + (int64_t)t * W + 8 * w8)
+                              : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int q = 0; q < kRowItems; ++q) {
+    const int i = threadIdx.x + q * kSweepThreads;
+    if (i >= n) continue;
+    int t, w8;
+    row_item(i, w8n, t, w8);
+    *reinterpret_cast<uint4*>(dst + tc5::mnmajor_off(8 * w8, t, C)) = v[q];
+  }
+}
+
+// Warp 0: G = inclusive cumsum of g over the block (rows >= c hold G[c-1]) and, when bt is
+// set, bt = beta (0 for rows >= c).  The caller synchronizes.
 GPA_DEV void chunk_gates(const ScanDesc& d, int u, int t0, int c, float* G, float* bt) {
   if (threadIdx.x < 32) {
     const int t = threadIdx.x;
     float x0 = t < c ? gate_at(d.g, d, u, t0 + t) : 0.f;
     float x1 = t + 32 < c ? gate_at(d.g, d, u, t0 + t + 32) : 0.f;
-    const float b0 = t < c ? gate_at(d.beta, d, u, t0 + t) : 0.f;
-    const float b1 = t + 32 < c ? gate_at(d.beta, d, u, t0 + t + 32) : 0.f;
+    const float b0 = bt && t < c ? gate_at(d.beta, d, u, t0 + t) : 0.f;
+    const float b1 = bt && t + 32 < c ? gate_at(d.beta, d, u, t0 + t + 32) : 0.f;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
@@ -529,8 +564,10 @@ GPA_DEV void chunk_gates(const ScanDesc& d, int u, int t0, int c, float* G, floa
     const float last = __shfl_sync(0xffffffffu, c - 1 < 32 ? x0 : x1, (c - 1) & 31);
     G[t] = t < c ? x0 : last;
     G[t + 32] = t + 32 < c ? x1 : last;
-    bt[t] = b0;
-    bt[t + 32] = b1;
+    if (bt) {
+      bt[t] = b0;
+      bt[t + 32] = b1;
+    }
   }
 }
 
@@ -574,6 +611,7 @@ __global__ void __launch_bounds__(kSweepThreads, 3) tc5_fwd_chunk(ScanBatch b, i
   if (tid == 0) {
     tc5::mbar_init(bar, 1);
     tc5::mbar_fence_init();
+    tc5::prefetch_l2(d.v + r0 * V, (uint32_t)(c * V * 4));  // fetched after the K tile
   }
   {
     RowRegs kv;
@@ -730,6 +768,187 @@ __global__ void __launch_bounds__(kSweepThreads, 3) tc5_fwd_chunk(ScanBatch b, i
   if (!ok && tid == 0) fail_status();
 }
 
+// Per block of c <= 64 tokens of a scan with output (gdn.cuh): O = e^G (Q S_n) + P W with
+// P = (Q K^T) o Gamma, Gamma_ts = e^{G_t - G_s} for s <= t (else 0).  Two tcgen05 rounds, M = 64
+// (rows t; TMEM lanes 0-15 of each quarter), 128 TMEM columns:
+//   P = Q K^T            Q, K hi, K-major                                  -> columns [0, 64)
+//   O = Qg S + P W       Qg = diag(e^G) Q hi, K-major; S hi, MN-major (rows v, reduction k);
+//                        P hi / lo, K-major; W hi (bf16 in memory), MN-major -> [0, V)
+// with the operand precision of the mma.sync kernel (Q, K, S, W single bf16; P split).  The
+// S and W tiles are built while the first round runs; Qg takes the K tile's place after it.
+struct LFwdOut5 {
+  uint32_t Qh, Kq, Sh, Wt, Ph, Pl, G, bar, slot, total;
+  __host__ __device__ LFwdOut5(int K, int V) {
+    uint32_t o = 0;
+    auto take = [&](uint32_t b) {
+      o = (o + 127u) & ~127u;
+      const uint32_t r = o;
+      o += b;
+      return r;
+    };
+    Qh = take(C * K * 2);
+    Kq = take(C * K * 2);  // K, then Qg
+    Sh = take(K * V * 2);
+    Wt = take(C * V * 2);
+    Ph = take(C * C * 2);
+    Pl = take(C * C * 2);
+    G = take(4 * C);
+    bar = take(8);
+    slot = take(16);
+    total = o;
+  }
+};
+
+// grid (U * NB, nscan), 256 threads; scans without output return at once.
+__global__ void __launch_bounds__(kSweepThreads, 3) tc5_fwd_out(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  if (!d.q || !d.O) return;
+  const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
+  const int t0 = bl.start(n), c = bl.end(n) - t0, K = d.K, V = d.V;
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const LFwdOut5 L(K, V);
+  unsigned char* Qh = sm + L.Qh;
+  unsigned char* Kq = sm + L.Kq;
+  unsigned char* Sh = sm + L.Sh;
+  unsigned char* Wt = sm + L.Wt;
+  unsigned char* Ph = sm + L.Ph;
+  unsigned char* Pl = sm + L.Pl;
+  float* G = reinterpret_cast<float*>(sm + L.G);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L.bar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = warp >> 2, trow = 16 * (warp & 3) + (lane & 15);
+  const bool rowlane = lane < 16;
+  constexpr uint32_t ncols = 128;
+  const int64_t r0 = row(u, T, t0), KV = (int64_t)K * V;
+  const RowTile qt{d.q + r0 * K, K, true, Qh, nullptr};
+  const RowTile kt{d.k + r0 * K, K, true, Kq, nullptr};
+  const float* sn = d.Sb + ((int64_t)u * (bl.nb + 1) + n) * KV;
+  const bf16* wn = reinterpret_cast<const bf16*>(d.W) + r0 * V;
+
+  if (warp == 0) tc5::tmem_alloc(slot, ncols);
+  if (tid == 0) {
+    tc5::mbar_init(bar, 1);
+    tc5::mbar_fence_init();
+    // every region this block reads is contiguous: start them all towards L2 at once, so
+    // that the tile loads below (one tile in registers at a time) wait on L2, not DRAM
+    tc5::prefetch_l2(d.q + r0 * K, (uint32_t)(c * K * 4));
+    tc5::prefetch_l2(sn, (uint32_t)(KV * 4));
+    tc5::prefetch_l2(wn, (uint32_t)(c * V * 2));
+  }
+  {
+    RowRegs r;
+    tile_fetch(kt, c, r);
+    chunk_gates(d, u, t0, c, G, nullptr);
+    tile_store(kt, r);
+    tile_fetch(qt, c, r);
+    tile_store(qt, r);
+  }
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tb = *slot;
+  uint32_t ph = 0;
+  bool ok = true;
+  if (tid == 0) {  // P = Q K^T
+    const uint32_t id = tc5::idesc_bf16(C, C, false, false);
+    const uint32_t qa = tc5::saddr(Qh), ka = tc5::saddr(Kq);
+    for (int ks = 0; ks < K / 16; ++ks)
+      tc5::mma(tb, tc5::sdesc(qa, K, ks), tc5::sdesc(ka, K, ks), id, ks > 0);
+    tc5::commit(bar);
+  }
+  {  // S_n (K x V fp32 -> MN-major, reduction over k) and W (bf16 -> MN-major) under MMA 1
+    const RowTile st{sn, V, false, Sh, nullptr, K};
+    constexpr int per_pass = kRowItems * kSweepThreads;
+    const int passes = (K * (V / 8) + per_pass - 1) / per_pass;
+    for (int pass = 0; pass < passes; ++pass) {
+      RowRegs r;
+      tile_fetch(st, K, r, pass);
+      tile_store(st, r, pass);
+    }
+    bf16_rows_to_mn(wn, c, V, Wt);
+  }
+  {
+    RowRegs qv;
+    tile_fetch(qt, c, qv);  // Q again (from L2) for Qg
+    ok = tc5::mbar_wait(bar, ph);
+    ph ^= 1;
+    tc5::fence_after_sync();
+    // MMA 1 has read K: Qg = diag(e^G) Q takes its tile
+    const RowTile gq{d.q + r0 * K, K, true, Kq, nullptr, C, G};
+    tile_store(gq, qv);
+  }
+  for (int ci = half; ci < C / 16; ci += 2) {  // P[t][s] = e^{G_t - G_s} (q_t . k_s), s <= t
+    float acc[16];
+    tc5::tmem_ld16(tc5::tmem_at(tb, 16 * ci), acc);
+    tc5::tmem_wait_ld();
+    if (rowlane) {
+      const float gt = G[trow];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int s = 16 * ci + 8 * h + e;
+          x[e] = s <= trow && trow < c ? __expf(gt - G[s]) * acc[8 * h + e] : 0.f;
+        }
+        uint4 hv, lv;
+        split8(x, hv, lv);
+        const uint32_t o = tc5::kmajor_off(trow, 16 * ci + 8 * h, C);
+        *reinterpret_cast<uint4*>(Ph + o) = hv;
+        *reinterpret_cast<uint4*>(Pl + o) = lv;
+      }
+    }
+  }
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  if (tid == 0 && ok) {  // O = Qg S + Ph W + Pl W
+    const uint32_t id = tc5::idesc_bf16(C, V, false, true);
+    const uint32_t qg = tc5::saddr(Kq), sa = tc5::saddr(Sh), wa = tc5::saddr(Wt),
+                   pha = tc5::saddr(Ph), pla = tc5::saddr(Pl);
+    for (int ks = 0; ks < K / 16; ++ks)
+      tc5::mma(tb, tc5::sdesc(qg, K, ks), tc5::sdesc(sa, K, ks), id, ks > 0);
+    for (int ks = 0; ks < C / 16; ++ks) {
+      tc5::mma(tb, tc5::sdesc(pha, C, ks), tc5::sdesc(wa, C, ks), id, true);
+      tc5::mma(tb, tc5::sdesc(pla, C, ks), tc5::sdesc(wa, C, ks), id, true);
+    }
+    tc5::commit(bar);
+  }
+  ok = ok && tc5::mbar_wait(bar, ph);
+  tc5::fence_after_sync();
+  // O rows out through the 16-lane TMEM shape: lane l of quarter q holds rows 16 q + l / 4 and
+  // + 8, columns 2 (l % 4) + {0, 1} and + 8 of a 16-column chunk; two chunks per wait
+  const int er = 16 * (warp & 3) + (lane >> 2), ec = 2 * (lane & 3), nv = V / 16;
+  auto chunk_out = [&](int ci, const float (&v)[8]) {
+    if (!ok) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = er + 8 * h;
+      if (t < c) {
+        float* p = d.O + (r0 + t) * V + 16 * ci + ec;
+        *reinterpret_cast<float2*>(p) = make_float2(v[2 * h], v[2 * h + 1]);
+        *reinterpret_cast<float2*>(p + 8) = make_float2(v[4 + 2 * h], v[5 + 2 * h]);
+      }
+    }
+  };
+  for (int ci = half; ci < nv; ci += 4) {
+    const bool two = ci + 2 < nv;  // warp-uniform
+    float a0[8], a1[8];
+    tc5::tmem_ld16x16(tc5::tmem_at(tb, 16 * ci), a0);
+    if (two) tc5::tmem_ld16x16(tc5::tmem_at(tb, 16 * (ci + 2)), a1);
+    tc5::tmem_wait_ld();
+    chunk_out(ci, a0);
+    if (two) chunk_out(ci + 2, a1);
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc5::tmem_free(tb, ncols);
+  if (!ok && tid == 0) fail_status();
+}
+
 }  // namespace
 
 size_t tc5_fwd_state_smem(int K, int V) { return LFwdSweep(K, V).total; }
@@ -783,6 +1002,43 @@ bool tc5_wy_enabled() {
     return !(e && std::strcmp(e, "mma") == 0);
   }();
   return on;
+}
+
+// Opt-in (GPA_B200_OUT=tc5): its per-block chain of tile loads (one tile in registers at a
+// time under the 80-register cap of three CTAs per SM, and the fp32 state snapshot converted
+// every block) measured slower than the 512-thread mma.sync kernel.
+bool tc5_out_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GPA_B200_OUT");
+    return e && std::strcmp(e, "tc5") == 0;
+  }();
+  return on;
+}
+
+cudaError_t tc5_fwd_out_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  bool done[kMaxScans] = {};
+  for (int i = 0; i < b.n; ++i) {
+    if (done[i]) continue;
+    ScanBatch sub;
+    sub.tc = b.tc;
+    sub.n = 0;
+    for (int j = i; j < b.n; ++j)
+      if (!done[j] && b.s[j].K == b.s[i].K && b.s[j].V == b.s[i].V) {
+        sub.s[sub.n++] = b.s[j];
+        done[j] = true;
+      }
+    const size_t smem = LFwdOut5(b.s[i].K, b.s[i].V).total;
+    if (smem > 227 * 1024 || b.s[i].K > kMaxScanWidth || b.s[i].V > kMaxScanWidth)
+      return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaFuncSetAttribute(tc5_fwd_out, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    Launch scope("tc5_fwd_out", st);
+    tc5_fwd_out<<<dim3(U * bl.nb, sub.n), kSweepThreads, smem, st>>>(sub, U, bl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t tc5_fwd_chunk_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {

@@ -130,6 +130,12 @@ GPA_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       : "memory");
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16, address 16-byte aligned) from global memory into
+// L2; nothing waits on it.
+GPA_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ------------------------------------------------------------------ TMEM
 // Allocate `ncols` (a power of two >= 32) columns; one whole warp executes it; the address is
 // written to shared memory at `slot`.
