@@ -19,8 +19,12 @@
 // read a second time): the step is HBM-bound on the cache, 2 x 4 x 155,968 bytes per unit at
 // the widths Dk = Dv = 128, slots (64, 64, 64, 128).
 #include "decode.cuh"
+#include "tc5.cuh"
 
 namespace gpa {
+
+__device__ int g_decode_status = 0;
+
 namespace {
 
 constexpr int kStepThreads = 256;
@@ -132,8 +136,35 @@ GPA_DEV void rowdot(const float* S, int R, int Cn, const float* x, float* y) {
   __syncthreads();
 }
 
-// shared <- global (n floats, multiple of 4, 16-byte aligned); optional copy to `also`
-GPA_DEV void load_mat(float* Ss, const float* g, int n, float* also) {
+// The mbarrier of the step's bulk state loads, its next phase parity, and whether every wait
+// on it completed.
+struct BulkLoad {
+  uint64_t* bar;
+  uint32_t parity;
+  bool ok;
+};
+
+// shared <- global (n floats, 16-byte aligned rows of float4); optional copy to `also`.  When
+// the matrix is 16-byte aligned and a whole number of 16-byte pieces it comes in as one bulk
+// (TMA) copy: one load latency and no registers held.  Otherwise float4 loads, four in flight
+// per thread.  A bulk wait that gives up (tc5::kWaitNs) clears bl.ok; the step then records
+// GPA_B200_DEVICE_TIMEOUT and its results are not to be used.
+GPA_DEV void load_mat(float* Ss, const float* g, int n, float* also, BulkLoad& bl) {
+  if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    tc5::fence_async_smem();  // every earlier access to Ss before the copy overwrites it
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      tc5::mbar_expect_tx(bl.bar, (uint32_t)n * 4u);
+      tc5::bulk_g2s(Ss, g, (uint32_t)n * 4u, bl.bar);
+    }
+    if (!tc5::mbar_wait(bl.bar, bl.parity)) bl.ok = false;
+    bl.parity ^= 1u;
+    if (also)
+      for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x)
+        *reinterpret_cast<float4*>(also + i) = *reinterpret_cast<const float4*>(Ss + i);
+    __syncthreads();
+    return;
+  }
   const int step = 4 * blockDim.x;
   for (int i0 = 4 * threadIdx.x; i0 < n; i0 += 4 * step) {  // four float4 in flight
     float4 x[4];
@@ -174,7 +205,7 @@ GPA_DEV void gdn_update(float* Ss, float* Sg, int K, int V, const float* kv, con
 
 struct StepSmem {
   size_t Ss, q, qn, key, kn, val, tmp, tmp2, pre, yb, part, red, slot, write, logits, valin, qo,
-      gates, total;
+      gates, bar, total;
   int msg_off[kMaxEdges];
   __host__ __device__ StepSmem(const StepArgs& a) {
     size_t off = 0;
@@ -216,6 +247,7 @@ struct StepSmem {
     qo = take(a.L * mx);
     gates = take(a.L * 4);
     for (int e = 0; e < a.E; ++e) msg_off[e] = (int)take(a.M[a.ed[e]]);
+    bar = take(4);  // the bulk loads' mbarrier (16-byte aligned)
     total = off * sizeof(float);
   }
 };
@@ -237,6 +269,11 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   float* tmp2 = sm + Lm.tmp2;
   float* part = sm + Lm.part;
   float* red = sm + Lm.red;
+  BulkLoad bl{reinterpret_cast<uint64_t*>(sm + Lm.bar), 0u, true};
+  if (threadIdx.x == 0) {
+    tc5::mbar_init(bl.bar, 1);
+    tc5::mbar_fence_init();
+  }
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     q[i] = load_in(a.q, (int64_t)u * D + i, a.dt);
     key[i] = load_in(a.k, (int64_t)u * D + i, a.dt);
@@ -288,13 +325,13 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     float* Bg = a.s.outer[j] + u * szB;
     float* rk = tmp;  // [D]
     if (o != 0) {     // write and rk from the frozen inner snapshot
-      load_mat(Ss, a.s.frozen_inner[j] + u * szA, (int)szA, nullptr);
+      load_mat(Ss, a.s.frozen_inner[j] + u * szA, (int)szA, nullptr, bl);
       colsum(Ss, D, M, kn, write, part);
       softmax_vec(write, write, M, red);
       rowdot(Ss, D, M, write, rk);
     }
     // inner GDN step; the pre-update A is the frozen snapshot when the token opens a block
-    load_mat(Ss, Ag, (int)szA, o == 0 ? a.s.frozen_inner[j] + u * szA : nullptr);
+    load_mat(Ss, Ag, (int)szA, o == 0 ? a.s.frozen_inner[j] + u * szA : nullptr, bl);
     float* pre = sm + Lm.pre;  // u(k)^T A_old [M]
     colsum(Ss, D, M, kn, pre, part);
     if (o == 0) {
@@ -314,7 +351,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     // rv = write^T B_f
     float* rv = tmp2;
     load_mat(Ss, o == 0 ? Bg : a.s.frozen_outer[j] + u * szB, (int)szB,
-             o == 0 ? a.s.frozen_outer[j] + u * szB : nullptr);
+             o == 0 ? a.s.frozen_outer[j] + u * szB : nullptr, bl);
     colsum(Ss, M, Dv, write, rv, part);
     float* vin = sm + Lm.valin + j * Dv;
     const float ek = 1.f + .25f * tanhf(a.p.residual_raw[(j * a.H + h) * 2 + 0]);
@@ -337,7 +374,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     unit_vec(lq, lq, Mi, red);
     const int64_t sz = (int64_t)Mi * Mj;
     float* Rg = a.s.relation[e] + u * sz;
-    load_mat(Ss, Rg, (int)sz, nullptr);
+    load_mat(Ss, Rg, (int)sz, nullptr, bl);
     float* prebuf = sm + Lm.pre;
     colsum(Ss, Mi, Mj, kv, prebuf, part);
     const float g = a.pos_none ? 0.f : -softplus(a.p.relation_decay_raw[e * a.H + h]);
@@ -416,7 +453,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     unit_vec(qv, sm + Lm.qo + j * mx, M, red);
     const int64_t szB = (int64_t)M * Dv;
     float* Bg = a.s.outer[j] + u * szB;
-    load_mat(Ss, Bg, (int)szB, nullptr);
+    load_mat(Ss, Bg, (int)szB, nullptr, bl);
     float* pre = sm + Lm.pre;
     colsum(Ss, M, Dv, kv, pre, part);
     const float* gt = sm + Lm.gates + 4 * j;
@@ -430,6 +467,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   // the last CTA to arrive may overwrite it.  It also resets the counter for the next step.
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (!bl.ok) atomicExch(&g_decode_status, GPA_B200_DEVICE_TIMEOUT);
     __threadfence();
     const unsigned done = atomicAdd(reinterpret_cast<unsigned*>(a.offset + 1), 1u);
     if (done == gridDim.x - 1) {
@@ -443,6 +481,16 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
 }  // namespace
 
 size_t decode_step_smem(const StepArgs& a) { return StepSmem(a).total; }
+
+int decode_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_decode_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
 
 cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st) {
   const size_t smem = decode_step_smem(a);

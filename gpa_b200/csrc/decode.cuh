@@ -26,5 +26,8 @@ size_t decode_step_smem(const StepArgs& a);
 // Stream-ordered, one kernel (its last CTA advances the offset).  No allocation, no host
 // synchronization (capturable in a CUDA graph).
 cudaError_t launch_decode_step(const StepArgs& a, cudaStream_t st);
+// device status word of the step kernel (GPA_B200_DEVICE_TIMEOUT after a bulk-load wait gave
+// up); synchronous read, optionally clearing it; -1 if the read failed
+int decode_device_status(bool clear);
 
 }  // namespace gpa

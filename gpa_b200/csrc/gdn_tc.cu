@@ -14,6 +14,7 @@
 #include "gdn.cuh"
 #include "gdn_dev.cuh"
 #include "mma.cuh"
+#include "tc5.cuh"
 #include "tc_util.cuh"
 
 namespace gpa {
@@ -805,6 +806,15 @@ __global__ void __launch_bounds__(kThreads) tc_bwd_chunk(ScanBatch b, int U, Blo
     db[t] = dlam[t] = rw[t] = 0.f;
   }
   if (threadIdx.x < 32) red[threadIdx.x] = 0.f;
+  if (threadIdx.x == 32) {
+    // rows the later stages read (U and V path, Wk path, the K tile, the dK accumulator):
+    // start them towards L2 now so that those stages wait on L2, not DRAM
+    tc5::prefetch_l2(d.k + r0 * K, (uint32_t)(c * K * 4));
+    tc5::prefetch_l2(d.Ub + r0 * V, (uint32_t)(c * V * 4));
+    tc5::prefetch_l2(d.v + r0 * V, (uint32_t)(c * V * 4));
+    tc5::prefetch_l2(d.Wk + r0 * K, (uint32_t)(c * K * 4));
+    tc5::prefetch_l2(d.dk + r0 * K, (uint32_t)(c * K * 4));
+  }
   float dsp = 0.f;  // this thread's part of <D, S>
   {  // gates, T of the block as the forward formed it, and the state-term operands
     const GateRegs gr = gate_fetch(d, u, t0, c, true);

@@ -163,11 +163,12 @@ int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, c
  * return_diagnostics routes of DenseGPA.forward (src/gpa/attention.py:407-413). */
 int gpa_b200_routes(const GpaDims* dims, const void* saved, void* const* routes, void* stream);
 
-/* Device status of the tensor-core kernels (no counterpart in the reference): 0, or
+/* Device status of the kernels that wait on mbarriers, the tensor-core kernels and
+ * the decode step's bulk state loads (no counterpart in the reference): 0, or
  * GPA_B200_DEVICE_TIMEOUT once a bounded wait inside one of them gave up since the
- * last clear (that kernel returned without its result).  Reads the device word
- * synchronously (the device must be current); clear != 0 resets it.  -1 if the
- * read failed. */
+ * last clear (that kernel returned without a usable result).  Reads the device
+ * words synchronously (the device must be current); clear != 0 resets them.  -1 if
+ * a read failed. */
 int gpa_b200_device_status(int clear);
 
 /* Self-test of the tensor-core building blocks (no counterpart in the reference):
