@@ -203,9 +203,25 @@ GPA_DEV void gdn_update(float* Ss, float* Sg, int K, int V, const float* kv, con
   colsum(Ss, K, V, qv, y, part);
 }
 
+// Offsets of one head's scalar parameters in shared memory: fetched together at kernel entry
+// (one load latency for all of them) instead of one dependent global load per use.
+struct HeadScalars {
+  int E, L;
+  GPA_DEV int edge_logit(int e) const { return e; }
+  GPA_DEV int relation_decay(int e) const { return E + e; }
+  GPA_DEV int relation_beta(int e) const { return 2 * E + e; }
+  GPA_DEV int relation_gain(int j) const { return 3 * E + j; }
+  GPA_DEV int count_gain(int j) const { return 3 * E + L + j; }
+  GPA_DEV int route_mlp_gain(int j) const { return 3 * E + 2 * L + j; }
+  GPA_DEV int output_logit(int j) const { return 3 * E + 3 * L + j; }
+  GPA_DEV int residual(int j, int c) const { return 3 * E + 4 * L + 2 * j + c; }
+  GPA_DEV int gate_bias(int j, int c) const { return 3 * E + 6 * L + 4 * j + c; }
+  GPA_DEV int count() const { return 3 * E + 10 * L; }
+};
+
 struct StepSmem {
   size_t Ss, q, qn, key, kn, val, tmp, tmp2, pre, yb, part, red, slot, write, logits, valin, qo,
-      gates, bar, total;
+      gates, hs, bar, total;
   int msg_off[kMaxEdges];
   __host__ __device__ StepSmem(const StepArgs& a) {
     size_t off = 0;
@@ -247,6 +263,7 @@ struct StepSmem {
     qo = take(a.L * mx);
     gates = take(a.L * 4);
     for (int e = 0; e < a.E; ++e) msg_off[e] = (int)take(a.M[a.ed[e]]);
+    hs = take(3 * kMaxEdges + 10 * kMaxLevels);  // this head's scalars (HeadScalars)
     bar = take(4);  // the bulk loads' mbarrier (16-byte aligned)
     total = off * sizeof(float);
   }
@@ -270,6 +287,30 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   float* part = sm + Lm.part;
   float* red = sm + Lm.red;
   BulkLoad bl{reinterpret_cast<uint64_t*>(sm + Lm.bar), 0u, true};
+  float* hs = sm + Lm.hs;
+  const HeadScalars hx{a.E, L};
+  for (int i = threadIdx.x; i < hx.count(); i += blockDim.x) {
+    const int E = a.E, H = a.H;
+    float x;
+    if (i < E) x = a.p.edge_logits[i * H + h];
+    else if (i < 2 * E) x = a.p.relation_decay_raw[(i - E) * H + h];
+    else if (i < 3 * E) x = a.p.relation_beta_raw[(i - 2 * E) * H + h];
+    else {
+      const int r = i - 3 * E, kind = r / L, j = r - kind * L;
+      if (kind == 0) x = a.p.relation_gain[j * H + h];
+      else if (kind == 1) x = a.p.count_gain_raw[j * H + h];
+      else if (kind == 2) x = a.p.route_mlp_gain[j * H + h];
+      else if (kind == 3) x = a.p.output_logits[j * H + h];
+      else if (kind < 6) {
+        const int q = r - 4 * L;  // residual_raw: 2 per level
+        x = a.p.residual_raw[((q >> 1) * H + h) * 2 + (q & 1)];
+      } else {
+        const int q = r - 6 * L;  // gate_bias: 4 per level
+        x = a.p.gate_bias[q >> 2][h * 4 + (q & 3)];
+      }
+    }
+    hs[i] = x;
+  }
   if (threadIdx.x == 0) {
     tc5::mbar_init(bl.bar, 1);
     tc5::mbar_fence_init();
@@ -309,7 +350,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
       __syncthreads();
       if (threadIdx.x == 0) {
         for (int c = 0; c < 4; ++c) {
-          float t = a.p.gate_bias[j][h * 4 + c];
+          float t = hs[hx.gate_bias(j, c)];
           for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[4 * w + c];
           r[c] = t;
         }
@@ -340,7 +381,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     }
     gdn_update(Ss, Ag, D, M, kn, slot, pre, gates[0], gates[1], qn, logits, part);  // logits <- raw
     {  // counts and base logits
-      const float cg = softplus(a.p.count_gain_raw[j * a.H + h]);
+      const float cg = softplus(hs[hx.count_gain(j)]);
       float* n = a.s.count[j] + (int64_t)u * M;
       for (int m = threadIdx.x; m < M; m += blockDim.x) {
         const float nn = n[m] + write[m];
@@ -354,8 +395,8 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
              o == 0 ? a.s.frozen_outer[j] + u * szB : nullptr, bl);
     colsum(Ss, M, Dv, write, rv, part);
     float* vin = sm + Lm.valin + j * Dv;
-    const float ek = 1.f + .25f * tanhf(a.p.residual_raw[(j * a.H + h) * 2 + 0]);
-    const float ev = 1.f + .25f * tanhf(a.p.residual_raw[(j * a.H + h) * 2 + 1]);
+    const float ek = 1.f + .25f * tanhf(hs[hx.residual(j, 0)]);
+    const float ev = 1.f + .25f * tanhf(hs[hx.residual(j, 1)]);
     for (int i = threadIdx.x; i < Dv; i += blockDim.x) {
       vin[i] = val[i];
       val[i] -= ev * rv[i];
@@ -377,8 +418,8 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     load_mat(Ss, Rg, (int)sz, nullptr, bl);
     float* prebuf = sm + Lm.pre;
     colsum(Ss, Mi, Mj, kv, prebuf, part);
-    const float g = a.pos_none ? 0.f : -softplus(a.p.relation_decay_raw[e * a.H + h]);
-    const float b = sigmoid(a.p.relation_beta_raw[e * a.H + h]);
+    const float g = a.pos_none ? 0.f : -softplus(hs[hx.relation_decay(e)]);
+    const float b = sigmoid(hs[hx.relation_beta(e)]);
     gdn_update(Ss, Rg, Mi, Mj, kv, sm + Lm.write + j * mx, prebuf, g, b, lq,
                sm + Lm.msg_off[e], part);
   }
@@ -394,17 +435,17 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     for (int e = 0; e < a.E; ++e)
       if (a.ed[e] == j) {
         ++nin;
-        wmax = fmaxf(wmax, a.p.edge_logits[e * a.H + h]);
+        wmax = fmaxf(wmax, hs[hx.edge_logit(e)]);
       }
     for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] = logits[m];
     if (nin > 0) {
       float ws = 0.f;
       for (int e = 0; e < a.E; ++e)
-        if (a.ed[e] == j) ws += __expf(a.p.edge_logits[e * a.H + h] - wmax);
+        if (a.ed[e] == j) ws += __expf(hs[hx.edge_logit(e)] - wmax);
       for (int m = threadIdx.x; m < M; m += blockDim.x) {
         float x = 0.f;
         for (int e = 0; e < a.E; ++e)
-          if (a.ed[e] == j) x += (__expf(a.p.edge_logits[e * a.H + h] - wmax) / ws) * sm[Lm.msg_off[e] + m];
+          if (a.ed[e] == j) x += (__expf(hs[hx.edge_logit(e)] - wmax) / ws) * sm[Lm.msg_off[e] + m];
         inc[m] = x;
       }
       __syncthreads();
@@ -414,7 +455,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
       float vs = 0.f;
       for (int m = threadIdx.x; m < M; m += blockDim.x) vs += (inc[m] - mean) * (inc[m] - mean);
       const float sd = rsqrtf(block_sum_all(vs, red) / M + kCenterEps);
-      const float rg = a.p.relation_gain[j * a.H + h];
+      const float rg = hs[hx.relation_gain(j)];
       for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] += rg * tanhf((inc[m] - mean) * sd);
       __syncthreads();
     }
@@ -425,7 +466,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     __syncthreads();
     float* mlp = sm + Lm.qo + j * mx;  // scratch until qo is formed
     colsum(a.p.route_down[j] + (int64_t)h * 2 * M * M, 2 * M, M, hid, mlp, part);
-    const float mg = a.p.route_mlp_gain[j * a.H + h];
+    const float mg = hs[hx.route_mlp_gain(j)];
     for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] += mg * mlp[m];
     __syncthreads();
     float* qo = sm + Lm.qo + j * mx;
@@ -437,9 +478,9 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   float ow[kMaxLevels];
   {
     float mxl = -INFINITY, s = 0.f;
-    for (int j = 0; j < L; ++j) mxl = fmaxf(mxl, a.p.output_logits[j * a.H + h]);
+    for (int j = 0; j < L; ++j) mxl = fmaxf(mxl, hs[hx.output_logit(j)]);
     for (int j = 0; j < L; ++j) {
-      ow[j] = __expf(a.p.output_logits[j * a.H + h] - mxl);
+      ow[j] = __expf(hs[hx.output_logit(j)] - mxl);
       s += ow[j];
     }
     for (int j = 0; j < L; ++j) ow[j] /= s;
