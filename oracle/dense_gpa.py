@@ -8,8 +8,9 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 It restates the reference's ``backend="torch"`` algorithm (package
 ``gpa-attention`` v0.4.0) for the default flag set the b200 backend accepts:
 ``positional_mode`` in {"gated", "none"}, linear slot features, no RSA update,
-no product read, no control input, no quadratic features, no balanced bridge,
-fixed read scale.  Every function cites the reference lines it follows
+no control input, no quadratic features, no balanced bridge, fixed read scale;
+the reader in its centred-tanh form or the product form (``paper_product_read``,
+optionally ``relation_marginal``).  Every function cites the reference lines it follows
 (paths are relative to the reference project root).  Dtype handling follows
 the reference exactly: states are float32 (float64 for float64 inputs) and the
 activation dtype is rounded at the same points, so the restatement can be
@@ -49,6 +50,8 @@ class OracleConfig:
     relation_beta_init: float = .6
     relation_decay_init: float = .0001
     read_scale: float = 1.
+    paper_product_read: bool = False
+    relation_marginal: bool = False
 
 
 @dataclass(frozen=True)
@@ -243,18 +246,30 @@ def _relations(cfg, p, edges, local, writes, rel_states):
     return messages, tuple(new)
 
 
-def _bridge(cfg, p, q, logits, messages):
-    """Dense reader: edge mix, centred tanh correction, route softmax + MLP, query
-    projection (src/gpa/attention.py:225-262, default flags)."""
+def _bridge(cfg, p, edges, q, logits, messages, counts):
+    """Dense reader: edge mix, then the centred tanh correction or the product read (each
+    message times the norm of its source level's route softmax, added with gain
+    M e^{clamp(g, -4, 4)}, minus e^{clamp(g)} log1p(counts) when marginal), route softmax +
+    MLP, query projection (src/gpa/attention.py:225-262, flags rsa_update,
+    shared_query_center and balanced_bridge off)."""
     routes, qouts = [], []
     for j, base in enumerate(logits):
         if messages[j]:
             ids = [e for e, _ in messages[j]]
             weights = p["edge_logits"][ids].softmax(0)
-            incoming = sum(w[..., None] * msg for w, (_, msg) in zip(weights, messages[j]))
-            centered = incoming - incoming.mean(-1, keepdim=True)
-            normalized = centered / (centered.square().mean(-1, keepdim=True) + 1e-5).sqrt()
-            base = base + p["relation_gain"][j][..., None] * normalized.tanh()
+            if cfg.paper_product_read:
+                gain = p["relation_gain"][j].clamp(-4, 4).exp()[..., None]
+                incoming = sum(w[..., None] * msg
+                               * logits[edges[e][0]].softmax(-1).norm(dim=-1, keepdim=True)
+                               for w, (e, msg) in zip(weights, messages[j]))
+                base = base + base.shape[-1] * gain * incoming
+                if cfg.relation_marginal:
+                    base = base - gain * counts[j].log1p()
+            else:
+                incoming = sum(w[..., None] * msg for w, (_, msg) in zip(weights, messages[j]))
+                centered = incoming - incoming.mean(-1, keepdim=True)
+                normalized = centered / (centered.square().mean(-1, keepdim=True) + 1e-5).sqrt()
+                base = base + p["relation_gain"][j][..., None] * normalized.tanh()
         route = base.softmax(-1).to(q.dtype)
         hidden = F.gelu(torch.einsum("...hm,hmr->...hr", route, p[f"route_up.{j}"].to(q.dtype)))
         route = route + p["route_mlp_gain"][j][..., None] * torch.einsum(
@@ -289,7 +304,7 @@ def _token(cfg, p, edges, q, k, v, state):
     local = [x.softmax(-1).to(q.dtype).unsqueeze(1) for x in logits]
     messages, rel = _relations(cfg, p, edges, local, [x.unsqueeze(1) for x in writes], state.relations)
     messages = [[(e, m[:, 0]) for e, m in group] for group in messages]
-    routes, qouts = _bridge(cfg, p, q, logits, messages)
+    routes, qouts = _bridge(cfg, p, edges, q, logits, messages, [lv[2] for lv in levels])
     weights = p["output_logits"].softmax(0)
     out = sum(weights[j][..., None] * read(qo, levels[j][1]) for j, qo in enumerate(qouts))
     new = OracleState(tuple(levels), rel, state.position + 1, cfg.chunk_size, 0, None)
@@ -300,7 +315,7 @@ def _block(cfg, p, edges, q, k, v, state):
     """One lag block with frozen residual snapshots (src/gpa/attention.py:299-345)."""
     frozen = state.frozen or tuple((a, b) for a, b, _ in state.levels)
     key, value = k, v
-    finals, writes, logits, outer_in = [], [], [], []
+    finals, writes, logits, outer_in, history = [], [], [], [], []
     for j, ((a_old, _b_old, n_old), (fa, fb)) in enumerate(zip(state.levels, frozen)):
         slot = _slot(p, j, key)
         gi, bi, go, bo = _gates(cfg, p, j, key)
@@ -308,6 +323,7 @@ def _block(cfg, p, edges, q, k, v, state):
         write = torch.einsum("bthd,bhdm->bthm", unit(key).to(fa.dtype), fa).softmax(-1)
         write = write.to(q.dtype)
         counts = n_old[:, None] + write.to(n_old.dtype).cumsum(1)
+        history.append(counts)
         logits.append(_base_logits(cfg, p, j, raw, counts))
         writes.append(write)
         finals.append((a, counts[:, -1]))
@@ -317,7 +333,7 @@ def _block(cfg, p, edges, q, k, v, state):
         key, value = _residual(p, j, key, value, rk, rv)
     local = [x.softmax(-1).to(q.dtype) for x in logits]
     messages, rel = _relations(cfg, p, edges, local, writes, state.relations)
-    routes, qouts = _bridge(cfg, p, q, logits, messages)
+    routes, qouts = _bridge(cfg, p, edges, q, logits, messages, history)
     outs, levels = [], []
     for j, qo in enumerate(qouts):
         slot, vl, go, bo = outer_in[j]

@@ -57,6 +57,24 @@ CASES = {
                                  chunk_size=64), execution="staged", batch=1, length=320,
                         dtype="bfloat16", seed=23, prefix_std=.02, unit_qk=True, decode=1,
                         oracle_param_tol=5e-2),
+    # the product reader (paper_product_read, src/gpa/attention.py:231-236): messages times the
+    # norm of the source level's route softmax, gain M e^{clamp(g)}; lag blocks, float64
+    "product_f64": dict(cfg=dict(heads=2, key_dim=8, value_dim=6, slots=(4, 8, 6), chunk_size=4,
+                                 paper_product_read=True),
+                        batch=2, length=13, dtype="float64", seed=31,
+                        partitions=((0, 5), (5, 6), (6, 13)), decode=2),
+    # product reader with the marginal count term, exact token recurrence, float64
+    "marginal_token_f64": dict(cfg=dict(heads=2, key_dim=4, value_dim=3, slots=(3, 2, 4),
+                                        chunk_size=1, paper_product_read=True,
+                                        relation_marginal=True),
+                               batch=2, length=7, dtype="float64", seed=32,
+                               partitions=((0, 3), (3, 7)), decode=1),
+    # product + marginal at 64-token blocks with a partial tail, fp32
+    "marginal_c64_f32": dict(cfg=dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
+                                      chunk_size=64, paper_product_read=True,
+                                      relation_marginal=True),
+                             batch=1, length=130, dtype="float32", seed=33, prefix_std=.02,
+                             partitions=((0, 47), (47, 65), (65, 130)), decode=1),
 }
 
 DTYPES = {"float32": torch.float32, "float64": torch.float64, "bfloat16": torch.bfloat16}
