@@ -12,7 +12,7 @@ from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_size_t, c_void_
 
 MAX_LEVELS = 8
 MAX_EDGES = 56
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgpa_b200.so")
 
 STATUS = {0: "ok", 1: "bad argument", 2: "unsupported configuration", 3: "CUDA launch failure",
@@ -25,7 +25,7 @@ class GpaDims(ctypes.Structure):
                 ("slots", c_int32 * MAX_LEVELS), ("chunk_size", c_int32),
                 ("chunk_offset", c_int32), ("input_dtype", c_int32),
                 ("positional_none", c_int32), ("read_scale", c_float),
-                ("query_scale", c_float), ("beta_max", c_float)]
+                ("query_scale", c_float), ("beta_max", c_float), ("reader_mode", c_int32)]
 
 
 _LEVEL_PARAMS = ("center", "route_weight", "query_weight", "route_up", "route_down",

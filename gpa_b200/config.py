@@ -76,8 +76,6 @@ class GPAConfig:
         unsupported = [name for name, on in (
             ("positional_mode='moments'", self.positional_mode == "moments"),
             ("rsa_update", self.rsa_update),
-            ("paper_product_read", self.paper_product_read),
-            ("relation_marginal", self.relation_marginal),
             ("control_dim", self.control_dim != 0),
             ("slot_feature!='linear'", self.slot_feature != "linear"),
             ("balanced_bridge", self.balanced_bridge),

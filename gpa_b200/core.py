@@ -57,6 +57,7 @@ class _Plan:
         d.input_dtype = _DTYPES[q.dtype]
         d.positional_none = int(cfg.positional_mode == "none")
         d.read_scale, d.query_scale, d.beta_max = cfg.read_scale, cfg.query_scale, cfg.beta_max
+        d.reader_mode = (2 if cfg.relation_marginal else 1) if cfg.paper_product_read else 0
         self.dims = d
 
     def state_ref(self, flat, with_frozen: bool) -> _lib.GpaStateRef:

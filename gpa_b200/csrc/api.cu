@@ -67,6 +67,7 @@ int fail(int code, const std::string& msg) {
 
 struct Geo {
   int B, T, H, D, Dv, L, E, C, offset, post, dt, pos_none, U;
+  int reader;  // GPA_B200_READER_*
   int M[kMaxLevels];
   int es[kMaxEdges], ed[kMaxEdges];
   float rs, qs, bm;
@@ -74,6 +75,13 @@ struct Geo {
   int Mmax;
   int fast;  // tensor-core GDN kernels (bf16 / fp16 inputs, widths multiples of 16)
 };
+
+// whether level j reads relation messages (some edge ends at it)
+bool has_incoming(const Geo& g, int j) {
+  for (int e = 0; e < g.E; ++e)
+    if (g.ed[e] == j) return true;
+  return false;
+}
 
 int make_geo(const GpaDims* d, Geo* g, std::string* why) {
   if (!d) {
@@ -93,6 +101,11 @@ int make_geo(const GpaDims* d, Geo* g, std::string* why) {
   g->rs = d->read_scale;
   g->qs = d->query_scale;
   g->bm = d->beta_max;
+  g->reader = d->reader_mode;
+  if (g->reader < GPA_B200_READER_TANH || g->reader > GPA_B200_READER_MARGINAL) {
+    *why = "reader_mode must be GPA_B200_READER_TANH, _PRODUCT or _MARGINAL";
+    return GPA_B200_BAD_ARGUMENT;
+  }
   if (g->B <= 0 || g->T < 0 || g->H <= 0 || g->D <= 0 || g->Dv <= 0 || g->L <= 0) {
     *why = "dimensions must be positive";
     return GPA_B200_BAD_ARGUMENT;
@@ -256,6 +269,7 @@ struct Scratch {
   float *dqoh[kMaxLevels], *dqo[kMaxLevels], *droute[kMaxLevels], *dhp[kMaxLevels];
   float *dlogits[kMaxLevels], *dlh[kMaxLevels], *dwh[kMaxLevels], *dwrite[kMaxLevels];
   float *odK[kMaxLevels], *odW[kMaxLevels], *odG[kMaxLevels];
+  float* dln[kMaxLevels];  // gradient of |softmax(logits_j)| per row (product reader)
   float* dmsg[kMaxEdges];
   float *draw, *dn, *dnsum, *extA, *extB, *dnk, *dslot, *dns, *dgates, *d4;
   float *dfzA, *dfzB;
@@ -290,6 +304,7 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
     s->odK[j] = b.take(UT * M);
     s->odW[j] = b.take(UT * g.Dv);
     s->odG[j] = b.take(UT);
+    s->dln[j] = b.take(UT);
   }
   for (int e = 0; e < g.E; ++e) s->dmsg[e] = b.take(UT * g.M[g.ed[e]]);
   s->draw = b.take(UT * Mx);
@@ -475,11 +490,15 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
   for (int j = 0; j < g.L; ++j) {
     BridgeIn bi;
     bi.n = 0;
+    bi.mode = g.reader;
+    bi.counts = s.counts[j];
     for (int e = 0; e < g.E; ++e)
       if (g.ed[e] == j) {
         bi.edge[bi.n] = e;
         bi.msg[bi.n] = s.msg[e];
         bi.dmsg[bi.n] = nullptr;
+        bi.ln[bi.n] = s.ln[g.es[e]];
+        bi.dln[bi.n] = nullptr;
         ++bi.n;
       }
     CK((g.fast ? tc_bridge : launch_bridge)(U, T, g.H, D, g.M[j], g.L, j, bi, p->edge_logits, p->relation_gain,
@@ -565,6 +584,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     CK(zero(x.dwrite[j], UT * M, st));
     CK(zero(x.odK[j], UT * M, st));
     CK(zero(x.odG[j], UT, st));
+    if (g.reader != GPA_B200_READER_TANH) CK(zero(x.dln[j], UT, st));
   }
   CK(launch_scales(U, H, L, p->output_logits, x.ow_scale, st));
   std::vector<const float*> ys(s.y, s.y + L);
@@ -603,11 +623,15 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
   for (int j = 0; j < L; ++j) {
     BridgeIn bi;
     bi.n = 0;
+    bi.mode = g.reader;
+    bi.counts = s.counts[j];
     for (int e = 0; e < E; ++e)
       if (g.ed[e] == j) {
         bi.edge[bi.n] = e;
         bi.msg[bi.n] = s.msg[e];
         bi.dmsg[bi.n] = x.dmsg[e];
+        bi.ln[bi.n] = s.ln[g.es[e]];
+        bi.dln[bi.n] = x.dln[g.es[e]];
         ++bi.n;
       }
     const int M = g.M[j];
@@ -687,7 +711,11 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     CK(zero(x.dnsum, (size_t)U * bl.nb * M, st));
     CK(launch_logits_bwd(U, bl, H, M, L, j, g.rs, p->count_gain_raw, s.logits[j], s.counts[j],
                          s.lh[j], s.ln[j], s.wh[j], s.wn[j], x.dlh[j], x.dwh[j], x.dlogits[j],
-                         x.dwrite[j], x.draw, x.dn, x.dnsum, x.scal, st));
+                         x.dwrite[j], x.draw, x.dn, x.dnsum, x.scal,
+                         ProductBwd{g.reader != GPA_B200_READER_TANH ? x.dln[j] : nullptr,
+                                    p->relation_gain,
+                                    g.reader == GPA_B200_READER_MARGINAL && has_incoming(g, j)},
+                         st));
     CK(launch_counts_bwd(U, bl, M, x.dn, x.dnsum, ds.count[j], x.dwrite[j], dsi->count[j], st));
     const size_t szA = (size_t)D * M, szB = (size_t)M * Dv;
     CK(zero(x.extA, (size_t)U * (bl.nb + 1) * szA, st));
@@ -899,6 +927,7 @@ int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, c
   }
   a.dt = g.dt;
   a.pos_none = g.pos_none;
+  a.reader = g.reader;
   a.query_scale = g.qs;
   a.beta_max = g.bm;
   a.read_scale = g.rs;
@@ -1041,7 +1070,7 @@ int gpa_b200_last_error(char* buf, size_t len) {
   return g_last_error.empty() ? 0 : 1;
 }
 
-int gpa_b200_abi_version(void) { return 1; }
+int gpa_b200_abi_version(void) { return 2; }
 
 long long gpa_b200_launch_count(void) { return g_launches.load(); }
 

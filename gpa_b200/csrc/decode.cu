@@ -425,6 +425,16 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   }
 
   // ------------------------------------------------ dense reader and outer steps
+  // product reader: |softmax(logits_i)| of every level, the factor of the messages it sends
+  float lnorm[kMaxLevels];
+  if (a.reader != GPA_B200_READER_TANH)
+    for (int i = 0; i < L; ++i) {
+      softmax_vec(tmp, sm + Lm.logits + i * mx, a.M[i], red);
+      float ss = 0.f;
+      for (int m = threadIdx.x; m < a.M[i]; m += blockDim.x) ss += tmp[m] * tmp[m];
+      lnorm[i] = sqrtf(block_sum_all(ss, red));
+      __syncthreads();
+    }
   for (int j = 0; j < L; ++j) {
     const int M = a.M[j];
     float* base = tmp;  // [M]
@@ -438,7 +448,24 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
         wmax = fmaxf(wmax, hs[hx.edge_logit(e)]);
       }
     for (int m = threadIdx.x; m < M; m += blockDim.x) base[m] = logits[m];
-    if (nin > 0) {
+    if (nin > 0 && a.reader != GPA_B200_READER_TANH) {
+      // base += e^{clamp(g)} (M sum_e w_e |softmax(logits_src)| msg_e - log1p(counts) if
+      // marginal), with this token's counts
+      float ws = 0.f;
+      for (int e = 0; e < a.E; ++e)
+        if (a.ed[e] == j) ws += __expf(hs[hx.edge_logit(e)] - wmax);
+      const float ge = __expf(fminf(fmaxf(hs[hx.relation_gain(j)], -4.f), 4.f));
+      const bool marg = a.reader == GPA_B200_READER_MARGINAL;
+      const float* cnt = a.s.count[j] + (int64_t)u * M;
+      for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        float x = 0.f;
+        for (int e = 0; e < a.E; ++e)
+          if (a.ed[e] == j)
+            x += (__expf(hs[hx.edge_logit(e)] - wmax) / ws) * lnorm[a.es[e]] * sm[Lm.msg_off[e] + m];
+        base[m] += ge * (M * x - (marg ? log1pf(cnt[m]) : 0.f));
+      }
+      __syncthreads();
+    } else if (nin > 0) {
       float ws = 0.f;
       for (int e = 0; e < a.E; ++e)
         if (a.ed[e] == j) ws += __expf(hs[hx.edge_logit(e)] - wmax);

@@ -12,6 +12,7 @@ struct StepArgs {
   int M[kMaxLevels];
   int es[kMaxEdges], ed[kMaxEdges];
   int dt, pos_none;
+  int reader;  // GPA_B200_READER_* (dense reader form)
   float query_scale, beta_max, read_scale;
   GpaParams p;
   GpaStateRef s;  // updated in place; frozen_* required

@@ -286,7 +286,25 @@ __global__ void __launch_bounds__(256) k_bridge(
     const int64_t o = row(u, T, t0 + t);
     float base[kMaxPerLane];
     load_vec(base, logits + o * M, M);
-    if (in.n > 0) {
+    if (in.n > 0 && in.mode != GPA_B200_READER_TANH) {
+      // product reader: base += e^{clamp(g)} (M sum_a w_a n_a msg_a - log1p(counts) if marginal)
+      float inc[kMaxPerLane], cn[kMaxPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+        const float f = w[a] * in.ln[a][o];
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) inc[i] += f * x[i];
+      }
+      const bool marg = in.mode == GPA_B200_READER_MARGINAL;
+      if (marg) load_vec(cn, in.counts + o * M, M);
+      const float ge = product_gain(rg);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i)
+        base[i] += ge * (M * inc[i] - (marg ? log1pf(cn[i]) : 0.f));
+    } else if (in.n > 0) {
       float inc[kMaxPerLane];
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
@@ -567,7 +585,41 @@ __global__ void __launch_bounds__(256) k_bridge_bwd(
     load_vec(dr, R + t * M, M);
     softmax_bwd(db, r, dr, M);
     store_vec(dlogits + o * M, db, M);
-    if (in.n > 0) {
+    if (in.n > 0 && in.mode != GPA_B200_READER_TANH) {
+      // product reader: dinc = e^{clamp(g)} M db; with s_a = dinc . msg_a and the source norm
+      // n_a, dmsg_a = w_a n_a dinc, d edge-weight_a += n_a s_a, dn_a += w_a s_a
+      float inc[kMaxPerLane], cn[kMaxPerLane], dz[kMaxPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+        const float f = w[a] * in.ln[a][o];
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) inc[i] += f * x[i];
+      }
+      const bool marg = in.mode == GPA_B200_READER_MARGINAL;
+      if (marg) load_vec(cn, in.counts + o * M, M);
+      const float ge = product_gain(rg);
+      float gp = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        const float tm = M * inc[i] - (marg ? log1pf(cn[i]) : 0.f);
+        if (lane + 32 * i < M) gp += db[i] * tm;
+        dz[i] = ge * M * db[i];
+      }
+      rg_acc += warp_sum(gp) * ge * product_gain_live(rg);
+      for (int a = 0; a < in.n; ++a) {
+        float x[kMaxPerLane], dm[kMaxPerLane];
+        load_vec(x, in.msg[a] + o * M, M);
+        const float na = in.ln[a][o], s = warp_dot(dz, x, M);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) dm[i] = w[a] * na * dz[i];
+        store_vec(in.dmsg[a] + o * M, dm, M);
+        ew_acc[a] += na * s;
+        if (lane == 0) in.dln[a][o] += w[a] * s;
+      }
+    } else if (in.n > 0) {
       float inc[kMaxPerLane];
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) inc[i] = 0.f;
@@ -664,7 +716,7 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     int U, Blocks bl, int H, int M, int L, int j, float read_scale, const float* count_gain_raw,
     const float* logits, const float* counts, const float* lh, const float* ln, const float* wh,
     const float* wn, const float* dlh, const float* dwh, const float* dlogits, float* dwrite,
-    float* draw, float* dn, float* dnsum, double* scal) {
+    float* draw, float* dn, float* dnsum, double* scal, ProductBwd pb) {
   __shared__ float red_dn[8][32 * NPL];
   __shared__ int blk[8];
   __shared__ float red_cg[8];  // count-gain partial of each warp's row (one atomic per unit run)
@@ -711,6 +763,12 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
 #pragma unroll
       for (int i = 0; i < NPL; ++i) d1.v[i] = dy.v[i] / kUnitEps;
     }
+    if (pb.dln) {  // the norm |softmax(logits)| read by the product reader: d/dp = lh
+      const float dl_n = pb.dln[w];
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) d1.v[i] += dl_n * y.v[i];
+    }
+    const float ge = pb.marginal ? product_gain(pb.relation_gain[j * H + h]) : 0.f;
     const float xd = x.dot(d1, M);
     RowV<NPL> dr, dnv;
     float cg = 0.f;
@@ -719,7 +777,7 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
       const float dl = dlg.v[i] + x.v[i] * (d1.v[i] - xd);
       dr.v[i] = read_scale * dl;
       if (lane + 32 * i < M) cg += dl * log1pf(cn.v[i]);
-      dnv.v[i] = gain * dl / (1.f + cn.v[i]);
+      dnv.v[i] = (gain * dl - ge * dlg.v[i]) / (1.f + cn.v[i]);
     }
     dr.store(draw + o, M);
     dnv.store(dn + o, M);
@@ -1346,7 +1404,8 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, double* scal, cudaStream_t st) {
+                              float* dn, float* dnsum, double* scal, ProductBwd pb,
+                              cudaStream_t st) {
   const int rows = U * bl.T;
   if (!rows) return cudaSuccess;
   Launch scope_("logits_bwd", st);
@@ -1354,17 +1413,17 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
     k_logits_bwd<2><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal);
+                                                     dnsum, scal, pb);
   else if (M <= 128)
     k_logits_bwd<4><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal);
+                                                     dnsum, scal, pb);
   else
     k_logits_bwd<8><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal);
+                                                     dnsum, scal, pb);
   return cudaGetLastError();
 }
 

@@ -2,6 +2,7 @@
 // Launchers are declared here and defined in level.cu; all are stream-ordered
 // and allocate nothing.  Buffers are fp32, unit-major [U, T, X] (see common.cuh).
 #pragma once
+#include "../../include/gpa_b200.h"
 #include "common.cuh"
 
 namespace gpa {
@@ -20,6 +21,13 @@ struct BridgeIn {
   int edge[kMaxIn];           // edge ids
   const float* msg[kMaxIn];   // [U,T,M]
   float* dmsg[kMaxIn];        // [U,T,M] (backward)
+  // product reader (mode GPA_B200_READER_PRODUCT / _MARGINAL): each message times the norm of
+  // its source level's route softmax, ln [U,T]; the backward adds the gradient of that norm
+  // into dln [U,T] (one writer per row and source level in a launch)
+  int mode;
+  const float* ln[kMaxIn];
+  float* dln[kMaxIn];
+  const float* counts;        // [U,T,M] counts of the target level (marginal term)
 };
 
 cudaError_t launch_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
@@ -75,12 +83,21 @@ cudaError_t launch_bridge_bwd(int U, int T, int H, int D, int M, int L, int j, c
                               const float* dqoh, float* dqo, float* droute, float* dhp,
                               float* dlogits, float* dq_direct, double* scal, double* scalE, int E,
                               cudaStream_t st);
+// Product-reader terms of a level's logits backward: dln [U,T] (gradient of the norm of the
+// level's route softmax, from the readers it feeds; null: none) and, for the marginal reader
+// on a level with incoming edges, the count term -e^{clamp(relation_gain)} dlogits / (1 + n).
+struct ProductBwd {
+  const float* dln;
+  const float* relation_gain;  // [L,H]
+  int marginal;
+};
 cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int j,
                               float read_scale, const float* count_gain_raw, const float* logits,
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, double* scal, cudaStream_t st);
+                              float* dn, float* dnsum, double* scal, ProductBwd pb,
+                              cudaStream_t st);
 cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, const float* dnsum,
                               const float* dn_final, float* dwrite, float* dn0, cudaStream_t st);
 cudaError_t launch_post_bwd(int U, const Blocks& bl, int post, int offset, int H, int D, int Dv,

@@ -247,16 +247,20 @@ GPA_DEV void stage_incoming(float* inc, const BridgeIn& in, const float* w, int6
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (t < c) {
       float4 x[kMaxIn];
-#pragma unroll
-      for (int a = 0; a < kMaxIn; ++a)
-        if (a < in.n) x[a] = *reinterpret_cast<const float4*>(in.msg[a] + r0 * M + 4 * i);
+      float f[kMaxIn];  // edge weight, times the source norm for the product reader
 #pragma unroll
       for (int a = 0; a < kMaxIn; ++a)
         if (a < in.n) {
-          acc.x += w[a] * x[a].x;
-          acc.y += w[a] * x[a].y;
-          acc.z += w[a] * x[a].z;
-          acc.w += w[a] * x[a].w;
+          x[a] = *reinterpret_cast<const float4*>(in.msg[a] + r0 * M + 4 * i);
+          f[a] = in.mode != GPA_B200_READER_TANH ? w[a] * in.ln[a][r0 + t] : w[a];
+        }
+#pragma unroll
+      for (int a = 0; a < kMaxIn; ++a)
+        if (a < in.n) {
+          acc.x += f[a] * x[a].x;
+          acc.y += f[a] * x[a].y;
+          acc.z += f[a] * x[a].z;
+          acc.w += f[a] * x[a].w;
         }
     }
     *reinterpret_cast<float4*>(inc + t * ld + 4 * i - t * M) = acc;
@@ -270,12 +274,22 @@ GPA_DEV void stage_rows(float* dst, const float* src, int c, int M) {
         i / m4 < c ? *reinterpret_cast<const float4*>(src + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// reader_row_fwd with the row's logits and weighted incoming message in shared memory
+// reader_row_fwd with the row's logits and weighted incoming message in shared memory; for
+// the product reader base += e^{clamp(g)} (M inc - log1p(counts) when marginal), cnt the
+// row's counts
 template <int N>
 GPA_DEV void reader_row_fwd_s(float (&base)[N], const float* lg, const float* incr,
-                              int M, bool has_in, float rg) {
+                              int M, bool has_in, float rg, int mode, const float* cnt) {
   load_vec(base, lg, M);
-  if (has_in) {
+  if (has_in && mode != GPA_B200_READER_TANH) {
+    float inc[N], cn[N];
+    load_vec(inc, incr, M);
+    if (mode == GPA_B200_READER_MARGINAL) load_vec(cn, cnt, M);
+    const float ge = product_gain(rg);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      base[i] += ge * (M * inc[i] - (mode == GPA_B200_READER_MARGINAL ? log1pf(cn[i]) : 0.f));
+  } else if (has_in) {
     const int lane = threadIdx.x & 31;
     float inc[N];
     load_vec(inc, incr, M);
@@ -300,16 +314,33 @@ GPA_DEV void reader_row_fwd_s(float (&base)[N], const float* lg, const float* in
 }
 
 // reader_row_bwd up to dz (the gradient of the weighted incoming message), which the caller
-// scatters to the messages and edge weights tile-wise.
+// scatters to the messages and edge weights.  Product reader: dz = e^{clamp(g)} M db, and the
+// gain's gradient sum db (M inc - log1p(counts)) e^{g} inside the clamp (cnt: the row's counts).
 template <int N>
 GPA_DEV void reader_row_bwd_s(float (&db)[N], float (&dz)[N], const float (&r)[N],
                               const float (&dr)[N],
-                              const float* incr, int M, bool has_in, float rg, float& rg_acc) {
+                              const float* incr, int M, bool has_in, float rg, float& rg_acc,
+                              int mode, const float* cnt) {
   const int lane = threadIdx.x & 31;
   softmax_bwd(db, r, dr, M);
 #pragma unroll
   for (int i = 0; i < N; ++i) dz[i] = 0.f;
   if (!has_in) return;
+  if (mode != GPA_B200_READER_TANH) {
+    float inc[N], cn[N];
+    load_vec(inc, incr, M);
+    if (mode == GPA_B200_READER_MARGINAL) load_vec(cn, cnt, M);
+    const float ge = product_gain(rg);
+    float gp = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float t = M * inc[i] - (mode == GPA_B200_READER_MARGINAL ? log1pf(cn[i]) : 0.f);
+      if (lane + 32 * i < M) gp += db[i] * t;
+      dz[i] = ge * M * db[i];
+    }
+    rg_acc += warp_sum(gp) * ge * product_gain_live(rg);
+    return;
+  }
   float inc[N];
   load_vec(inc, incr, M);
   float mean = 0.f;
@@ -398,7 +429,8 @@ __global__ void __launch_bounds__(512) tk_bridge(
     float x[NPL];
     if (t < c) {
       const int64_t o = row(u, T, t0 + t);
-      reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * (M + 8), M, in.n > 0, rg);
+      reader_row_fwd_s(x, (const float*)(smem + Lb.Hb) + t * M, Of + t * (M + 8), M, in.n > 0, rg,
+                       in.mode, in.counts ? in.counts + o * M : nullptr);
       store_vec(r_out + o * M, x, M);
     } else {
 #pragma unroll
@@ -625,7 +657,8 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
       float r[NPL], dr[NPL], db[NPL];
       load_vec(r, Rr + t * M, M);
       load_vec(dr, Rf + t * M, M);
-      reader_row_bwd_s(db, dz, r, dr, Inc + t * M, M, in.n > 0, rg, rg_acc);
+      reader_row_bwd_s(db, dz, r, dr, Inc + t * M, M, in.n > 0, rg, rg_acc, in.mode,
+                       in.counts ? in.counts + row(u, T, t0 + t) * M : nullptr);
       store_vec(dlogits + row(u, T, t0 + t) * M, db, M);
     } else {
 #pragma unroll
@@ -636,6 +669,31 @@ __global__ void __launch_bounds__(512) tk_bridge_bwd(
   if (in.n == 0) return;
   if (lane == 0) atomicAdd(&scal[((int64_t)u * L + j) * kNScal + kS_RelGain], (double)rg_acc);
   __syncthreads();
+  if (in.mode != GPA_B200_READER_TANH) {
+    // product reader, a warp per row: with s_a = dz . msg_a and the source norm n_a of the row,
+    // dmsg_a = w_a n_a dz, d edge-weight_a += n_a s_a, dn_a += w_a s_a
+    for (int a = 0; a < in.n; ++a) {
+      float part = 0.f;
+      for (int t = warp; t < c; t += nw) {
+        const int64_t o = row(u, T, t0 + t);
+        float z[NPL], x[NPL], dm[NPL];
+        load_vec(z, DZ + t * M, M);
+        load_vec(x, in.msg[a] + o * M, M);
+        const float na = in.ln[a][o], s = warp_dot(z, x, M);
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) dm[i] = w[a] * na * z[i];
+        store_vec(in.dmsg[a] + o * M, dm, M);
+        if (lane == 0) {
+          part += na * s;
+          in.dln[a][o] += w[a] * s;
+        }
+      }
+      const float tot = block_sum(part, red);
+      if (threadIdx.x == 0)
+        atomicAdd(&scalE[((int64_t)u * E + in.edge[a]) * kNEdge + kE_W], (double)tot);
+    }
+    return;
+  }
   // dmsg_a = w_a dz ; d edge-weight_a = sum dz o msg_a
   const int m4 = M >> 2;
   const int64_t r0 = row(u, T, t0) * M;

@@ -105,6 +105,11 @@ GPA_DEV float block_sum(float x, float* red) {
 }
 
 // softmax over the incoming edges' logits for head h
+// The product reader's gain e^{clamp(g, -4, 4)} and whether g lies inside the clamp
+// (src/gpa/attention.py:234)
+GPA_DEV float product_gain(float g) { return __expf(fminf(fmaxf(g, -4.f), 4.f)); }
+GPA_DEV float product_gain_live(float g) { return g >= -4.f && g <= 4.f ? 1.f : 0.f; }
+
 GPA_DEV void edge_weights(const BridgeIn& in, const float* edge_logits, int H, int h,
                           float* w) {
   float mx = -INFINITY;

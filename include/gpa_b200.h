@@ -48,7 +48,15 @@ typedef struct GpaDims {
   int32_t input_dtype;     /* GPA_B200_F32 / _BF16 / _F16 */
   int32_t positional_none; /* positional_mode == "none": zero decays */
   float read_scale, query_scale, beta_max;
+  int32_t reader_mode;     /* dense reader: GPA_B200_READER_TANH (centred tanh,
+                              src/gpa/attention.py:238-241), _PRODUCT
+                              (paper_product_read, :231-234) or _MARGINAL
+                              (product and relation_marginal, :235-236) */
 } GpaDims;
+
+#define GPA_B200_READER_TANH 0
+#define GPA_B200_READER_PRODUCT 1
+#define GPA_B200_READER_MARGINAL 2
 
 /* Parameter pointers (per-level lists by level, edges in the reference order
  * (i, j) for i != j, row-major).  The learned prefixes are not listed: they
@@ -193,7 +201,7 @@ int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, 
 /* Message of the last failure on the calling thread (0 if none). */
 int gpa_b200_last_error(char* buf, size_t len);
 
-/* ABI version of this header. */
+/* ABI version of this header: 2 (GpaDims.reader_mode added). */
 int gpa_b200_abi_version(void);
 
 /* Kernel accounting (no counterpart in the reference, which has no native

@@ -66,7 +66,9 @@ def oracle_config(model: DenseGPA) -> oracle.OracleConfig:
                                positional_mode=c.positional_mode, query_scale=c.query_scale,
                                beta_init=c.beta_init, beta_max=c.beta_max,
                                decay_init=c.decay_init, relation_beta_init=c.relation_beta_init,
-                               relation_decay_init=c.relation_decay_init, read_scale=c.read_scale)
+                               relation_decay_init=c.relation_decay_init, read_scale=c.read_scale,
+                               paper_product_read=c.paper_product_read,
+                               relation_marginal=c.relation_marginal)
 
 
 def run_pair(model: DenseGPA, q, k, v, *, oracle_dtype=torch.float64, state_weights=True,

@@ -57,6 +57,14 @@ FP32_CASES = {
                           chunk_size=1), 2, 16),
     "c2head_T200": (dict(heads=2, key_dim=128, value_dim=128, slots=(64, 64, 64, 128),
                          chunk_size=64), 1, 200),
+    # the product reader (paper_product_read) and its marginal count term
+    "product_chunk4": (dict(heads=2, key_dim=8, value_dim=6, slots=(4, 8, 6), chunk_size=4,
+                            paper_product_read=True), 2, 13),
+    "marginal_token": (dict(heads=2, key_dim=4, value_dim=3, slots=(3, 2, 4), chunk_size=1,
+                            paper_product_read=True, relation_marginal=True), 2, 7),
+    "marginal_chunk64_T130": (dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
+                                   chunk_size=64, paper_product_read=True,
+                                   relation_marginal=True), 1, 130),
 }
 
 
@@ -92,6 +100,10 @@ BF16_CASES = {
     # on them across seeds at these sizes, hence the alternative criterion below.
     "odd_widths_T200": (dict(heads=2, key_dim=48, value_dim=80, slots=(16, 48, 112),
                              chunk_size=64), 2, 200),
+    # the product reader with the marginal count term at the benched head shape
+    "marginal_c2head_T200": (dict(heads=2, key_dim=128, value_dim=128, slots=(64, 64, 64, 128),
+                                  chunk_size=64, paper_product_read=True,
+                                  relation_marginal=True), 1, 200),
 }
 
 

@@ -26,8 +26,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def test_config_accepts_default_flags_and_rejects_unimplemented_operators():
     GPAConfig(heads=16, key_dim=128, value_dim=128, slots=(64, 64, 64, 128), chunk_size=64)
     GPAConfig(positional_mode="none", chunk_size=1)
+    GPAConfig(paper_product_read=True)
+    GPAConfig(paper_product_read=True, relation_marginal=True)
     for bad in (dict(positional_mode="moments"), dict(rsa_update=True),
-                dict(paper_product_read=True), dict(control_dim=4), dict(slot_feature="tanh"),
+                dict(relation_marginal=True), dict(control_dim=4), dict(slot_feature="tanh"),
                 dict(balanced_bridge=True), dict(quadratic_features=True),
                 dict(learn_read_scale=True), dict(shared_query_center=True),
                 dict(chunk_size=65), dict(slots=(256,)), dict(key_dim=130), dict(slots=(4,) * 9),
@@ -118,6 +120,9 @@ def test_workspace_queries_and_argument_errors():
     assert lib.gpa_b200_last_error(buf, 256) == 1 and b"params" in buf.value
     with pytest.raises(ValueError, match="params"):
         _lib.check(rc, "gpa_b200_forward")
+    d.reader_mode = 3  # beyond GPA_B200_READER_MARGINAL
+    rc = lib.gpa_b200_forward(d, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == 1 and lib.gpa_b200_last_error(buf, 256) == 1 and b"reader_mode" in buf.value
 
 
 def test_bench_layer_workspaces_fit_one_b200():
