@@ -801,6 +801,9 @@ def main():
                     help="weak: B=8 per rank, data parallel; strong: global B=8 x 16 heads "
                          "split by heads over the ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="train workload on one GPU: skip the decode leg (one-token steps of the "
+                         "same layer at B=1/64/256, reported under \"decode\")")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="per-rank batch (default 8); smaller values are for profiling")
     ap.add_argument("--length", type=int, default=LENGTH,
@@ -834,6 +837,13 @@ def main():
         return
     res = run_b200(args, rank, world, local)
     if rank == 0:
+        if world == 1 and not args.no_decode and (BATCH, LENGTH) == (8, 8192):
+            # the decode workload of the same layer, timed after the training
+            # step: CUDA-graph replays of the one-kernel step at each batch size
+            torch.cuda.empty_cache()
+            dec = run_decode(args)
+            res["decode"] = {k: dec[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
+                                                 "gpu_launches", "roofline", "by_batch", "config")}
         if not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(os.cpu_count() or 1)
         print(json.dumps(res), flush=True)

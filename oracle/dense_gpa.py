@@ -7,7 +7,7 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 
 It restates the reference's ``backend="torch"`` algorithm (package
 ``gpa-attention`` v0.4.0) for the default flag set the b200 backend accepts:
-``positional_mode`` in {"gated", "none"}, linear slot features, no RSA update,
+``positional_mode`` in {"gated", "none", "moments"}, linear slot features, no RSA update,
 no control input, no quadratic features, no balanced bridge, fixed read scale;
 the reader in its centred-tanh form or the product form (``paper_product_read``,
 optionally ``relation_marginal``).  Every function cites the reference lines it follows
@@ -58,7 +58,8 @@ class OracleConfig:
 class OracleState:
     """Mirror of ``GPAState`` (src/gpa/state.py:30-58) with plain tuples.
 
-    levels: tuple of (inner A [B,H,D,M], outer B [B,H,M,Dv], count [B,H,M])
+    levels: tuple of (inner A [B,H,D,M], outer B [B,H,M,Dv], count [B,H,M][, moments
+            P [B,H,D,M] when positional_mode is "moments"])
     relations: tuple of R [B,H,M_i,M_j] in edge order
     frozen: tuple of (A, B) snapshots or None
     """
@@ -72,10 +73,11 @@ class OracleState:
 
 def tensors_of(state: OracleState):
     """Flatten in the reference's ``tensors()`` order (src/gpa/state.py:16-24):
-    per level inner, outer, count; per relation memory; per frozen level inner, outer."""
+    per level inner, outer, count[, moments]; per relation memory; per frozen level inner,
+    outer."""
     out = []
-    for a, b, n in state.levels:
-        out += [a, b, n]
+    for lv in state.levels:
+        out += list(lv)
     out += list(state.relations)
     if state.frozen is not None:
         for a, b in state.frozen:
@@ -160,7 +162,10 @@ def initial_state(cfg: OracleConfig, p: dict, batch: int, dtype: torch.dtype) ->
         a = p[f"inner_prefix.{j}"].to(work).unsqueeze(0).expand(batch, -1, -1, -1)
         b = p[f"outer_prefix.{j}"].to(work).unsqueeze(0).expand(batch, -1, -1, -1)
         n = torch.zeros(batch, cfg.heads, m, dtype=work)
-        levels.append((a, b, n))
+        if cfg.positional_mode == "moments":
+            levels.append((a, b, n, torch.zeros(batch, cfg.heads, cfg.key_dim, m, dtype=work)))
+        else:
+            levels.append((a, b, n))
     rel = tuple(p[f"relation_prefix.{e}"].to(work).unsqueeze(0).expand(batch, -1, -1, -1)
                 for e in range(len(edges_of(len(cfg.slots)))))
     return OracleState(tuple(levels), rel, 0, cfg.chunk_size, 0, None)
@@ -195,6 +200,31 @@ def gdn_scan(q, k, v, g, beta, state):
     return torch.stack(ys, 1), state
 
 
+def rope(x, positions):
+    """Adjacent-pair rotary embedding, base 10000 (src/gpa/ops.py:117-132): pair i of the last
+    dimension turns by positions * 10000^(-2i/D); x [B,T,H,D] with positions [T], or [B,H,D] with
+    one position."""
+    d = x.shape[-1]
+    work = x.to(_work_dtype(x))
+    pos = torch.as_tensor(positions, dtype=work.dtype)
+    if x.ndim == 4:
+        pos = pos[None, :, None]
+    freq = 10000. ** (-torch.arange(0, d, 2, dtype=work.dtype) / d)
+    ang = pos[..., None] * freq
+    ev, od = work[..., 0::2], work[..., 1::2]
+    return torch.stack((ev * ang.cos() - od * ang.sin(), ev * ang.sin() + od * ang.cos()),
+                       -1).flatten(-2).to(x.dtype)
+
+
+def linear_scan(q, k, v, state):
+    """Additive moments S += k v^T, read q^T S after each update (src/gpa/ops.py:86-114)."""
+    outs = []
+    for t in range(q.shape[1]):
+        state = state + k[:, t].to(state.dtype)[..., :, None] * v[:, t].to(state.dtype)[..., None, :]
+        outs.append(torch.einsum("bhd,bhdm->bhm", q[:, t].to(state.dtype), state).to(q.dtype))
+    return torch.stack(outs, 1), state
+
+
 # --------------------------------------------------------------------------
 # Level pieces (src/gpa/attention.py:161-262)
 # --------------------------------------------------------------------------
@@ -224,10 +254,14 @@ def _residual(p, j, key, value, rk, rv):
             (value - eta[:, 1, None] * rv.to(value.dtype)).to(value.dtype))
 
 
-def _base_logits(cfg, p, j, raw, count):
-    """read_scale * raw + softplus(c) log1p(n) (src/gpa/attention.py:196-204, no moments)."""
+def _base_logits(cfg, p, j, raw, count, moment=None):
+    """read_scale * raw + softplus(c) log1p(n), plus g_m tanh(moment / (1 + n)) with positional
+    moments (src/gpa/attention.py:196-204)."""
     gain = _softplus(p["count_gain_raw"][j])[..., None]
-    return cfg.read_scale * raw.to(count.dtype) + gain * count.log1p()
+    logits = cfg.read_scale * raw.to(count.dtype) + gain * count.log1p()
+    if moment is not None:
+        logits = logits + p["moment_gain"][j][..., None] * torch.tanh(moment / (1 + count))
+    return logits
 
 
 def _relations(cfg, p, edges, local, writes, rel_states):
@@ -284,27 +318,39 @@ def _bridge(cfg, p, edges, q, logits, messages, counts):
 
 
 def _token(cfg, p, edges, q, k, v, state):
-    """Exact recurrence for one token, post-update writes (src/gpa/attention.py:264-297)."""
+    """Exact recurrence for one token, post-update writes (src/gpa/attention.py:264-297); with
+    positional moments the query is rotated (RoPE at the cache position) and each level adds
+    the moment read to its base logits."""
+    moments = cfg.positional_mode == "moments"
+    pos = state.position
+    qr = rope(q, pos) if moments else q
     key, value = k, v
     levels, writes, logits = [], [], []
-    for j, (a_old, b_old, n_old) in enumerate(state.levels):
+    for j, old in enumerate(state.levels):
+        a_old, b_old, n_old = old[:3]
         slot = _slot(p, j, key)
         gi, bi, go, bo = _gates(cfg, p, j, key)
         a = gdn_step(a_old, key, slot, gi, bi)
         b = gdn_step(b_old, slot, value, go, bo)
         write = read(key, a).softmax(-1)
         count = n_old + write.to(n_old.dtype)
-        raw = read(q, a)
-        logits.append(_base_logits(cfg, p, j, raw, count))
+        corr = None
+        if moments:
+            kh = unit(key)
+            delta = (rope(kh, pos) - kh).to(old[3].dtype)
+            mom = old[3] + delta[..., :, None] * write.to(delta.dtype)[..., None, :]
+            corr = read(qr, mom)
+        raw = read(qr, a)
+        logits.append(_base_logits(cfg, p, j, raw, count, corr))
         writes.append(write)
-        levels.append((a, b, count))
+        levels.append((a, b, count, mom) if moments else (a, b, count))
         rk = torch.einsum("bhdm,bhm->bhd", a, write.to(a.dtype))
         rv = torch.einsum("bhm,bhmv->bhv", write.to(b.dtype), b)
         key, value = _residual(p, j, key, value, rk, rv)
     local = [x.softmax(-1).to(q.dtype).unsqueeze(1) for x in logits]
     messages, rel = _relations(cfg, p, edges, local, [x.unsqueeze(1) for x in writes], state.relations)
     messages = [[(e, m[:, 0]) for e, m in group] for group in messages]
-    routes, qouts = _bridge(cfg, p, edges, q, logits, messages, [lv[2] for lv in levels])
+    routes, qouts = _bridge(cfg, p, edges, qr, logits, messages, [lv[2] for lv in levels])
     weights = p["output_logits"].softmax(0)
     out = sum(weights[j][..., None] * read(qo, levels[j][1]) for j, qo in enumerate(qouts))
     new = OracleState(tuple(levels), rel, state.position + 1, cfg.chunk_size, 0, None)
@@ -312,33 +358,45 @@ def _token(cfg, p, edges, q, k, v, state):
 
 
 def _block(cfg, p, edges, q, k, v, state):
-    """One lag block with frozen residual snapshots (src/gpa/attention.py:299-345)."""
-    frozen = state.frozen or tuple((a, b) for a, b, _ in state.levels)
+    """One lag block with frozen residual snapshots (src/gpa/attention.py:299-345); with
+    positional moments the queries are rotated (RoPE at their positions) and each level adds
+    the linear-scan moment read to its base logits."""
+    moments = cfg.positional_mode == "moments"
+    positions = torch.arange(state.position, state.position + q.shape[1])
+    qr = rope(q, positions) if moments else q
+    frozen = state.frozen or tuple((lv[0], lv[1]) for lv in state.levels)
     key, value = k, v
     finals, writes, logits, outer_in, history = [], [], [], [], []
-    for j, ((a_old, _b_old, n_old), (fa, fb)) in enumerate(zip(state.levels, frozen)):
+    for j, (old, (fa, fb)) in enumerate(zip(state.levels, frozen)):
+        a_old, n_old = old[0], old[2]
         slot = _slot(p, j, key)
         gi, bi, go, bo = _gates(cfg, p, j, key)
-        raw, a = gdn_scan(q, key, slot, gi, bi, a_old)
+        raw, a = gdn_scan(qr, key, slot, gi, bi, a_old)
         write = torch.einsum("bthd,bhdm->bthm", unit(key).to(fa.dtype), fa).softmax(-1)
         write = write.to(q.dtype)
         counts = n_old[:, None] + write.to(n_old.dtype).cumsum(1)
         history.append(counts)
-        logits.append(_base_logits(cfg, p, j, raw, counts))
+        corr, mom = None, None
+        if moments:
+            kh = unit(key)
+            delta = rope(kh, positions) - kh
+            corr, mom = linear_scan(unit(qr), delta, write, old[3])
+        logits.append(_base_logits(cfg, p, j, raw, counts, corr))
         writes.append(write)
-        finals.append((a, counts[:, -1]))
+        finals.append((a, counts[:, -1], mom))
         outer_in.append((slot, value, go, bo))
         rk = torch.einsum("bhdm,bthm->bthd", fa, write.to(fa.dtype))
         rv = torch.einsum("bthm,bhmv->bthv", write.to(fb.dtype), fb)
         key, value = _residual(p, j, key, value, rk, rv)
     local = [x.softmax(-1).to(q.dtype) for x in logits]
     messages, rel = _relations(cfg, p, edges, local, writes, state.relations)
-    routes, qouts = _bridge(cfg, p, edges, q, logits, messages, history)
+    routes, qouts = _bridge(cfg, p, edges, qr, logits, messages, history)
     outs, levels = [], []
     for j, qo in enumerate(qouts):
         slot, vl, go, bo = outer_in[j]
         y, b = gdn_scan(qo, slot, vl, go, bo, state.levels[j][1])
-        levels.append((finals[j][0], b, finals[j][1]))
+        a_f, n_f, mom = finals[j]
+        levels.append((a_f, b, n_f, mom) if moments else (a_f, b, n_f))
         outs.append(y)
     weights = p["output_logits"].softmax(0)
     out = sum(weights[j][..., None] * y for j, y in enumerate(outs))

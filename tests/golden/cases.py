@@ -75,6 +75,20 @@ CASES = {
                                       relation_marginal=True),
                              batch=1, length=130, dtype="float32", seed=33, prefix_std=.02,
                              partitions=((0, 47), (47, 65), (65, 130)), decode=1),
+    # positional moments (src/gpa/attention.py:277-283, 318-322; src/gpa/ops.py:86-132): rotated
+    # queries and the per-level additive moment state read into the base logits
+    "moments_f64": dict(cfg=dict(heads=2, key_dim=8, value_dim=6, slots=(4, 8, 6), chunk_size=4,
+                                 positional_mode="moments"),
+                        batch=2, length=13, dtype="float64", seed=41,
+                        partitions=((0, 5), (5, 6), (6, 13)), decode=2),
+    "moments_token_f64": dict(cfg=dict(heads=2, key_dim=4, value_dim=3, slots=(3, 2, 4),
+                                       chunk_size=1, positional_mode="moments"),
+                              batch=2, length=7, dtype="float64", seed=42,
+                              partitions=((0, 3), (3, 7)), decode=1),
+    "moments_c64_f32": dict(cfg=dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
+                                     chunk_size=64, positional_mode="moments"),
+                            batch=1, length=130, dtype="float32", seed=43, prefix_std=.02,
+                            partitions=((0, 47), (47, 65), (65, 130)), decode=1),
 }
 
 DTYPES = {"float32": torch.float32, "float64": torch.float64, "bfloat16": torch.bfloat16}
