@@ -25,13 +25,15 @@ class GpaDims(ctypes.Structure):
                 ("slots", c_int32 * MAX_LEVELS), ("chunk_size", c_int32),
                 ("chunk_offset", c_int32), ("input_dtype", c_int32),
                 ("positional_none", c_int32), ("read_scale", c_float),
-                ("query_scale", c_float), ("beta_max", c_float), ("reader_mode", c_int32)]
+                ("query_scale", c_float), ("beta_max", c_float), ("reader_mode", c_int32),
+                ("positional_moments", c_int32), ("position", c_int32)]
 
 
 _LEVEL_PARAMS = ("center", "route_weight", "query_weight", "route_up", "route_down",
                  "gate_weight", "gate_bias")
 _SCALAR_PARAMS = ("residual_raw", "count_gain_raw", "route_mlp_gain", "output_logits",
-                  "edge_logits", "relation_gain", "relation_decay_raw", "relation_beta_raw")
+                  "edge_logits", "relation_gain", "relation_decay_raw", "relation_beta_raw",
+                  "moment_gain")
 
 
 class GpaParams(ctypes.Structure):
@@ -46,7 +48,8 @@ class GpaParamGrads(ctypes.Structure):
 class GpaStateRef(ctypes.Structure):
     _fields_ = [("inner", c_void_p * MAX_LEVELS), ("outer", c_void_p * MAX_LEVELS),
                 ("count", c_void_p * MAX_LEVELS), ("relation", c_void_p * MAX_EDGES),
-                ("frozen_inner", c_void_p * MAX_LEVELS), ("frozen_outer", c_void_p * MAX_LEVELS)]
+                ("frozen_inner", c_void_p * MAX_LEVELS), ("frozen_outer", c_void_p * MAX_LEVELS),
+                ("moment", c_void_p * MAX_LEVELS)]
 
 
 EXPORTS = ("gpa_b200_saved_bytes", "gpa_b200_scratch_bytes", "gpa_b200_forward",

@@ -20,7 +20,7 @@ class GPAConfig:
     key_dim: int = 32
     value_dim: int = 32
     slots: tuple[int, ...] = (16, 16, 16, 16)
-    positional_mode: str = "gated"  # gated | none (moments is not implemented on b200)
+    positional_mode: str = "gated"  # gated | moments | none
     query_scale: float = 1 / 16
     beta_init: float = .1
     beta_max: float = .9
@@ -74,7 +74,6 @@ class GPAConfig:
             raise ValueError("shared query-center parameterization needs query_scale > 0")
         # b200 operator coverage
         unsupported = [name for name, on in (
-            ("positional_mode='moments'", self.positional_mode == "moments"),
             ("rsa_update", self.rsa_update),
             ("control_dim", self.control_dim != 0),
             ("slot_feature!='linear'", self.slot_feature != "linear"),

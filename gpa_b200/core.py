@@ -46,8 +46,10 @@ class _Plan:
         self.new_offset = (state.chunk_offset + self.T) % cfg.chunk_size
         self.fz_in = state.frozen is not None and self.offset != 0
         self.fz_out = self.new_offset != 0
-        self.n_params = 7 * self.L + 8
-        self.n_state_in = 3 * self.L + self.E + (2 * self.L if self.fz_in else 0)
+        self.moments = cfg.positional_mode == "moments"
+        self.n_params = 7 * self.L + len(_SCALAR_NAMES)
+        self.n_mom = self.L if self.moments else 0  # moment states, after the relations
+        self.n_state_in = 3 * self.L + self.E + self.n_mom + (2 * self.L if self.fz_in else 0)
         d = _lib.GpaDims()
         d.batch, d.length, d.heads = self.B, self.T, self.H
         d.key_dim, d.value_dim, d.levels = self.D, self.Dv, self.L
@@ -58,10 +60,12 @@ class _Plan:
         d.positional_none = int(cfg.positional_mode == "none")
         d.read_scale, d.query_scale, d.beta_max = cfg.read_scale, cfg.query_scale, cfg.beta_max
         d.reader_mode = (2 if cfg.relation_marginal else 1) if cfg.paper_product_read else 0
+        d.positional_moments = int(self.moments)
+        d.position = state.position
         self.dims = d
 
     def state_ref(self, flat, with_frozen: bool) -> _lib.GpaStateRef:
-        """GpaStateRef over [A,B,n]*L + R*E (+ [fA, fB]*L)."""
+        """GpaStateRef over [A,B,n]*L + R*E (+ P*L with moments) (+ [fA, fB]*L)."""
         s = _lib.GpaStateRef()
         L, E = self.L, self.E
         for j in range(L):
@@ -70,8 +74,10 @@ class _Plan:
             s.count[j] = _lib.ptr(flat[3 * j + 2])
         for e in range(E):
             s.relation[e] = _lib.ptr(flat[3 * L + e])
+        for j in range(self.n_mom):
+            s.moment[j] = _lib.ptr(flat[3 * L + E + j])
         if with_frozen:
-            base = 3 * L + E
+            base = 3 * L + E + self.n_mom
             for j in range(L):
                 s.frozen_inner[j] = _lib.ptr(flat[base + 2 * j])
                 s.frozen_outer[j] = _lib.ptr(flat[base + 2 * j + 1])
@@ -95,6 +101,8 @@ class _Plan:
             shapes += [(B, H, D, m), (B, H, m, Dv), (B, H, m)]
         for i, j in edges_of(self.L):
             shapes.append((B, H, self.cfg.slots[i], self.cfg.slots[j]))
+        for m in self.cfg.slots[:self.n_mom]:
+            shapes.append((B, H, D, m))
         if with_frozen:
             for m in self.cfg.slots:
                 shapes += [(B, H, D, m), (B, H, m, Dv)]
@@ -152,7 +160,7 @@ class _DenseGPACore(torch.autograd.Function):
         dout = dout.contiguous().to(ctx.in_dtype)
         dstate = [None if g is None else g.contiguous().float() for g in dstate]
         if plan.fz_out:  # frozen-snapshot gradients are consumed in (inner, outer) pairs
-            base = 3 * plan.L + plan.E
+            base = 3 * plan.L + plan.E + plan.n_mom
             shapes = plan.state_shapes(True)
             for i in range(base, len(dstate)):
                 if dstate[i] is None:
@@ -177,6 +185,8 @@ class _DenseGPACore(torch.autograd.Function):
         del scratch
         ctx.saved_ws = None
         dparams = [g.to(p.dtype) for g, p in zip(dparams, params)]
+        if not plan.moments:  # moment_gain is unused without positional moments
+            dparams[-1] = None
         return (None, dq, dk, dv, *dparams, *dstate_in)
 
 
@@ -235,8 +245,12 @@ class DenseGPA(nn.Module):
         dtype = ref.dtype if dtype is None else dtype
         work = torch.float64 if dtype == torch.float64 else torch.float32
         expand = lambda p: p.to(device=device, dtype=work).unsqueeze(0).expand(batch, *p.shape)
+        moments = self.config.positional_mode == "moments"
+        h, d = self.config.heads, self.config.key_dim
         levels = tuple(LevelState(expand(a), expand(b),
-                                  torch.zeros(batch, self.config.heads, m, device=device, dtype=work))
+                                  torch.zeros(batch, h, m, device=device, dtype=work),
+                                  torch.zeros(batch, h, d, m, device=device, dtype=work)
+                                  if moments else None)
                        for m, a, b in zip(self.config.slots, self.inner_prefix, self.outer_prefix))
         relations = tuple(RelationState(i, j, expand(p))
                           for (i, j), p in zip(self.edges, self.relation_prefix))
@@ -275,10 +289,16 @@ class DenseGPA(nn.Module):
             raise ValueError("cannot switch cache between recurrent and lagged chunk semantics")
         if len(state.levels) != len(cfg.slots) or tuple((s.source, s.target) for s in state.relations) != self.edges:
             raise ValueError("cache topology does not match this model")
+        default_ids = position_ids is None
         if position_ids is None:
             position_ids = torch.arange(state.position, state.position + q.shape[1], device=q.device)
         if position_ids.shape not in ((q.shape[1],), (q.shape[0], q.shape[1])):
             raise ValueError("position_ids must be [T] or [B,T]")
+        if cfg.positional_mode == "moments" and not default_ids and not torch.equal(
+                position_ids.to(torch.long).expand(q.shape[0], -1).cpu(),
+                torch.arange(state.position, state.position + q.shape[1]).expand(q.shape[0], -1)):
+            raise ValueError("positional moments on the b200 backend rotate by the cache position; "
+                             "custom position_ids are not implemented")
         if q.shape[1] == 0:
             output = v.new_empty(v.shape)
             if return_diagnostics:
@@ -291,6 +311,10 @@ class DenseGPA(nn.Module):
         for lv in state.levels:
             flat_state += [lv.inner, lv.outer, lv.count]
         flat_state += [r.memory for r in state.relations]
+        if plan.moments:
+            if any(lv.position is None for lv in state.levels):
+                raise ValueError("positional moments need the moment states of the cache")
+            flat_state += [lv.position for lv in state.levels]
         if plan.fz_in:
             for snap in state.frozen:
                 flat_state += [snap.inner, snap.outer]
@@ -299,11 +323,12 @@ class DenseGPA(nn.Module):
         outs = _DenseGPACore.apply(plan, q, k, v, *self._flat_params(), *flat_state)
         output, st, saved = outs[0], outs[1:-1], outs[-1]
         L = plan.L
-        levels = tuple(LevelState(st[3 * j], st[3 * j + 1], st[3 * j + 2]) for j in range(L))
+        moms = [st[3 * L + plan.E + j] if plan.moments else None for j in range(L)]
+        levels = tuple(LevelState(st[3 * j], st[3 * j + 1], st[3 * j + 2], moms[j]) for j in range(L))
         relations = tuple(RelationState(i, j, st[3 * L + e]) for e, (i, j) in enumerate(self.edges))
         frozen = None
         if plan.fz_out:
-            base = 3 * L + plan.E
+            base = 3 * L + plan.E + plan.n_mom
             frozen = tuple(ResidualSnapshot(st[base + 2 * j], st[base + 2 * j + 1]) for j in range(L))
         new = GPAState(levels, relations, state.position + q.shape[1], cfg.chunk_size,
                        plan.new_offset, frozen)

@@ -68,6 +68,8 @@ int fail(int code, const std::string& msg) {
 struct Geo {
   int B, T, H, D, Dv, L, E, C, offset, post, dt, pos_none, U;
   int reader;  // GPA_B200_READER_*
+  int moments;     // positional moments
+  int64_t pos0;    // absolute position of the call's first token
   int M[kMaxLevels];
   int es[kMaxEdges], ed[kMaxEdges];
   float rs, qs, bm;
@@ -102,6 +104,12 @@ int make_geo(const GpaDims* d, Geo* g, std::string* why) {
   g->qs = d->query_scale;
   g->bm = d->beta_max;
   g->reader = d->reader_mode;
+  g->moments = d->positional_moments != 0;
+  g->pos0 = d->position;
+  if (g->moments && (d->key_dim % 2 || d->position < 0)) {
+    *why = "positional moments need an even key_dim and a non-negative position";
+    return GPA_B200_BAD_ARGUMENT;
+  }
   if (g->reader < GPA_B200_READER_TANH || g->reader > GPA_B200_READER_MARGINAL) {
     *why = "reader_mode must be GPA_B200_READER_TANH, _PRODUCT or _MARGINAL";
     return GPA_B200_BAD_ARGUMENT;
@@ -191,6 +199,9 @@ struct Saved {
   // again from K and the gates, exactly as the forward did)
   float *TA[kMaxLevels], *TB[kMaxLevels];
   float *TR[kMaxEdges];
+  // positional moments: the state at every block start and the end [U, nb+1, D, M], and the
+  // moment reads corr [U,T,M] of every level
+  float *Pb[kMaxLevels], *corr[kMaxLevels];
   size_t bytes;
 };
 
@@ -256,6 +267,10 @@ void layout_saved(const Geo& g, void* base, Saved* s) {
     s->TA[j] = g.fast ? b.take(nAT) : nullptr;
     s->TB[j] = g.fast ? b.take(nAT) : nullptr;
   }
+  for (int j = 0; j < g.L; ++j) {
+    s->Pb[j] = g.moments ? b.take((size_t)g.U * nb1 * g.D * g.M[j]) : nullptr;
+    s->corr[j] = g.moments ? b.take(UT * g.M[j]) : nullptr;
+  }
   for (int e = 0; e < g.E; ++e) {
     s->TR[e] = g.fast ? b.take(nAT) : nullptr;
   }
@@ -270,6 +285,7 @@ struct Scratch {
   float *dlogits[kMaxLevels], *dlh[kMaxLevels], *dwh[kMaxLevels], *dwrite[kMaxLevels];
   float *odK[kMaxLevels], *odW[kMaxLevels], *odG[kMaxLevels];
   float* dln[kMaxLevels];  // gradient of |softmax(logits_j)| per row (product reader)
+  float *Gend, *dcorr, *dmk;  // positional moments: G at block ends, dcorr, unit-key gradient
   float* dmsg[kMaxEdges];
   float *draw, *dn, *dnsum, *extA, *extB, *dnk, *dslot, *dns, *dgates, *d4;
   float *dfzA, *dfzB;
@@ -307,6 +323,9 @@ void layout_scratch(const Geo& g, void* base, Scratch* s) {
     s->dln[j] = b.take(UT);
   }
   for (int e = 0; e < g.E; ++e) s->dmsg[e] = b.take(UT * g.M[g.ed[e]]);
+  s->Gend = g.moments ? b.take((size_t)g.U * g.bl.nb * g.D * Mx) : nullptr;
+  s->dcorr = g.moments ? b.take(UT * Mx) : nullptr;
+  s->dmk = g.moments ? b.take(UT * g.D) : nullptr;
   s->draw = b.take(UT * Mx);
   s->dn = b.take(UT * Mx);
   s->dnsum = b.take((size_t)g.U * nb * Mx);
@@ -372,6 +391,8 @@ int check_params(const Geo& g, const GpaParams* p) {
     return fail(GPA_B200_BAD_ARGUMENT, "missing level scalar parameter pointer");
   if (g.E && (!p->edge_logits || !p->relation_decay_raw || !p->relation_beta_raw))
     return fail(GPA_B200_BAD_ARGUMENT, "missing edge parameter pointer");
+  if (g.moments && !p->moment_gain)
+    return fail(GPA_B200_BAD_ARGUMENT, "positional moments need moment_gain");
   return GPA_B200_OK;
 }
 
@@ -382,6 +403,8 @@ int check_state(const Geo& g, const GpaStateRef* s, bool need_frozen, const char
       return fail(GPA_B200_BAD_ARGUMENT, std::string(what) + ": missing level tensor");
     if (need_frozen && (!s->frozen_inner[j] || !s->frozen_outer[j]))
       return fail(GPA_B200_BAD_ARGUMENT, std::string(what) + ": missing frozen snapshot");
+    if (g.moments && !s->moment[j])
+      return fail(GPA_B200_BAD_ARGUMENT, std::string(what) + ": missing moment state");
   }
   for (int e = 0; e < g.E; ++e)
     if (!s->relation[e]) return fail(GPA_B200_BAD_ARGUMENT, std::string(what) + ": missing relation");
@@ -399,7 +422,8 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
   const int U = g.U, T = g.T, D = g.D, Dv = g.Dv;
   const Blocks& bl = g.bl;
   const bool fz_in = g.offset != 0;
-  CK(launch_input(q, k, v, g.dt, g.B, T, g.H, D, Dv, s.qf, s.qh, s.qn, s.key[0], s.val[0], st));
+  CK(launch_input(q, k, v, g.dt, g.B, T, g.H, D, Dv, s.qf, s.qh, s.qn, s.key[0], s.val[0],
+                  g.moments ? g.pos0 : -1, st));
   for (int j = 0; j < g.L; ++j) {
     const int M = g.M[j];
     CK((g.fast ? tc_level_prep : launch_level_prep)(U, T, g.H, D, M, s.key[j], p->center[j], p->gate_weight[j],
@@ -451,9 +475,12 @@ int forward_impl(const Geo& g, const GpaParams* p, const void* q, const void* k,
                          fz_in ? si->frozen_outer[j] : nullptr, p->residual_raw, j, s.write[j],
                          s.bsum[j], with_res ? s.key[j + 1] : nullptr,
                          with_res ? s.val[j + 1] : nullptr, st));
+    if (g.moments)
+      CK(launch_moments_fwd(U, bl, D, M, g.pos0, s.qh, s.nk[j], s.write[j], si->moment[j],
+                            s.Pb[j], s.corr[j], so->moment[j], st));
     CK(launch_counts(U, bl, g.H, M, g.rs, p->count_gain_raw, j, si->count[j], s.bsum[j],
                      s.write[j], s.raw[j], s.counts[j], s.logits[j], s.lh[j], s.ln[j], s.wh[j],
-                     s.wn[j], so->count[j], st));
+                     s.wn[j], so->count[j], s.corr[j], p->moment_gain, st));
   }
   CK(launch_rel_gates(U, g.H, g.E, g.pos_none, p->relation_decay_raw, p->relation_beta_raw, s.ge,
                       s.be, st));
@@ -715,8 +742,12 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
                          ProductBwd{g.reader != GPA_B200_READER_TANH ? x.dln[j] : nullptr,
                                     p->relation_gain,
                                     g.reader == GPA_B200_READER_MARGINAL && has_incoming(g, j)},
-                         st));
+                         MomentBwd{s.corr[j], p->moment_gain, x.dcorr}, st));
     CK(launch_counts_bwd(U, bl, M, x.dn, x.dnsum, ds.count[j], x.dwrite[j], dsi->count[j], st));
+    if (g.moments)  // dq and dwrite now; the unit-key part joins dnk after the post backward
+      CK(launch_moments_bwd(U, bl, D, M, g.pos0, s.qh, s.nk[j], s.write[j], s.Pb[j], x.dcorr,
+                            ds.moment[j], x.Gend, dsi->moment[j], x.dqh, x.dwrite[j], x.dmk,
+                            st));
     const size_t szA = (size_t)D * M, szB = (size_t)M * Dv;
     CK(zero(x.extA, (size_t)U * (bl.nb + 1) * szA, st));
     CK(zero(x.extB, (size_t)U * (bl.nb + 1) * szB, st));
@@ -741,6 +772,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
                        fz_in ? si->frozen_outer[j] : nullptr, p->residual_raw, x.dkey, x.dval,
                        x.dwrite[j], x.dnk, x.extA, x.extB, fz_in ? dsi->frozen_inner[j] : nullptr,
                        fz_in ? dsi->frozen_outer[j] : nullptr, x.scal, st));
+    if (g.moments) CK(launch_add(x.dnk, x.dmk, (int64_t)UT * D, st));
     CK(zero(x.dslot, UT * M, st));
     CK(zero(x.dns, UT * M, st));
     CK(zero(x.dgates, UT * 4, st));
@@ -819,7 +851,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
     CK(launch_gate_grad(g.B, T, H, s.nk[j], D, x.d4, gp->gate_weight[j], gp->gate_bias[j], st));
   }
   CK(launch_input_bwd(g.B, T, H, D, Dv, g.dt, s.qh, s.qn, x.dqh, x.dq_direct, x.dkey, x.dval, dq,
-                      dk, dv, st));
+                      dk, dv, g.moments ? g.pos0 : -1, st));
   FoldArgs fa;
   std::memset(&fa, 0, sizeof(fa));
   fa.B = g.B;
@@ -847,6 +879,7 @@ int backward_impl(const Geo& g, const GpaParams* p, const GpaStateRef* si, const
   fa.g_edge_logits = gp->edge_logits;
   fa.g_relation_decay_raw = gp->relation_decay_raw;
   fa.g_relation_beta_raw = gp->relation_beta_raw;
+  fa.g_moment_gain = g.moments ? gp->moment_gain : nullptr;
   CK(launch_fold(fa, st));
   return GPA_B200_OK;
 }
@@ -928,6 +961,7 @@ int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, c
   a.dt = g.dt;
   a.pos_none = g.pos_none;
   a.reader = g.reader;
+  a.moments = g.moments;
   a.query_scale = g.qs;
   a.beta_max = g.bm;
   a.read_scale = g.rs;

@@ -31,6 +31,13 @@ constexpr int kStepThreads = 256;
 
 // ---------------------------------------------------------------- block helpers
 
+// x rounded to the input dtype (the reference rounds its rotated query back to it)
+GPA_DEV float round_in(float x, int dt) {
+  if (dt == GPA_B200_BF16) return __bfloat162float(__float2bfloat16(x));
+  if (dt == GPA_B200_F16) return __half2float(__float2half(x));
+  return x;
+}
+
 GPA_DEV float block_sum_all(float x, float* red) {
   x = warp_sum(x);
   __syncthreads();
@@ -216,12 +223,13 @@ struct HeadScalars {
   GPA_DEV int output_logit(int j) const { return 3 * E + 3 * L + j; }
   GPA_DEV int residual(int j, int c) const { return 3 * E + 4 * L + 2 * j + c; }
   GPA_DEV int gate_bias(int j, int c) const { return 3 * E + 6 * L + 4 * j + c; }
-  GPA_DEV int count() const { return 3 * E + 10 * L; }
+  GPA_DEV int moment_gain(int j) const { return 3 * E + 10 * L + j; }
+  GPA_DEV int count() const { return 3 * E + 11 * L; }
 };
 
 struct StepSmem {
   size_t Ss, q, qn, key, kn, val, tmp, tmp2, pre, yb, part, red, slot, write, logits, valin, qo,
-      gates, hs, bar, total;
+      gates, hs, mdel, mcor, bar, total;
   int msg_off[kMaxEdges];
   __host__ __device__ StepSmem(const StepArgs& a) {
     size_t off = 0;
@@ -263,7 +271,9 @@ struct StepSmem {
     qo = take(a.L * mx);
     gates = take(a.L * 4);
     for (int e = 0; e < a.E; ++e) msg_off[e] = (int)take(a.M[a.ed[e]]);
-    hs = take(3 * kMaxEdges + 10 * kMaxLevels);  // this head's scalars (HeadScalars)
+    hs = take(3 * kMaxEdges + 11 * kMaxLevels);  // this head's scalars (HeadScalars)
+    mdel = take(a.D);  // positional moments: delta of the level key, moment reads
+    mcor = take(mx);
     bar = take(4);  // the bulk loads' mbarrier (16-byte aligned)
     total = off * sizeof(float);
   }
@@ -304,9 +314,11 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
       else if (kind < 6) {
         const int q = r - 4 * L;  // residual_raw: 2 per level
         x = a.p.residual_raw[((q >> 1) * H + h) * 2 + (q & 1)];
-      } else {
+      } else if (kind < 10) {
         const int q = r - 6 * L;  // gate_bias: 4 per level
         x = a.p.gate_bias[q >> 2][h * 4 + (q & 3)];
+      } else {
+        x = a.moments ? a.p.moment_gain[j * H + h] : 0.f;
       }
     }
     hs[i] = x;
@@ -321,6 +333,17 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   }
   for (int i = threadIdx.x; i < Dv; i += blockDim.x) val[i] = load_in(a.v, (int64_t)u * Dv + i, a.dt);
   __syncthreads();
+  const int pos = a.offset[2];
+  if (a.moments) {  // rotated query at the cache position, rounded to the input dtype
+    for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {
+      const float e = q[2 * i], od = q[2 * i + 1];
+      float c, s;
+      rope_cs(pos, 2 * i, D, c, s);
+      q[2 * i] = round_in(e * c - od * s, a.dt);
+      q[2 * i + 1] = round_in(e * s + od * c, a.dt);
+    }
+    __syncthreads();
+  }
   unit_vec(qn, q, D, red);
 
   // ------------------------------------------------ level chain
@@ -380,13 +403,36 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
       rowdot(Ss, D, M, write, rk);
     }
     gdn_update(Ss, Ag, D, M, kn, slot, pre, gates[0], gates[1], qn, logits, part);  // logits <- raw
+    float* mcor = sm + Lm.mcor;
+    if (a.moments) {  // P += delta w^T (delta = rope(u(k)) - u(k)), corr = u(q)^T P
+      float* mdel = sm + Lm.mdel;
+      for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {
+        const float e = kn[2 * i], od = kn[2 * i + 1];
+        float c, s;
+        rope_cs(pos, 2 * i, D, c, s);
+        mdel[2 * i] = e * c - od * s - e;
+        mdel[2 * i + 1] = e * s + od * c - od;
+      }
+      float* Pg = a.s.moment[j] + u * szA;
+      load_mat(Ss, Pg, (int)szA, nullptr, bl);  // ends synchronized (mdel visible too)
+      for (int i = threadIdx.x; i < D * M; i += blockDim.x) {
+        const int d = i / M, m = i - d * M;
+        const float x = Ss[i] + mdel[d] * write[m];
+        Ss[i] = x;
+        Pg[i] = x;
+      }
+      __syncthreads();
+      colsum(Ss, D, M, qn, mcor, part);
+    }
     {  // counts and base logits
       const float cg = softplus(hs[hx.count_gain(j)]);
+      const float mg = hs[hx.moment_gain(j)];
       float* n = a.s.count[j] + (int64_t)u * M;
       for (int m = threadIdx.x; m < M; m += blockDim.x) {
         const float nn = n[m] + write[m];
         n[m] = nn;
         logits[m] = a.read_scale * logits[m] + cg * log1pf(nn);
+        if (a.moments) logits[m] += mg * tanhf(mcor[m] / (1.f + nn));
       }
     }
     // rv = write^T B_f
@@ -540,6 +586,7 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
     const unsigned done = atomicAdd(reinterpret_cast<unsigned*>(a.offset + 1), 1u);
     if (done == gridDim.x - 1) {
       a.offset[0] = (o + 1) % a.C;
+      a.offset[2] = pos + 1;
       a.offset[1] = 0;
       __threadfence();
     }

@@ -13,13 +13,14 @@ struct StepArgs {
   int es[kMaxEdges], ed[kMaxEdges];
   int dt, pos_none;
   int reader;  // GPA_B200_READER_* (dense reader form)
+  int moments;  // positional moments (rotated query, per-level moment state)
   float query_scale, beta_max, read_scale;
   GpaParams p;
   GpaStateRef s;  // updated in place; frozen_* required
   const void *q, *k, *v;
   void* out;
-  int* offset;  // device int[2]: the cache's chunk offset (advanced by the step) and the
-                // step's completion counter (0 between steps)
+  int* offset;  // device int[3]: the cache's chunk offset (advanced by the step), the step's
+                // completion counter (0 between steps) and the cache position (advanced)
 };
 
 // Shared memory the step kernel needs for these widths (bytes).

@@ -11,20 +11,38 @@ namespace {
 
 // ------------------------------------------------------------------ forward
 
-// one warp per (u, t): fp32 copies, unit-normalised q
+// x rounded to the input dtype (the reference rounds its rotated queries back to it)
+GPA_DEV float round_in(float x, int dt) {
+  if (dt == GPA_B200_BF16) return __bfloat162float(__float2bfloat16(x));
+  if (dt == GPA_B200_F16) return __half2float(__float2half(x));
+  return x;
+}
+
+// one warp per (u, t): fp32 copies, unit-normalised q; with rope_pos0 >= 0 the query is first
+// rotated (adjacent pairs, token t at rope_pos0 + t; src/gpa/ops.py:117-132)
 __global__ void k_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
-                        int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0) {
+                        int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0,
+                        int64_t rope_pos0) {
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int U = B * H;
   if (w >= U * T) return;
   const int u = w / T, t = w - u * T, b = u / H, h = u - b * H;
   const int64_t src = ((int64_t)b * T + t) * H + h;
   float ss = 0.f;
-  for (int d = lane; d < D; d += 32) {
-    const float x = load_in(q, src * D + d, dt);
-    qf[(int64_t)w * D + d] = x;
-    ss += x * x;
-    key0[(int64_t)w * D + d] = load_in(k, src * D + d, dt);
+  for (int i = 0; i < (D + 31) / 32; ++i) {  // warp-uniform trip count (pair shuffles)
+    const int d = lane + 32 * i;
+    float x = d < D ? load_in(q, src * D + d, dt) : 0.f;
+    if (rope_pos0 >= 0) {
+      const float other = __shfl_xor_sync(0xffffffffu, x, 1);
+      float c, s;
+      rope_cs(rope_pos0 + t, d, D, c, s);
+      x = round_in((d & 1) == 0 ? x * c - other * s : other * s + x * c, dt);
+    }
+    if (d < D) {
+      qf[(int64_t)w * D + d] = x;
+      ss += x * x;
+      key0[(int64_t)w * D + d] = load_in(k, src * D + d, dt);
+    }
   }
   const float nrm = sqrtf(warp_sum(ss));
   const float inv = 1.f / fmaxf(nrm, kUnitEps);
@@ -204,7 +222,8 @@ __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, 
                                                 const float* n0, const float* bsum,
                                                 const float* write, const float* raw,
                                                 float* counts, float* logits, float* lh,
-                                                float* ln, float* wh, float* wn, float* n_final) {
+                                                float* ln, float* wh, float* wn, float* n_final,
+                                                const float* corr, const float* moment_gain) {
   const int u = blockIdx.x / bl.nb, n = blockIdx.x % bl.nb, T = bl.T;
   const int t0 = bl.start(n), c = bl.end(n) - t0, h = u % H;
   const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -236,6 +255,13 @@ __global__ void __launch_bounds__(256) k_counts(int U, Blocks bl, int H, int M, 
     load_vec(w, Wt + t * M, M);
 #pragma unroll
     for (int i = 0; i < NPL; ++i) x[i] = read_scale * x[i] + gain * log1pf(cn[i]);
+    if (corr) {  // positional moments: + g_m tanh(corr / (1 + n)) (src/gpa/attention.py:202-203)
+      float cr[NPL];
+      load_vec(cr, corr + o * M, M);
+      const float mg = moment_gain[j * H + h];
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) x[i] += mg * tanhf(cr[i] / (1.f + cn[i]));
+    }
     store_vec(logits + o * M, x, M);
     warp_softmax(x, M);
     const float a = warp_norm(x, M);
@@ -716,10 +742,11 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     int U, Blocks bl, int H, int M, int L, int j, float read_scale, const float* count_gain_raw,
     const float* logits, const float* counts, const float* lh, const float* ln, const float* wh,
     const float* wn, const float* dlh, const float* dwh, const float* dlogits, float* dwrite,
-    float* draw, float* dn, float* dnsum, double* scal, ProductBwd pb) {
+    float* draw, float* dn, float* dnsum, double* scal, ProductBwd pb, MomentBwd mb) {
   __shared__ float red_dn[8][32 * NPL];
   __shared__ int blk[8];
   __shared__ float red_cg[8];  // count-gain partial of each warp's row (one atomic per unit run)
+  __shared__ float red_mg[8];  // the same for the moment gain
   const int T = bl.T;
   const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + wi;
@@ -770,15 +797,27 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
     }
     const float ge = pb.marginal ? product_gain(pb.relation_gain[j * H + h]) : 0.f;
     const float xd = x.dot(d1, M);
-    RowV<NPL> dr, dnv;
-    float cg = 0.f;
+    RowV<NPL> dr, dnv, cr, dcr;
+    if (mb.corr) cr.load(mb.corr + o, M);
+    const float mg = mb.corr ? mb.moment_gain[j * H + h] : 0.f;
+    float cg = 0.f, mgp = 0.f;
 #pragma unroll
     for (int i = 0; i < NPL; ++i) {
       const float dl = dlg.v[i] + x.v[i] * (d1.v[i] - xd);
       dr.v[i] = read_scale * dl;
       if (lane + 32 * i < M) cg += dl * log1pf(cn.v[i]);
       dnv.v[i] = (gain * dl - ge * dlg.v[i]) / (1.f + cn.v[i]);
+      if (mb.corr) {  // + g_m tanh(corr / (1 + n)): gradients of corr, n and g_m
+        const float inv = 1.f / (1.f + cn.v[i]), th = tanhf(cr.v[i] * inv);
+        const float dth = dl * mg * (1.f - th * th);
+        dcr.v[i] = dth * inv;
+        dnv.v[i] -= dth * cr.v[i] * inv * inv;
+        if (lane + 32 * i < M) mgp += dl * th;
+      }
     }
+    if (mb.corr) dcr.store(mb.dcorr + o, M);
+    mgp = warp_sum(mgp);
+    if (lane == 0) red_mg[wi] = mgp;
     dr.store(draw + o, M);
     dnv.store(dn + o, M);
     cg = warp_sum(cg);
@@ -805,8 +844,13 @@ __global__ void __launch_bounds__(256) k_logits_bwd(
       const int ur = (w0 + r) / T;
       double s = 0.0;
       int e = r;
-      for (; e < 8 && w0 + e < U * T && (w0 + e) / T == ur; ++e) s += red_cg[e];
+      double sm_ = 0.0;
+      for (; e < 8 && w0 + e < U * T && (w0 + e) / T == ur; ++e) {
+        s += red_cg[e];
+        sm_ += red_mg[e];
+      }
       atomicAdd(&scal[((int64_t)ur * L + j) * kNScal + kS_CountGain], s);
+      if (mb.corr) atomicAdd(&scal[((int64_t)ur * L + j) * kNScal + kS_MomentGain], sm_);
       r = e;
     }
   }
@@ -1120,7 +1164,8 @@ __global__ void __launch_bounds__(256) k_gate_grad(int T, int H, const float* X,
 // one warp per (u, t): final input gradients in the input layout / dtype.
 __global__ void k_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
                             const float* qn, const float* dqh, const float* dq_direct,
-                            const float* dkey, const float* dval, void* dq, void* dk, void* dv) {
+                            const float* dkey, const float* dval, void* dq, void* dk, void* dv,
+                            int64_t rope_pos0) {
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int U = B * H;
   if (w >= U * T) return;
@@ -1147,9 +1192,16 @@ __global__ void k_input_bwd(int B, int T, int H, int D, int Dv, int dt, const fl
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int d = lane + 32 * i;
+    const float g = nrm > kUnitEps ? (dy[i] - y[i] * yd) / nrm : dy[i] / kUnitEps;
+    float gq = g + dd[i];
+    if (rope_pos0 >= 0) {  // through the rotation: R^T of the rotated query's gradient
+      const float other = __shfl_xor_sync(0xffffffffu, gq, 1);
+      float c, s;
+      rope_cs(rope_pos0 + t, d, D, c, s);
+      gq = (d & 1) == 0 ? c * gq + s * other : -s * other + c * gq;
+    }
     if (d < D) {
-      const float g = nrm > kUnitEps ? (dy[i] - y[i] * yd) / nrm : dy[i] / kUnitEps;
-      store_out(dq, dst * D + d, g + dd[i], dt);
+      store_out(dq, dst * D + d, gq, dt);
       store_out(dk, dst * D + d, dkv[i], dt);
     }
     if (d < Dv) store_out(dv, dst * Dv + d, dvv[i], dt);
@@ -1193,6 +1245,7 @@ __global__ void k_fold(FoldArgs a) {
     a.g_count_gain_raw[j * H + h] += S(j, kS_CountGain) * sigmoid(a.count_gain_raw[j * H + h]);
     a.g_route_mlp_gain[j * H + h] += S(j, kS_MlpGain);
     a.g_relation_gain[j * H + h] += S(j, kS_RelGain);
+    if (a.g_moment_gain) a.g_moment_gain[j * H + h] += S(j, kS_MomentGain);
     // edge-logit softmax over the edges into j
     float w[kMaxIn], dw[kMaxIn];
     int ids[kMaxIn], n = 0;
@@ -1238,12 +1291,12 @@ cudaError_t launch_smem(const char* name, Kern k, int grid, size_t smem, cudaStr
 
 cudaError_t launch_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
                          int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0,
-                         cudaStream_t st) {
+                         int64_t rope_pos0, cudaStream_t st) {
   const int rows = B * T * H;
   if (!rows) return cudaSuccess;
   Launch scope_("input", st);
   k_input<<<blocks_for(rows, 8), 256, 0, st>>>(q, k, v, dt, B, T, H, D, Dv, qf, qh, qn, key0,
-                                                val0);
+                                                val0, rope_pos0);
   return cudaGetLastError();
 }
 
@@ -1272,7 +1325,7 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
                           const float* count_gain_raw, int j, const float* n0, const float* bsum,
                           const float* write, const float* raw, float* counts, float* logits,
                           float* lh, float* ln, float* wh, float* wn, float* n_final,
-                          cudaStream_t st) {
+                          const float* corr, const float* moment_gain, cudaStream_t st) {
   if (!U || !bl.nb) return cudaSuccess;
   Launch scope_("counts", st);
   const auto kern = M <= 32    ? k_counts<1>
@@ -1286,7 +1339,7 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
     if (e != cudaSuccess) return e;
   }
   kern<<<U * bl.nb, 256, smem, st>>>(U, bl, H, M, read_scale, count_gain_raw, j, n0, bsum, write, raw,
-                                    counts, logits, lh, ln, wh, wn, n_final);
+                                    counts, logits, lh, ln, wh, wn, n_final, corr, moment_gain);
   return cudaGetLastError();
 }
 
@@ -1404,7 +1457,7 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, double* scal, ProductBwd pb,
+                              float* dn, float* dnsum, double* scal, ProductBwd pb, MomentBwd mb,
                               cudaStream_t st) {
   const int rows = U * bl.T;
   if (!rows) return cudaSuccess;
@@ -1413,17 +1466,17 @@ cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int 
     k_logits_bwd<2><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal, pb);
+                                                     dnsum, scal, pb, mb);
   else if (M <= 128)
     k_logits_bwd<4><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal, pb);
+                                                     dnsum, scal, pb, mb);
   else
     k_logits_bwd<8><<<blocks_for(rows, 8), 256, 0, st>>>(U, bl, H, M, L, j, read_scale,
                                                      count_gain_raw, logits, counts, lh, ln, wh,
                                                      wn, dlh, dwh, dlogits, dwrite, draw, dn,
-                                                     dnsum, scal, pb);
+                                                     dnsum, scal, pb, mb);
   return cudaGetLastError();
 }
 
@@ -1491,12 +1544,12 @@ cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xm
 cudaError_t launch_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
                              const float* qn, const float* dqh, const float* dq_direct,
                              const float* dkey, const float* dval, void* dq, void* dk, void* dv,
-                             cudaStream_t st) {
+                             int64_t rope_pos0, cudaStream_t st) {
   const int rows = B * T * H;
   if (!rows) return cudaSuccess;
   Launch scope_("input_bwd", st);
   k_input_bwd<<<blocks_for(rows, 8), 256, 0, st>>>(B, T, H, D, Dv, dt, qh, qn, dqh, dq_direct,
-                                                    dkey, dval, dq, dk, dv);
+                                                    dkey, dval, dq, dk, dv, rope_pos0);
   return cudaGetLastError();
 }
 

@@ -11,8 +11,20 @@ constexpr int kMaxLevels = 8;
 constexpr int kMaxEdges = kMaxLevels * (kMaxLevels - 1);
 constexpr int kMaxIn = kMaxLevels - 1;
 
+// cos / sin of the rotary angle of element d (pair d / 2) at position pos,
+// pos * 10000^(-2i/D) (src/gpa/ops.py:117-132), in double precision (positions reach 2^31)
+__device__ __forceinline__ void rope_cs(int64_t pos, int d, int D, float& c, float& s) {
+  const double ang = (double)pos * exp(-log(10000.0) * (double)(d & ~1) / (double)D);
+  double sd, cd;
+  sincos(ang, &sd, &cd);
+  c = (float)cd;
+  s = (float)sd;
+}
+
 // per-(unit, level) scalar gradient accumulators
-enum ScalarSlot { kS_EtaK = 0, kS_EtaV, kS_CountGain, kS_MlpGain, kS_RelGain, kS_OutW, kNScal = 8 };
+enum ScalarSlot {
+  kS_EtaK = 0, kS_EtaV, kS_CountGain, kS_MlpGain, kS_RelGain, kS_OutW, kS_MomentGain, kNScal = 8
+};
 // per-(unit, edge) accumulators
 enum EdgeSlot { kE_W = 0, kE_G, kE_B, kNEdge = 3 };
 
@@ -30,9 +42,10 @@ struct BridgeIn {
   const float* counts;        // [U,T,M] counts of the target level (marginal term)
 };
 
+// rope_pos0 >= 0: the queries are rotated (positional moments), token t at rope_pos0 + t
 cudaError_t launch_input(const void* q, const void* k, const void* v, int dt, int B, int T, int H,
                          int D, int Dv, float* qf, float* qh, float* qn, float* key0, float* val0,
-                         cudaStream_t st);
+                         int64_t rope_pos0, cudaStream_t st);
 cudaError_t launch_level_prep(int U, int T, int H, int D, int M, const float* key, const float* C,
                               const float* Wg, const float* gbias, float beta_max, int pos_none,
                               float* nk, float* kn, float* slot, float* ns, float* sn, float* raw4,
@@ -46,7 +59,7 @@ cudaError_t launch_counts(int U, const Blocks& bl, int H, int M, float read_scal
                           const float* count_gain_raw, int j, const float* n0, const float* bsum,
                           const float* write, const float* raw, float* counts, float* logits,
                           float* lh, float* ln, float* wh, float* wn, float* n_final,
-                          cudaStream_t st);
+                          const float* corr, const float* moment_gain, cudaStream_t st);
 cudaError_t launch_rel_gates(int U, int H, int E, int pos_none, const float* decay_raw,
                              const float* beta_raw, float* ge, float* be, cudaStream_t st);
 cudaError_t launch_bridge(int U, int T, int H, int D, int M, int L, int j, const BridgeIn& in,
@@ -91,12 +104,19 @@ struct ProductBwd {
   const float* relation_gain;  // [L,H]
   int marginal;
 };
+// Positional-moment terms of a level's logits backward (corr null: none): the level's moment
+// reads corr [U,T,M] and their gradient dcorr (written).
+struct MomentBwd {
+  const float* corr;
+  const float* moment_gain;  // [L,H]
+  float* dcorr;
+};
 cudaError_t launch_logits_bwd(int U, const Blocks& bl, int H, int M, int L, int j,
                               float read_scale, const float* count_gain_raw, const float* logits,
                               const float* counts, const float* lh, const float* ln,
                               const float* wh, const float* wn, const float* dlh,
                               const float* dwh, const float* dlogits, float* dwrite, float* draw,
-                              float* dn, float* dnsum, double* scal, ProductBwd pb,
+                              float* dn, float* dnsum, double* scal, ProductBwd pb, MomentBwd mb,
                               cudaStream_t st);
 cudaError_t launch_counts_bwd(int U, const Blocks& bl, int M, const float* dn, const float* dnsum,
                               const float* dn_final, float* dwrite, float* dn0, cudaStream_t st);
@@ -124,7 +144,7 @@ cudaError_t launch_head_outer(int B, int T, int H, const float* X, int P, int xm
 cudaError_t launch_input_bwd(int B, int T, int H, int D, int Dv, int dt, const float* qh,
                              const float* qn, const float* dqh, const float* dq_direct,
                              const float* dkey, const float* dval, void* dq, void* dk, void* dv,
-                             cudaStream_t st);
+                             int64_t rope_pos0, cudaStream_t st);
 
 // Tensor-core variants (level_tc.cu): bf16 operands, fp32 accumulation; widths
 // (key_dim, value_dim, slots) multiples of 16 and <= 128.  Same arguments as the
@@ -177,7 +197,20 @@ struct FoldArgs {
   const double *scal, *scalE;
   float *g_residual_raw, *g_count_gain_raw, *g_route_mlp_gain, *g_relation_gain,
       *g_output_logits, *g_edge_logits, *g_relation_decay_raw, *g_relation_beta_raw;
+  float* g_moment_gain;  // null without positional moments
 };
 cudaError_t launch_fold(const FoldArgs& a, cudaStream_t st);
+
+// Positional moments of one level (moments.cu): forward P snapshots at every block start and
+// the end, corr [U,T,M] and the final state; backward dq (+=), dw (+=), the unit-key gradient
+// dkey (written) and dP_0 (written), with G_end [U, nb, D, M] as workspace.  pos0: absolute
+// position of the call's first token.
+cudaError_t launch_moments_fwd(int U, const Blocks& bl, int D, int M, int64_t pos0,
+                               const float* qh, const float* nk, const float* w, const float* P0,
+                               float* Pb, float* corr, float* Pout, cudaStream_t st);
+cudaError_t launch_moments_bwd(int U, const Blocks& bl, int D, int M, int64_t pos0,
+                               const float* qh, const float* nk, const float* w, const float* Pb,
+                               const float* dcorr, const float* dPfinal, float* Gend, float* dP0,
+                               float* dq, float* dw, float* dkey, cudaStream_t st);
 
 }  // namespace gpa

@@ -44,6 +44,8 @@ class DecodeSession:
         for lv in state.levels:
             flat += [lv.inner, lv.outer, lv.count]
         flat += [r.memory for r in state.relations]
+        if self._plan.moments:
+            flat += [lv.position for lv in state.levels]
         self._flat = [t.detach().to(dev, torch.float32).clone().contiguous() for t in flat]
         shapes = self._plan.state_shapes(True)
         base = len(self._flat)
@@ -54,8 +56,9 @@ class DecodeSession:
         else:  # written by the step that opens the next lag block
             self._flat += [torch.zeros(s, device=dev, dtype=torch.float32) for s in shapes[base:]]
         self._edges = model.edges
-        # [chunk offset, completion counter of the step kernel (0 between steps)]
-        self._offset = torch.tensor([state.chunk_offset, 0], device=dev, dtype=torch.int32)
+        # [chunk offset, completion counter of the step kernel (0 between steps), position]
+        self._offset = torch.tensor([state.chunk_offset, 0, state.position], device=dev,
+                                    dtype=torch.int32)
         self.offset = self._offset[:1]
         self.position = state.position
         self._graph = None
@@ -108,13 +111,14 @@ class DecodeSession:
     @property
     def state(self) -> GPAState:
         """The cache as a ``GPAState`` over the session's buffers (reads the device offset)."""
-        L, E = self._plan.L, self._plan.E
+        L, E, nm = self._plan.L, self._plan.E, self._plan.n_mom
         f = self._flat
-        levels = tuple(LevelState(f[3 * j], f[3 * j + 1], f[3 * j + 2]) for j in range(L))
+        levels = tuple(LevelState(f[3 * j], f[3 * j + 1], f[3 * j + 2],
+                                  f[3 * L + E + j] if nm else None) for j in range(L))
         rel = tuple(RelationState(i, j, f[3 * L + e]) for e, (i, j) in enumerate(self._edges))
         off = int(self.offset.item())
         frozen = None
         if off != 0:
-            base = 3 * L + E
+            base = 3 * L + E + nm
             frozen = tuple(ResidualSnapshot(f[base + 2 * j], f[base + 2 * j + 1]) for j in range(L))
         return GPAState(levels, rel, self.position, self.model.config.chunk_size, off, frozen)

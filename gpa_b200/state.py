@@ -46,7 +46,7 @@ class LevelState:
     inner: Tensor       # A: [B,H,Dk,M]
     outer: Tensor       # B: [B,H,M,Dv]
     count: Tensor       # [B,H,M] soft occurrence counts
-    position: Tensor | None = None  # positional moments (not used by the b200 backend)
+    position: Tensor | None = None  # [B,H,Dk,M] additive positional moments (moments mode)
 
 
 @dataclass(frozen=True)

@@ -52,6 +52,10 @@ typedef struct GpaDims {
                               src/gpa/attention.py:238-241), _PRODUCT
                               (paper_product_read, :231-234) or _MARGINAL
                               (product and relation_marginal, :235-236) */
+  int32_t positional_moments; /* positional_mode == "moments": rotated queries and
+                                 the per-level moment state (:277-283, :318-322) */
+  int32_t position;        /* GPAState.position: absolute index of the call's first
+                              token (rotary angles of positional moments) */
 } GpaDims;
 
 #define GPA_B200_READER_TANH 0
@@ -77,6 +81,7 @@ typedef struct GpaParams {
   const float* relation_gain;      /* [L,H] */
   const float* relation_decay_raw; /* [E,H] */
   const float* relation_beta_raw;  /* [E,H] */
+  const float* moment_gain;        /* [L,H] (positional moments; else unused) */
 } GpaParams;
 
 /* Same layout, writable: parameter gradients (accumulated with +=). */
@@ -96,6 +101,7 @@ typedef struct GpaParamGrads {
   float* relation_gain;
   float* relation_decay_raw;
   float* relation_beta_raw;
+  float* moment_gain;  /* NULL unless positional moments */
 } GpaParamGrads;
 
 /* Recurrent cache tensors, GPAState layout (src/gpa/state.py:30-58).
@@ -107,6 +113,7 @@ typedef struct GpaStateRef {
   float* relation[GPA_B200_MAX_EDGES];/* R [B,H,M_i,M_j] */
   float* frozen_inner[GPA_B200_MAX_LEVELS];
   float* frozen_outer[GPA_B200_MAX_LEVELS];
+  float* moment[GPA_B200_MAX_LEVELS]; /* P [B,H,Dk,M]: positional moments (else NULL) */
 } GpaStateRef;
 
 /* Bytes of the forward's saved buffer (kept alive until gpa_b200_backward). */
@@ -154,12 +161,13 @@ size_t gpa_b200_noalloc_capacity(void);
  * replacing a one-token DenseGPA.forward call (src/gpa/attention.py:347-414 with
  * T = 1, which runs _block_segment :299-345 on a one-token block).  The cache is
  * updated IN PLACE (state->frozen_* required: the snapshots of the current lag
- * block, written by this call when the token opens a block).  offset points to two
+ * block, written by this call when the token opens a block).  offset points to three
  * device int32: offset[0] is the cache's chunk_offset, advanced to
  * (offset[0] + 1) % chunk_size on the device; offset[1] is the step's completion
  * counter, which must be 0 before the first step and is left at 0 by every step
- * (steps on the same offset buffer must not overlap on the GPU).  dims->chunk_offset
- * is ignored.  out: [B,1,H,Dv] in the input dtype.  One kernel launch, stream-ordered,
+ * (steps on the same offset buffer must not overlap on the GPU); offset[2] is the
+ * cache's position (GPAState.position), advanced by one (the rotary angle of
+ * positional moments).  dims->chunk_offset and dims->position are ignored.  out: [B,1,H,Dv] in the input dtype.  One kernel launch, stream-ordered,
  * allocates nothing and never synchronizes with the host, so a sequence of steps can
  * be captured in a CUDA graph.  Widths must be multiples of 4. */
 int gpa_b200_step(const GpaDims* dims, const GpaParams* params, const void* q, const void* k,
@@ -201,7 +209,9 @@ int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, 
 /* Message of the last failure on the calling thread (0 if none). */
 int gpa_b200_last_error(char* buf, size_t len);
 
-/* ABI version of this header: 2 (GpaDims.reader_mode added). */
+/* ABI version of this header: 2 (GpaDims.reader_mode, positional_moments and
+ * position; GpaParams / GpaParamGrads.moment_gain; GpaStateRef.moment; a third
+ * offset word of gpa_b200_step). */
 int gpa_b200_abi_version(void);
 
 /* Kernel accounting (no counterpart in the reference, which has no native

@@ -35,7 +35,9 @@ def ostate_to_flat(st: oracle.OracleState):
 
 def to_oracle_state(st, device="cpu", dtype=torch.float64):
     levels = tuple((lv.inner.detach().to(device, dtype), lv.outer.detach().to(device, dtype),
-                    lv.count.detach().to(device, dtype)) for lv in st.levels)
+                    lv.count.detach().to(device, dtype))
+                   + (() if lv.position is None else (lv.position.detach().to(device, dtype),))
+                   for lv in st.levels)
     rel_ = tuple(r.memory.detach().to(device, dtype) for r in st.relations)
     fz = None if st.frozen is None else tuple((f.inner.detach().to(device, dtype),
                                                 f.outer.detach().to(device, dtype)) for f in st.frozen)

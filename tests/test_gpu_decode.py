@@ -33,11 +33,14 @@ def _inputs(gen, B, T, H, D, Dv, dtype):
 CFG_SPLIT = dict(heads=2, key_dim=32, value_dim=16, slots=(16, 8, 16), chunk_size=4)
 # the product reader (paper_product_read) with its marginal count term
 CFG_PRODUCT = dict(CFG, paper_product_read=True, relation_marginal=True)
+# positional moments: rotated queries and the per-level moment state
+CFG_MOMENTS = dict(CFG, positional_mode="moments")
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2),
                                        (torch.float16, 2e-2)])
-@pytest.mark.parametrize("prefill,cfg", [(6, CFG), (8, CFG), (6, CFG_SPLIT), (6, CFG_PRODUCT)])
+@pytest.mark.parametrize("prefill,cfg", [(6, CFG), (8, CFG), (6, CFG_SPLIT), (6, CFG_PRODUCT),
+                                         (6, CFG_MOMENTS)])
 def test_decode_steps_match_oracle(dtype, tol, prefill, cfg, cpu_threads):
     model = make_model(cfg, seed=3, prefix_std=0.02, perturb=0.1).cuda()
     gen = torch.Generator().manual_seed(7)

@@ -65,6 +65,13 @@ FP32_CASES = {
     "marginal_chunk64_T130": (dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
                                    chunk_size=64, paper_product_read=True,
                                    relation_marginal=True), 1, 130),
+    # positional moments: rotated queries and the per-level moment state
+    "moments_chunk4": (dict(heads=2, key_dim=8, value_dim=6, slots=(4, 8, 6), chunk_size=4,
+                            positional_mode="moments"), 2, 13),
+    "moments_token": (dict(heads=2, key_dim=4, value_dim=3, slots=(3, 2, 4), chunk_size=1,
+                           positional_mode="moments"), 2, 7),
+    "moments_chunk64_T130": (dict(heads=2, key_dim=32, value_dim=32, slots=(16, 16, 16, 32),
+                                  chunk_size=64, positional_mode="moments"), 1, 130),
 }
 
 
@@ -104,6 +111,9 @@ BF16_CASES = {
     "marginal_c2head_T200": (dict(heads=2, key_dim=128, value_dim=128, slots=(64, 64, 64, 128),
                                   chunk_size=64, paper_product_read=True,
                                   relation_marginal=True), 1, 200),
+    # positional moments at the benched head shape
+    "moments_c2head_T200": (dict(heads=2, key_dim=128, value_dim=128, slots=(64, 64, 64, 128),
+                                 chunk_size=64, positional_mode="moments"), 1, 200),
 }
 
 
@@ -180,6 +190,13 @@ def test_golden_reference_vectors(name, cpu_threads):
         exact = _golden_f64_param_grads(name)
         bad = {n: e for n, e in bad.items()
                if not rel(grads[n], exact[n]) <= max(tol, 2.5 * compare_summary(exact[n], rec["grad_params"][n]))}
+    if bad and dt == torch.float32:
+        # fp32 against a float64 record: a token-summed scalar gradient dominated by cancellation
+        # may instead be within max(2e-4, 3 x the fp32 reference's own error) of the record.  On
+        # moments_f64 the edge_logits gradient has norm 1.2e-7 (the others ~1e-3): the
+        # reference algorithm run in fp32 is 1.2e-4 from float64 there, this backend 3.0e-4.
+        own = _golden_f32_param_errors(name)
+        bad = {n: e for n, e in bad.items() if not e <= max(2e-4, 3 * own[n])}
     assert not bad, bad
     for i, (a, b) in enumerate(zip(tensors(st), rec["state"])):
         assert compare_summary(a.cpu(), b) <= tol, f"state[{i}]"
@@ -219,6 +236,19 @@ def _golden_f64_param_grads(name):
     out, _ = oracle.forward(oracle.OracleConfig(**cfg), p, *xs)
     out.square().mean().backward()
     return {n: t.grad for n, t in p.items() if t.grad is not None}
+
+
+def _golden_f32_param_errors(name):
+    """Relative error of each parameter gradient of the oracle run in fp32 (the reference
+    algorithm at this backend's precision) against a golden case's stored float64 record."""
+    rec = load_golden(name)
+    cfg, params, inputs = build(name)
+    p = {n: t.float().clone().requires_grad_() for n, t in params.items()}
+    xs = [inputs[x].float().clone().requires_grad_() for x in ("q", "k", "v")]
+    out, _ = oracle.forward(oracle.OracleConfig(**cfg), p, *xs)
+    out.float().square().mean().backward()
+    return {n: compare_summary(t.grad.double(), rec["grad_params"][n])
+            for n, t in p.items() if t.grad is not None and n in rec["grad_params"]}
 
 
 # ------------------------------------------------------- cache and call contracts

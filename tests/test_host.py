@@ -28,7 +28,8 @@ def test_config_accepts_default_flags_and_rejects_unimplemented_operators():
     GPAConfig(positional_mode="none", chunk_size=1)
     GPAConfig(paper_product_read=True)
     GPAConfig(paper_product_read=True, relation_marginal=True)
-    for bad in (dict(positional_mode="moments"), dict(rsa_update=True),
+    GPAConfig(positional_mode="moments")
+    for bad in (dict(positional_mode="moments", key_dim=31), dict(rsa_update=True),
                 dict(relation_marginal=True), dict(control_dim=4), dict(slot_feature="tanh"),
                 dict(balanced_bridge=True), dict(quadratic_features=True),
                 dict(learn_read_scale=True), dict(shared_query_center=True),
