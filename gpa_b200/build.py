@@ -19,7 +19,7 @@ from concurrent.futures import ThreadPoolExecutor
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 SOURCES = ("api.cu", "decode.cu", "gdn.cu", "gdn_tc.cu", "level.cu", "level_tc.cu", "tc5_probe.cu",
-           "gdn_tc5.cu", "moments.cu")
+           "gdn_tc5.cu", "moments.cu", "outer_tc5.cu")
 OUTPUT = os.path.join(HERE, "libgpa_b200.so")
 OBJDIR = os.path.join(HERE, "_build")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"

@@ -1034,8 +1034,9 @@ size_t gpa_b200_noalloc_capacity(void) { return kNoAllocBytes; }
 
 int gpa_b200_device_status(int clear) {
   const int a = gpa::tc5_device_status(clear != 0), b = gpa::decode_device_status(clear != 0);
-  if (a < 0 || b < 0) return -1;
-  return a ? a : b;
+  const int c = gpa::outer_device_status(clear != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a ? a : b ? b : c;
 }
 
 int gpa_b200_umma_selftest(int M, int mma_m, int N, int Kd, int a_mn, int b_mn, int flags,

@@ -201,6 +201,16 @@ struct FoldArgs {
 };
 cudaError_t launch_fold(const FoldArgs& a, cudaStream_t st);
 
+// Parameter-gradient reductions on tcgen05 (outer_tc5.cu), selected in tc_head_outer by
+// GPA_B200_OUTER=tc5 (the mma.sync kernel is the default).  P, Q multiples of 8, <= 256.
+bool tc5_outer_enabled();
+cudaError_t tc5_head_outer_launch(int B, int T, int H, const float* X, int P, int xmode,
+                                  const float* Y, int Q, const float* scale,
+                                  int64_t scale_stride, float cscale, float* out,
+                                  cudaStream_t st);
+// device status word of that kernel (GPA_B200_DEVICE_TIMEOUT after a wait gave up)
+int outer_device_status(bool clear);
+
 // Positional moments of one level (moments.cu): forward P snapshots at every block start and
 // the end, corr [U,T,M] and the final state; backward dq (+=), dw (+=), the unit-key gradient
 // dkey (written) and dP_0 (written), with G_end [U, nb, D, M] as workspace.  pos0: absolute

@@ -1209,6 +1209,8 @@ cudaError_t tc_prep_bwd(int U, int T, int H, int D, int M, const float* C, const
 cudaError_t tc_head_outer(int B, int T, int H, const float* X, int P, int xmode, const float* Y,
                           int Q, const float* scale, int64_t scale_stride, float cscale,
                           float* out, cudaStream_t st) {
+  if (tc5_outer_enabled())
+    return tc5_head_outer_launch(B, T, H, X, P, xmode, Y, Q, scale, scale_stride, cscale, out, st);
   const int64_t total = (int64_t)B * T;
   // the wider operand gets the 128-wide side of the CTA tile; half the tokens per CTA keep
   // the CTA count (and its work) as with 64 x 64 tiles

@@ -384,13 +384,14 @@ def test_backward_peak_memory_is_workspaces_plus_io():
 def test_mma_sync_fallback_kernels_match_in_a_child_process():
     """The kernels that are not the default pass the bf16 parity cases of the benched widths
     in a child process: the mma.sync WY transform and state sweep (GPA_B200_WY=mma,
-    GPA_B200_SWEEPS=mma) and the tcgen05 block outputs (GPA_B200_OUT=tc5); the switches are
-    read once per process."""
+    GPA_B200_SWEEPS=mma) and the tcgen05 block outputs and parameter-gradient reductions
+    (GPA_B200_OUT=tc5, GPA_B200_OUTER=tc5); the switches are read once per process."""
     import os
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
-    env = dict(os.environ, GPA_B200_WY="mma", GPA_B200_SWEEPS="mma", GPA_B200_OUT="tc5")
+    env = dict(os.environ, GPA_B200_WY="mma", GPA_B200_SWEEPS="mma", GPA_B200_OUT="tc5",
+               GPA_B200_OUTER="tc5")
     r = subprocess.run([sys.executable, "-m", "pytest", os.path.join(here, "test_gpu_parity.py"),
                         "-x", "-q", "-p", "no:cacheprovider", "-k",
                         "test_bf16_forward_backward and (c2head or odd_widths)"],
