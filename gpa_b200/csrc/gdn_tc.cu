@@ -644,6 +644,18 @@ __global__ void __launch_bounds__(kStateThreads, 2) tc_bwd_state(ScanBatch b, in
                            false);
   for (int n = bl.nb - 1; n >= 0; --n) {
     const int t0 = bl.start(n), c = bl.end(n) - t0;
+    if (n > 0 && threadIdx.x == 0) {
+      // the rows block n - 1 reads, towards L2 while this block computes (the sweep otherwise
+      // waits on DRAM at every block start)
+      const int p0 = bl.start(n - 1), pc = bl.end(n - 1) - p0;
+      const int64_t pr = row(u, T, p0);
+      tc5::prefetch_l2(d.k + pr * K, (uint32_t)(pc * K * 4));
+      tc5::prefetch_l2(d.q + pr * K, (uint32_t)(pc * K * 4));
+      tc5::prefetch_l2(d.Wk + pr * K, (uint32_t)(pc * K * 4));
+      tc5::prefetch_l2(d.dO + pr * V, (uint32_t)(pc * V * 4));
+      tc5::prefetch_l2(d.sc_dW + pr * V, (uint32_t)(pc * V * 4));
+      if (d.ext) tc5::prefetch_l2(d.ext + ((int64_t)u * (bl.nb + 1) + n - 1) * KV, (uint32_t)(KV * 4));
+    }
     get_slice(d.Dend + ((int64_t)u * bl.nb + n) * KV);
     gate_finish(gr, c, G, nullptr);
     for (int t = threadIdx.x; t < C; t += blockDim.x) {
