@@ -229,7 +229,7 @@ struct HeadScalars {
 
 struct StepSmem {
   size_t Ss, q, qn, key, kn, val, tmp, tmp2, pre, yb, part, red, slot, write, logits, valin, qo,
-      gates, hs, mdel, mcor, bar, total;
+      gates, hs, mdel, mcor, wu, lqu, bar, total;
   int msg_off[kMaxEdges];
   __host__ __device__ StepSmem(const StepArgs& a) {
     size_t off = 0;
@@ -274,6 +274,8 @@ struct StepSmem {
     hs = take(3 * kMaxEdges + 11 * kMaxLevels);  // this head's scalars (HeadScalars)
     mdel = take(a.D);  // positional moments: delta of the level key, moment reads
     mcor = take(mx);
+    wu = take(a.L * mx);   // u(write_i) of every level (relation keys)
+    lqu = take(a.L * mx);  // u(softmax(logits_i)) of every level (relation queries)
     bar = take(4);  // the bulk loads' mbarrier (16-byte aligned)
     total = off * sizeof(float);
   }
@@ -452,13 +454,26 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   }
 
   // ------------------------------------------------ relations
+  // the relation keys u(write_i) and queries u(softmax(logits_i)) of every level, once (each
+  // level sends L - 1 edges); lnorm[i] = |softmax(logits_i)| (the product reader's factor)
+  float lnorm[kMaxLevels];
+  if (a.E > 0)
+    for (int i = 0; i < L; ++i) {
+      const int Mi = a.M[i];
+      float* lqi = sm + Lm.lqu + i * mx;
+      unit_vec(sm + Lm.wu + i * mx, sm + Lm.write + i * mx, Mi, red);
+      softmax_vec(lqi, sm + Lm.logits + i * mx, Mi, red);
+      float ss = 0.f;
+      for (int m = threadIdx.x; m < Mi; m += blockDim.x) ss += lqi[m] * lqi[m];
+      lnorm[i] = sqrtf(block_sum_all(ss, red));
+      const float inv = 1.f / fmaxf(lnorm[i], kUnitEps);
+      for (int m = threadIdx.x; m < Mi; m += blockDim.x) lqi[m] *= inv;
+      __syncthreads();
+    }
   for (int e = 0; e < a.E; ++e) {
     const int i = a.es[e], j = a.ed[e], Mi = a.M[i], Mj = a.M[j];
-    float* kv = tmp;   // u(write_i)
-    float* lq = tmp2;  // u(softmax(logits_i))
-    unit_vec(kv, sm + Lm.write + i * mx, Mi, red);
-    softmax_vec(lq, sm + Lm.logits + i * mx, Mi, red);
-    unit_vec(lq, lq, Mi, red);
+    const float* kv = sm + Lm.wu + i * mx;   // u(write_i)
+    const float* lq = sm + Lm.lqu + i * mx;  // u(softmax(logits_i))
     const int64_t sz = (int64_t)Mi * Mj;
     float* Rg = a.s.relation[e] + u * sz;
     load_mat(Ss, Rg, (int)sz, nullptr, bl);
@@ -471,16 +486,6 @@ __global__ void __launch_bounds__(kStepThreads) k_decode_step(StepArgs a) {
   }
 
   // ------------------------------------------------ dense reader and outer steps
-  // product reader: |softmax(logits_i)| of every level, the factor of the messages it sends
-  float lnorm[kMaxLevels];
-  if (a.reader != GPA_B200_READER_TANH)
-    for (int i = 0; i < L; ++i) {
-      softmax_vec(tmp, sm + Lm.logits + i * mx, a.M[i], red);
-      float ss = 0.f;
-      for (int m = threadIdx.x; m < a.M[i]; m += blockDim.x) ss += tmp[m] * tmp[m];
-      lnorm[i] = sqrtf(block_sum_all(ss, red));
-      __syncthreads();
-    }
   for (int j = 0; j < L; ++j) {
     const int M = a.M[j];
     float* base = tmp;  // [M]
