@@ -52,7 +52,7 @@ CPU_SAMPLE = dict(batch=2, length=64)  # bounded CPU sample of the same layer
 TRAFFIC_RATIO = {"tc_bwd_chunk": 1.00}
 # kernels of the chunked GDN scans: tensor-core bound by their algorithmic FLOPs
 CHUNK_KERNELS = ("tc_fwd_chunk", "tc5_fwd_chunk", "tc_fwd_state", "tc5_fwd_state", "tc_fwd_out",
-                 "tc5_fwd_out", "tc_bwd_local", "tc_bwd_state", "tc_bwd_chunk")
+                 "tc5_fwd_out", "tc_bwd_local", "tc_bwd_state", "tc5_bwd_state", "tc_bwd_chunk")
 
 
 def peaks():
@@ -134,6 +134,7 @@ def kernel_flops(cfg, units, length):
                    ("tc_bwd_local", "gdn_bwd_local"), ("tc_bwd_state", "gdn_bwd_state")):
         out[tk] = out[sk]
     out["tc5_fwd_state"] = out["gdn_fwd_state"]  # the tcgen05 forward sweep
+    out["tc5_bwd_state"] = out["gdn_bwd_state"]  # the tcgen05 backward sweep
     out["tc_fwd_chunk"] = out["gdn_fwd_chunk"] // 2
     out["tc5_fwd_chunk"] = out["tc_fwd_chunk"]  # the tcgen05 WY / UT transform
     out["tc5_fwd_out"] = out["tc_fwd_out"]  # the tcgen05 block outputs

@@ -98,6 +98,7 @@ cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaSt
 // mma.sync sweeps instead (kept for comparison)
 bool tc5_sweeps_enabled();
 cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
+cudaError_t tc5_bwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st);
 // tcgen05 WY / UT transform of every block (gdn_tc5.cu): A, T (kept), U, Wk;
 // GPA_B200_WY=mma selects the mma.sync kernel instead
 bool tc5_wy_enabled();

@@ -1171,7 +1171,9 @@ cudaError_t tc_backward_local(const ScanBatch& b, int U, const Blocks& bl, cudaS
 
 // U and Wk of every block come from the forward (kept in the saved buffer).
 cudaError_t tc_backward_rest(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
-  cudaError_t e = tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st, true);
+  cudaError_t e = tc5_sweeps_enabled()
+                      ? tc5_bwd_state_launch(b, U, bl, st)
+                      : tc_launch_groups<LBwdState>("tc_bwd_state", tc_bwd_state, U, b, U, bl, st, true);
   if (e != cudaSuccess) return e;
   return tc_launch_groups<LBwdChunk>("tc_bwd_chunk", tc_bwd_chunk, U * bl.nb, b, U, bl, st,
                                      false, 113);

@@ -402,6 +402,373 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
   if (warp == 0) tc5::tmem_free(tbase, kSweepCols);
 }
 
+// ------------------------------------------------------------------ backward state sweep
+
+// The reverse sweep carries D = dL/dS [K x V] from the last block to the first:
+//   dW = dW_local + diag(lambda) K D                 (dW_local: the read path's, in sc_dW)
+//   D <- e^{G_c} D + (e^G Q)^T dO - Wk^T dW + ext_n
+// Dend[n] holds D at the end of block n, dS0 the gradient of the initial state.  As in the
+// forward sweep both products run transposed, a TMEM lane being a value column v:
+//   X^T  [V x c] = D^T K^T                      (A = D^T hi / lo, 128 rows v; B = K, rows t)
+//   D'^T [V x K] = dO^T (e^G Q) + (-dW)^T Wk    (A = dO^T, (-dW)^T hi / lo, rows v, reduction
+//                                                over t; B = e^G Q, Wk hi / lo, MN-major)
+// and D' = e^{G_c} D + ext_n + D'^T^T is formed in the epilogue from the fp32 D each thread
+// keeps in registers (thread (v, half) holds D[k][v] for half of the k).  Products per
+// block: D hi K + D lo K, dO Qg, and dW hi Wk hi + dW hi Wk lo + dW lo Wk hi: the operand
+// split of the mma.sync sweep, with D carried in fp32 instead of a bf16 hi / lo pair.
+//
+// Per block n of a unit (one CTA per unit and scan, 256 threads):
+//   MMA 1 issued; while it runs the e^G Q and Wk rows of block n are converted into their
+//   operand tiles (straight from global memory, bulk-prefetched into L2 one block ahead),
+//   dO^T is packed and the dW_local values of the epilogue are loaded;
+//   epilogue 1 (dW out, (-dW)^T hi / lo); MMA 2 issued; while it runs the fp32 K rows of
+//   block n-1 (landed by a bulk copy) become the next MMA-1 operand; epilogue 2 (D update,
+//   Dend[n-1] or dS0 out, D^T hi / lo).
+struct LBwdSweep {
+  uint32_t DtH, DtL, Kb, dOt, NWh, NWl, Qb, WkH, WkL, rawK, G, lam, eG, bar, slot, total;
+  __host__ __device__ LBwdSweep(int K, int V) {
+    uint32_t o = 0;
+    auto take = [&](uint32_t b) {
+      o = (o + 127u) & ~127u;
+      const uint32_t r = o;
+      o += b;
+      return r;
+    };
+    DtH = take(128 * K * 2);  // D^T: A of MMA 1, K-major, rows v (128), reduction k
+    DtL = take(128 * K * 2);
+    Kb = take(C * K * 2);     // K: B of MMA 1, K-major, rows t, reduction k (hi only)
+    dOt = take(128 * C * 2);  // dO^T: A of MMA 2, K-major, rows v, reduction t (hi only)
+    NWh = take(128 * C * 2);  // (-dW)^T: A of MMA 2, K-major, rows v, reduction t
+    NWl = take(128 * C * 2);
+    Qb = take(K * C * 2);     // e^G Q: B of MMA 2, MN-major, rows k, reduction t (hi only)
+    WkH = take(K * C * 2);    // Wk: B of MMA 2, MN-major, rows k, reduction t
+    WkL = take(K * C * 2);
+    rawK = take(C * K * 4);   // fp32 K rows of the next block, landed by a bulk copy
+    G = take(C * 4);
+    lam = take(C * 4);
+    eG = take(C * 4);
+    bar = take(2 * 8);
+    slot = take(16);
+    total = o;
+    (void)V;
+  }
+};
+
+constexpr int kBwdThreads = 512;              // 16 warps: four per TMEM lane quarter
+constexpr int kBwdParts = kBwdThreads / 128;  // threads per state column
+
+// fp32 rows [c x K] in global memory (row stride K) -> bf16 operand tiles as stage_to_tiles
+// lays them out (rows >= c zero), each row times rowmul[t] when given; every load of the
+// thread is in flight before the first conversion.  kBwdThreads threads, K <= 128.
+constexpr int kGlobalItems = C * kMaxScanWidth / 8 / kBwdThreads;
+GPA_DEV void global_rows_to_tiles(const float* src, int c, int K, bool kmajor, unsigned char* hi,
+                                  unsigned char* lo, const float* rowmul) {
+  const int k8n = K >> 3, n = C * k8n;
+  float4 a[kGlobalItems], b[kGlobalItems];
+#pragma unroll
+  for (int q = 0; q < kGlobalItems; ++q) {
+    const int i = threadIdx.x + q * kBwdThreads;
+    const int j = i & 7, g = i >> 3, tq = g / k8n;
+    const int t = 8 * tq + j, k8 = (g - tq * k8n + j) % k8n;
+    if (i < n && t < c) {
+      const float* p = src + (int64_t)t * K + 8 * k8;
+      a[q] = *reinterpret_cast<const float4*>(p);
+      b[q] = *reinterpret_cast<const float4*>(p + 4);
+    } else {
+      a[q] = b[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kGlobalItems; ++q) {
+    const int i = threadIdx.x + q * kBwdThreads;
+    if (i < n) {
+      const int j = i & 7, g = i >> 3, tq = g / k8n;
+      const int t = 8 * tq + j, k8 = (g - tq * k8n + j) % k8n;
+      const float f = (rowmul && t < c) ? rowmul[t] : 1.f;
+      const float x[8] = {a[q].x * f, a[q].y * f, a[q].z * f, a[q].w * f,
+                          b[q].x * f, b[q].y * f, b[q].z * f, b[q].w * f};
+      const uint32_t o = kmajor ? tc5::kmajor_off(t, 8 * k8, K) : tc5::mnmajor_off(8 * k8, t, C);
+      uint4 h, l;
+      split8(x, h, l);
+      *reinterpret_cast<uint4*>(hi + o) = h;
+      if (lo) *reinterpret_cast<uint4*>(lo + o) = l;
+    }
+  }
+}
+
+// G, lambda (sweep_gate_finish) and eG_t = e^{G_t} (0 for t >= c) of a block, by warp 0.
+GPA_DEV void bwd_gate_finish(const SweepGates& r, int c, float* G, float* lam, float* eG) {
+  sweep_gate_finish(r, c, G, lam);
+  if (threadIdx.x < 32) {
+    const int t = threadIdx.x;
+    __syncwarp();
+    eG[t] = t < c ? __expf(G[t]) : 0.f;
+    eG[t + 32] = t + 32 < c ? __expf(G[t + 32]) : 0.f;
+  }
+}
+
+// grid (U, nscan), 512 threads, one CTA per SM.  KMAX bounds the key width K.
+// Thread (v, part) of lane quarter v / 32 owns column v for tokens 16 part .. + 15 in epilogue
+// 1 and for a contiguous range of up to KMAX / 4 state rows (whole groups of 8) in epilogue 2.
+template <int KMAX>
+__global__ void __launch_bounds__(kBwdThreads, 1) tc5_bwd_state(ScanBatch b, int U, Blocks bl) {
+  const ScanDesc& d = b.s[blockIdx.y];
+  const int u = blockIdx.x, K = d.K, V = d.V, T = bl.T;
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const LBwdSweep L(K, V);
+  unsigned char* DtH = sm + L.DtH;
+  unsigned char* DtL = sm + L.DtL;
+  unsigned char* Kb = sm + L.Kb;
+  unsigned char* dOt = sm + L.dOt;
+  unsigned char* NWh = sm + L.NWh;
+  unsigned char* NWl = sm + L.NWl;
+  unsigned char* Qb = sm + L.Qb;
+  unsigned char* WkH = sm + L.WkH;
+  unsigned char* WkL = sm + L.WkL;
+  float* rawK = reinterpret_cast<float*>(sm + L.rawK);
+  float* G = reinterpret_cast<float*>(sm + L.G);
+  float* lam = reinterpret_cast<float*>(sm + L.lam);
+  float* eG = reinterpret_cast<float*>(sm + L.eG);
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L.bar);
+  uint64_t* bar_tma = bar_mma + 1;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
+  constexpr int SH = KMAX / kBwdParts;  // D values per thread (max)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, part = warp >> 2;
+  const int v = 32 * q + lane;
+  const bool active = 32 * q < V;  // warp-uniform: the quarter holds state columns
+  const bool vok = v < V;
+  const int gp = (K / 8 + kBwdParts - 1) / kBwdParts;  // groups of 8 rows per part
+  const int kb = 8 * gp * part;                        // this thread's first row of D
+  const int kn = max(0, min(K - kb, 8 * gp));          // and how many it holds
+  const int tb = 16 * part;                            // its first token of epilogue 1
+  const int64_t KV = (int64_t)K * V;
+  const int nb = bl.nb;
+  const float sc = d.dO_scale ? d.dO_scale[u] : 1.f;
+
+  // A tiles: rows v >= V stay zero for the whole sweep
+  for (uint32_t i = tid * 16; i < 128u * K * 2; i += blockDim.x * 16) {
+    *reinterpret_cast<uint4*>(DtH + i) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(DtL + i) = make_uint4(0, 0, 0, 0);
+  }
+  for (uint32_t i = tid * 16; i < 128u * C * 2; i += blockDim.x * 16) {
+    *reinterpret_cast<uint4*>(dOt + i) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(NWh + i) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(NWl + i) = make_uint4(0, 0, 0, 0);
+  }
+  if (warp == 0) tc5::tmem_alloc(slot, kSweepCols);
+  if (tid == 0) {
+    tc5::mbar_init(bar_mma, 1);
+    tc5::mbar_init(bar_tma, 1);
+    tc5::mbar_fence_init();
+  }
+  auto issue_k = [&](int n) {  // bulk copy of block n's fp32 K rows
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    const uint32_t bytes = (uint32_t)(c * K * 4);
+    tc5::mbar_expect_tx(bar_tma, bytes);
+    tc5::bulk_g2s(rawK, d.k + row(u, T, t0) * K, bytes, bar_tma);
+  };
+  // D^T hi / lo of this thread's rows (8 at a time) into the MMA-1 operand; D to dst
+  float dr[SH];
+  auto put_state = [&](float* dst) {
+#pragma unroll
+    for (int i = 0; i < SH; i += 8) {
+      if (i < kn) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[j] = dr[i + j];
+          if (vok) dst[(int64_t)(kb + i + j) * V + v] = x[j];
+        }
+        uint4 h, l;
+        split8(x, h, l);
+        const uint32_t o = tc5::kmajor_off(v, kb + i, K);
+        *reinterpret_cast<uint4*>(DtH + o) = h;
+        *reinterpret_cast<uint4*>(DtL + o) = l;
+      }
+    }
+  };
+  tc5::fence_before_sync();
+  __syncthreads();  // barriers initialised, tiles zeroed, TMEM allocated
+  tc5::fence_after_sync();
+  if (tid == 0) issue_k(nb - 1);
+#pragma unroll
+  for (int i = 0; i < SH; ++i) dr[i] = 0.f;
+  if (active) {  // D at the end of the last block: dS_final + ext[nb]
+    const float* e0 = d.ext ? d.ext + ((int64_t)u * (nb + 1) + nb) * KV : nullptr;
+    const float* f0 = d.dS_final ? d.dS_final + (int64_t)u * KV : nullptr;
+#pragma unroll
+    for (int i = 0; i < SH; ++i) {
+      if (i < kn && vok) {
+        const int64_t o = (int64_t)(kb + i) * V + v;
+        dr[i] = (e0 ? e0[o] : 0.f) + (f0 ? f0[o] : 0.f);
+      }
+    }
+    put_state(d.Dend + ((int64_t)u * nb + nb - 1) * KV);
+  }
+  uint32_t tph = 0, mph = 0;
+  bool ok = true, all_ok = true;
+  {
+    const int cl = bl.end(nb - 1) - bl.start(nb - 1);
+    bwd_gate_finish(sweep_gate_fetch(d, u, bl.start(nb - 1), cl), cl, G, lam, eG);
+    ok = tc5::mbar_wait(bar_tma, tph);
+    tph ^= 1;
+    stage_to_tiles(rawK, cl, K, true, Kb, nullptr);
+  }
+  SweepGates gr{0.f, 0.f};
+  if (nb > 1) gr = sweep_gate_fetch(d, u, bl.start(nb - 2), bl.end(nb - 2) - bl.start(nb - 2));
+  tc5::fence_async_smem();
+  tc5::fence_before_sync();
+  all_ok = __syncthreads_and(ok);
+  tc5::fence_after_sync();
+  const uint32_t tbase = *slot;
+  if (tid == 0 && all_ok && nb > 1) issue_k(nb - 2);
+  const uint32_t id1 = tc5::idesc_bf16(128, C, false, false);
+  const uint32_t id2 = tc5::idesc_bf16(128, K, false, true);
+  for (int n = nb - 1; all_ok && n >= 0; --n) {
+    const int t0 = bl.start(n), c = bl.end(n) - t0;
+    const int64_t r0 = row(u, T, t0);
+    if (tid == 0) {
+      // MMA 1: X^T = D^T K^T (D hi and lo)
+      const uint32_t ah = tc5::saddr(DtH), al = tc5::saddr(DtL), bk = tc5::saddr(Kb);
+      for (int ks = 0; ks < K / 16; ++ks)
+        tc5::mma(tbase, tc5::sdesc(ah, K, ks), tc5::sdesc(bk, K, ks), id1, ks > 0);
+      for (int ks = 0; ks < K / 16; ++ks)
+        tc5::mma(tbase, tc5::sdesc(al, K, ks), tc5::sdesc(bk, K, ks), id1, true);
+      tc5::commit(bar_mma);
+      if (n > 0) {  // the rows block n - 1 reads, towards L2 while this block computes
+        const int p0 = bl.start(n - 1), pc = bl.end(n - 1) - p0;
+        const int64_t pr = row(u, T, p0);
+        tc5::prefetch_l2(d.q + pr * K, (uint32_t)(pc * K * 4));
+        tc5::prefetch_l2(d.Wk + pr * K, (uint32_t)(pc * K * 4));
+        tc5::prefetch_l2(d.dO + pr * V, (uint32_t)(pc * V * 4));
+        tc5::prefetch_l2(d.sc_dW + pr * V, (uint32_t)(pc * V * 4));
+        if (d.ext) tc5::prefetch_l2(d.ext + ((int64_t)u * (nb + 1) + n - 1) * KV, (uint32_t)(KV * 4));
+      }
+    }
+    // while MMA 1 runs: this thread's dO and dW_local values (loads issued first), the MMA-2
+    // B operands of block n, dO^T
+    float dw[16], o16[16];
+    {
+      const bool act = active && vok;
+      const float* op = d.dO + row(u, T, t0 + tb) * V + v;
+      const float* wp = d.sc_dW + row(u, T, t0 + tb) * V + v;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const bool in = act && tb + j < c;
+        o16[j] = in ? ld_pinned(op + (int64_t)j * V) : 0.f;
+        dw[j] = in ? ld_pinned(wp + (int64_t)j * V) : 0.f;
+      }
+    }
+    global_rows_to_tiles(d.q + r0 * K, c, K, false, Qb, nullptr, eG);
+    global_rows_to_tiles(d.Wk + r0 * K, c, K, false, WkH, WkL, nullptr);
+    if (active) {
+#pragma unroll
+      for (int g8 = 0; g8 < 2; ++g8) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = sc * o16[8 * g8 + j];
+        *reinterpret_cast<uint4*>(dOt + tc5::kmajor_off(v, tb + 8 * g8, C)) = pack8(x);
+      }
+    }
+    ok = ok && tc5::mbar_wait(bar_mma, mph);
+    mph ^= 1;
+    tc5::fence_after_sync();
+    if (active) {  // epilogue 1: dW = dW_local + lambda X; dW out; (-dW)^T hi / lo
+      float acc[16];
+      tc5::tmem_ld16(tc5::tmem_at(tbase, tb), acc);
+      tc5::tmem_wait_ld();
+#pragma unroll
+      for (int j8 = 0; j8 < 2; ++j8) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int jj = 8 * j8 + j, t = tb + jj;
+          const bool in = vok && t < c;
+          const float w = in ? dw[jj] + lam[t] * acc[jj] : 0.f;
+          if (in) d.sc_dW[row(u, T, t0 + t) * V + v] = w;
+          x[j] = -w;
+        }
+        uint4 h, l;
+        split8(x, h, l);
+        const uint32_t o = tc5::kmajor_off(v, tb + 8 * j8, C);
+        *reinterpret_cast<uint4*>(NWh + o) = h;
+        *reinterpret_cast<uint4*>(NWl + o) = l;
+      }
+    }
+    tc5::fence_async_smem();
+    tc5::fence_before_sync();
+    __syncthreads();
+    tc5::fence_after_sync();
+    if (tid == 0 && ok) {  // MMA 2: D'^T = dO^T Qg + (-dW)^T Wk (hi hi, hi lo, lo hi)
+      const uint32_t ao = tc5::saddr(dOt), ah = tc5::saddr(NWh), al = tc5::saddr(NWl);
+      const uint32_t bq = tc5::saddr(Qb), bh = tc5::saddr(WkH), bl_ = tc5::saddr(WkL);
+      const uint32_t d2 = tbase + C;
+      for (int ks = 0; ks < C / 16; ++ks) {
+        tc5::mma(d2, tc5::sdesc(ao, C, ks), tc5::sdesc(bq, C, ks), id2, ks > 0);
+        tc5::mma(d2, tc5::sdesc(ah, C, ks), tc5::sdesc(bh, C, ks), id2, true);
+        tc5::mma(d2, tc5::sdesc(ah, C, ks), tc5::sdesc(bl_, C, ks), id2, true);
+        tc5::mma(d2, tc5::sdesc(al, C, ks), tc5::sdesc(bh, C, ks), id2, true);
+      }
+      tc5::commit(bar_mma);
+    }
+    // ext_n of this thread's D rows, 16 at a time in two alternating buffers: the first
+    // group is loaded while MMA 2 runs, each next one before the current group is used
+    const float* ext = (d.ext && active && vok) ? d.ext + ((int64_t)u * (nb + 1) + n) * KV + v : nullptr;
+    float ea[16], eb[16];
+    auto load_ext = [&](float (&e)[16], int i) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        e[j] = (ext && i + j < kn) ? ext[(int64_t)(kb + i + j) * V] : 0.f;
+    };
+    load_ext(ea, 0);
+    int cn = 0;
+    if (n > 0) {  // while MMA 2 runs: the K rows of block n - 1 -> its MMA-1 operand
+      cn = bl.end(n - 1) - bl.start(n - 1);
+      ok = ok && tc5::mbar_wait(bar_tma, tph);
+      tph ^= 1;
+      stage_to_tiles(rawK, cn, K, true, Kb, nullptr);
+    }
+    ok = ok && tc5::mbar_wait(bar_mma, mph);
+    mph ^= 1;
+    tc5::fence_after_sync();
+    const float gc = __expf(G[c - 1]);
+    if (active) {  // epilogue 2: D <- e^{G_c} D + acc + ext_n; Dend[n - 1] (or dS0); D^T tiles
+#pragma unroll
+      for (int i = 0; i < SH; i += 16) {
+        if (i < kn) {
+          float(&cur)[16] = ((i >> 4) & 1) ? eb : ea;
+          float(&nxt)[16] = ((i >> 4) & 1) ? ea : eb;
+          if (i + 16 < kn) load_ext(nxt, i + 16);
+          float acc[16];
+          tc5::tmem_ld16(tc5::tmem_at(tbase, C + kb + i), acc);
+          tc5::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) dr[i + j] = gc * dr[i + j] + acc[j] + cur[j];
+        }
+      }
+      put_state(n > 0 ? d.Dend + ((int64_t)u * nb + n - 1) * KV : d.dS0 + (int64_t)u * KV);
+    }
+    if (n > 0) {  // the gates of block n - 1
+      __syncthreads();  // every thread has read G[c - 1] and lambda
+      bwd_gate_finish(gr, cn, G, lam, eG);
+      if (n >= 2) gr = sweep_gate_fetch(d, u, bl.start(n - 2), bl.end(n - 2) - bl.start(n - 2));
+    }
+    tc5::fence_async_smem();
+    tc5::fence_before_sync();
+    all_ok = __syncthreads_and(ok);
+    tc5::fence_after_sync();
+    if (tid == 0 && all_ok && n >= 2) issue_k(n - 2);  // the staging rows were read
+  }
+  if (!all_ok && tid == 0) {
+    fail_status();
+    tc5::mbar_wait(bar_tma, tph);  // a bulk copy may still be landing: bounded wait
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc5::tmem_free(tbase, kSweepCols);
+}
+
 // ------------------------------------------------------------------ WY / UT transform
 
 // Per block of c <= 64 tokens of a (K, V) scan (gdn.cuh):
@@ -990,6 +1357,32 @@ cudaError_t tc5_fwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cu
     if (e != cudaSuccess) return e;
     Launch scope("tc5_fwd_state", st);
     kern<<<dim3(U, sub.n), kSweepThreads, smem, st>>>(sub, U, bl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t tc5_bwd_state_launch(const ScanBatch& b, int U, const Blocks& bl, cudaStream_t st) {
+  bool done[kMaxScans] = {};
+  for (int i = 0; i < b.n; ++i) {
+    if (done[i]) continue;
+    ScanBatch sub;
+    sub.tc = b.tc;
+    sub.n = 0;
+    for (int j = i; j < b.n; ++j)
+      if (!done[j] && b.s[j].K == b.s[i].K && b.s[j].V == b.s[i].V) {
+        sub.s[sub.n++] = b.s[j];
+        done[j] = true;
+      }
+    const size_t smem = LBwdSweep(b.s[i].K, b.s[i].V).total;
+    if (smem > 227 * 1024 || b.s[i].K > kMaxScanWidth || b.s[i].V > kMaxScanWidth)
+      return cudaErrorInvalidConfiguration;
+    const auto kern = b.s[i].K <= 64 ? tc5_bwd_state<64> : tc5_bwd_state<128>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    Launch scope("tc5_bwd_state", st);
+    kern<<<dim3(U, sub.n), kBwdThreads, smem, st>>>(sub, U, bl);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
