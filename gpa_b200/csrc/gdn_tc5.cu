@@ -413,11 +413,12 @@ __global__ void __launch_bounds__(kSweepThreads, KMAX <= 64 ? 2 : 1)
 //   D'^T [V x K] = dO^T (e^G Q) + (-dW)^T Wk    (A = dO^T, (-dW)^T hi / lo, rows v, reduction
 //                                                over t; B = e^G Q, Wk hi / lo, MN-major)
 // and D' = e^{G_c} D + ext_n + D'^T^T is formed in the epilogue from the fp32 D each thread
-// keeps in registers (thread (v, half) holds D[k][v] for half of the k).  Products per
-// block: D hi K + D lo K, dO Qg, and dW hi Wk hi + dW hi Wk lo + dW lo Wk hi: the operand
-// split of the mma.sync sweep, with D carried in fp32 instead of a bf16 hi / lo pair.
+// keeps in registers (four threads per column v, each holding D[k][v] for a quarter of the
+// k).  Products per block: D hi K + D lo K, dO Qg, and dW hi Wk hi + dW hi Wk lo + dW lo Wk
+// hi: the operand split of the mma.sync sweep, with D carried in fp32 instead of a bf16 hi /
+// lo pair.
 //
-// Per block n of a unit (one CTA per unit and scan, 256 threads):
+// Per block n of a unit (one CTA per unit and scan, 512 threads):
 //   MMA 1 issued; while it runs the e^G Q and Wk rows of block n are converted into their
 //   operand tiles (straight from global memory, bulk-prefetched into L2 one block ahead),
 //   dO^T is packed and the dW_local values of the epilogue are loaded;
