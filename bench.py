@@ -839,8 +839,9 @@ def main():
     res = run_b200(args, rank, world, local)
     if rank == 0:
         if world == 1 and not args.no_decode and (BATCH, LENGTH) == (8, 8192):
-            # the decode workload of the same layer, timed after the training
-            # step: CUDA-graph replays of the one-kernel step at each batch size
+            # the decode workload of the same layer (4096-token prefill, one-token steps at
+            # B = 1, 64, 256), timed after the training step: CUDA-graph replays of the
+            # one-kernel step at each batch size
             torch.cuda.empty_cache()
             dec = run_decode(args)
             res["decode"] = {k: dec[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
